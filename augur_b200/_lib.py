@@ -1,0 +1,107 @@
+"""ctypes binding of libaugur_kv.so (declared in include/augur_kv.h).
+
+There is no fallback: if the library is missing or fails to load, every data
+movement call raises KVLibraryError. Build it with
+``python -m augur_b200.csrc.build``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libaugur_kv.so")
+
+OK = 0
+EINVAL = 1
+EBOUNDS = 2
+ECUDA = 3
+ETIMEOUT = 4
+
+F32 = 0
+F16 = 1
+BF16 = 2
+
+COPY_AUTO = 0
+COPY_VECTOR = 1
+COPY_BULK = 2
+
+STATUS_NAMES = {
+    OK: "ok",
+    EINVAL: "invalid argument",
+    EBOUNDS: "index out of bounds",
+    ECUDA: "CUDA error",
+    ETIMEOUT: "device wait timed out",
+}
+
+# Every exported symbol the header declares, with (restype, argtypes).
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I32 = ctypes.c_int32
+_I64P = ctypes.POINTER(ctypes.c_int64)
+
+SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "augur_kv_version": (ctypes.c_int, []),
+    "augur_kv_last_error": (ctypes.c_char_p, []),
+    "augur_kv_scatter": (
+        ctypes.c_int,
+        [_P, _P, _I64P, _I64P, _I64, _I32, _P, _P, _I64P, _I64, _I64, _I32, _P, _I64P, _I64,
+         _I64, _I32, _I32, _I32, _P, _P],
+    ),
+    "augur_kv_copy_runs": (
+        ctypes.c_int,
+        [_P, _P, _I64P, _I64, _I64, _I32, _P, _P, _I64P, _I64, _I64, _I32, _P, _I64, _I32,
+         _I32, _I32, _I32, _I32, _P, _P],
+    ),
+}
+
+
+class KVLibraryError(RuntimeError):
+    """libaugur_kv.so is missing, failed to load, or a call returned an error."""
+
+    def __init__(self, message: str, code: int = ECUDA) -> None:
+        super().__init__(message)
+        self.code = code
+
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the library once and bind every declared symbol."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise KVLibraryError(
+                f"{LIB_PATH} is missing: build it with `python -m augur_b200.csrc.build` "
+                "(augur_b200 has no CPU or torch fallback for KV-cache data movement)",
+                EINVAL,
+            )
+        try:
+            lib = ctypes.CDLL(LIB_PATH)
+        except OSError as exc:
+            raise KVLibraryError(f"cannot load {LIB_PATH}: {exc}", EINVAL) from exc
+        for name, (restype, argtypes) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = restype
+            fn.argtypes = argtypes
+        _lib = lib
+        return lib
+
+
+def i64_array(values) -> ctypes.Array:
+    vals = [int(v) for v in values]
+    return (ctypes.c_int64 * len(vals))(*vals)
+
+
+def check(code: int, what: str) -> None:
+    if code == OK:
+        return
+    detail = load().augur_kv_last_error().decode("utf-8", "replace")
+    raise KVLibraryError(f"{what}: {STATUS_NAMES.get(code, code)}: {detail}", code)

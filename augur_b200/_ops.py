@@ -1,0 +1,218 @@
+"""Tensor-level launchers for libaugur_kv.so.
+
+These functions turn torch tensors (device memory owned by the caller) into
+the raw pointers, element strides and stream the C ABI takes, and raise on a
+non-zero status. They never allocate cache memory and never fall back to
+torch indexing: a CPU tensor is a ValueError.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Sequence
+
+import torch
+from torch import Tensor
+
+from . import _lib
+
+_DTYPE_CODES = {torch.float32: _lib.F32, torch.float16: _lib.F16, torch.bfloat16: _lib.BF16}
+
+_status_words: dict[int, Tensor] = {}
+
+# Number of launches issued through this module; bench and tests read it.
+launch_count = 0
+
+
+def dtype_code(t: Tensor) -> int:
+    try:
+        return _DTYPE_CODES[t.dtype]
+    except KeyError:
+        raise ValueError(
+            f"unsupported KV cache dtype {t.dtype}; augur_b200 moves float32, float16 and bfloat16"
+        ) from None
+
+
+def require_cuda(what: str, *tensors: Tensor | None) -> None:
+    for t in tensors:
+        if t is not None and t.device.type != "cuda":
+            raise ValueError(
+                f"{what} needs CUDA tensors: augur_b200 moves KV-cache data only with its "
+                f"sm_100a kernels and has no CPU fallback (got a tensor on {t.device})"
+            )
+
+
+def status_word(device: torch.device) -> Tensor:
+    """The per-device int32 word kernels write their first error code into."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    word = _status_words.get(idx)
+    if word is None:
+        word = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _status_words[idx] = word
+    return word
+
+
+def read_status(device: torch.device | int | None = None, reset: bool = True) -> int:
+    """Synchronise the device and return (and by default clear) its status word."""
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    elif isinstance(device, int):
+        device = torch.device("cuda", device)
+    word = status_word(device)
+    torch.cuda.synchronize(device)
+    code = int(word.item())
+    if reset and code != 0:
+        word.zero_()
+    return code
+
+
+def check_status(device: torch.device | int | None = None) -> None:
+    """Raise KVLibraryError if a kernel on this device recorded an error."""
+    code = read_status(device)
+    if code != _lib.OK:
+        raise _lib.KVLibraryError(
+            f"a KV kernel recorded a device-side error: {_lib.STATUS_NAMES.get(code, code)}", code
+        )
+
+
+class _DeviceGuard:
+    """Make `device` current for the duration of a launch if it is not already."""
+
+    __slots__ = ("idx", "prev")
+
+    def __init__(self, device: torch.device) -> None:
+        self.idx = device.index if device.index is not None else torch.cuda.current_device()
+        self.prev = -1
+
+    def __enter__(self) -> None:
+        cur = torch.cuda.current_device()
+        if cur != self.idx:
+            self.prev = cur
+            torch.cuda.set_device(self.idx)
+
+    def __exit__(self, *exc) -> None:
+        if self.prev >= 0:
+            torch.cuda.set_device(self.prev)
+
+
+def _ptr(t: Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def scatter(
+    *,
+    src_k: Tensor,
+    src_v: Tensor | None,
+    src_k_strides: Sequence[int],
+    src_v_strides: Sequence[int] | None,
+    tokens_per_row: int,
+    dst_k: Tensor,
+    dst_v: Tensor | None,
+    dst_strides: Sequence[int],
+    rows_per_major: int,
+    num_majors: int,
+    index: Tensor,
+    index_strides: Sequence[int],
+    index_row_base: int,
+    n_tokens: int,
+    n_layers: int,
+    n_heads: int,
+    head_dim: int,
+    stream: torch.cuda.Stream | None = None,
+) -> None:
+    """Launch augur_kv_scatter. Strides are element strides as the header documents."""
+    global launch_count
+    require_cuda("KV scatter", src_k, src_v, dst_k, dst_v, index)
+    if index.dtype != torch.int64:
+        raise ValueError("scatter index must be int64")
+    lib = _lib.load()
+    device = dst_k.device
+    st = stream if stream is not None else torch.cuda.current_stream(device)
+    with _DeviceGuard(device):
+        code = lib.augur_kv_scatter(
+            _ptr(src_k),
+            _ptr(src_v),
+            _lib.i64_array(src_k_strides),
+            _lib.i64_array(src_v_strides if src_v_strides is not None else src_k_strides),
+            int(tokens_per_row),
+            dtype_code(src_k),
+            _ptr(dst_k),
+            _ptr(dst_v),
+            _lib.i64_array(dst_strides),
+            int(rows_per_major),
+            int(num_majors),
+            dtype_code(dst_k),
+            _ptr(index),
+            _lib.i64_array(index_strides),
+            int(index_row_base),
+            int(n_tokens),
+            int(n_layers),
+            int(n_heads),
+            int(head_dim),
+            status_word(device).data_ptr(),
+            st.cuda_stream,
+        )
+    _lib.check(code, "augur_kv_scatter")
+    if n_tokens > 0 and n_layers > 0:
+        launch_count += 1
+
+
+def copy_runs(
+    *,
+    src_k: Tensor,
+    src_v: Tensor | None,
+    src_strides: Sequence[int],
+    src_majors: int,
+    src_rows_per_major: int,
+    dst_k: Tensor,
+    dst_v: Tensor | None,
+    dst_strides: Sequence[int],
+    dst_majors: int,
+    dst_rows_per_major: int,
+    runs: Tensor,
+    max_rows: int,
+    n_layers: int,
+    n_heads: int,
+    head_dim: int,
+    flags: int = _lib.COPY_AUTO,
+    stream: torch.cuda.Stream | None = None,
+) -> None:
+    """Launch augur_kv_copy_runs; runs is a device int32 [n_runs, 5] tensor."""
+    global launch_count
+    require_cuda("KV block copy", src_k, src_v, dst_k, dst_v, runs)
+    if runs.dtype != torch.int32 or runs.dim() != 2 or runs.shape[1] != 5 or not runs.is_contiguous():
+        raise ValueError("runs must be a contiguous int32 tensor of shape [n_runs, 5]")
+    lib = _lib.load()
+    device = dst_k.device
+    st = stream if stream is not None else torch.cuda.current_stream(device)
+    with _DeviceGuard(device):
+        code = lib.augur_kv_copy_runs(
+            _ptr(src_k),
+            _ptr(src_v),
+            _lib.i64_array(src_strides),
+            int(src_majors),
+            int(src_rows_per_major),
+            dtype_code(src_k),
+            _ptr(dst_k),
+            _ptr(dst_v),
+            _lib.i64_array(dst_strides),
+            int(dst_majors),
+            int(dst_rows_per_major),
+            dtype_code(dst_k),
+            _ptr(runs),
+            int(runs.shape[0]),
+            int(max_rows),
+            int(n_layers),
+            int(n_heads),
+            int(head_dim),
+            int(flags),
+            status_word(device).data_ptr(),
+            st.cuda_stream,
+        )
+    _lib.check(code, "augur_kv_copy_runs")
+    if runs.shape[0] > 0 and n_layers > 0:
+        launch_count += 1
+
+
+def max_rows_for(head_dim: int, elem_size: int, cap_rows: int = 64, cap_bytes: int = 8192) -> int:
+    """Largest run length (rows) to cut copies into: at most cap_rows rows and cap_bytes bytes."""
+    return max(1, min(cap_rows, cap_bytes // max(1, head_dim * elem_size)))

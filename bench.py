@@ -1,0 +1,570 @@
+"""KV-cache data-movement benchmark (paged scatter / handoff / append / fork).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline (N=1): the paged scatter microbenchmark — 64 sequences, 8192 tokens
+(lengths U[32,256] rescaled to 8192), K and V [8192, 2, 64] bf16 N(0,1) for
+each of 24 layers, block size 16, a 65536-block pool, seeded random block
+tables. One step = one all-layer scatter of the batch (one kernel launch);
+value = algorithmic GB/s = (2 x payload + slot bytes) / time. Steps rotate
+over 4 independently seeded batches with disjoint destination blocks
+(805 MB touched per rotation, 201 MB per step, L2 = 126 MB), so no step
+finds its inputs or outputs in L2.
+
+Also reported on the same line: e2e (same metric through the public API with
+the step's K/V and slot mapping copied from pinned host memory each step and
+the status word read back), the contiguous->paged handoff of 32 prompts of
+U[512,2048] tokens (us per sequence), the decode append (us per step), the
+prefix fork with copy-on-write, the roofline of the scatter kernel and the
+CPU baseline (the C oracle on this host's cores).
+
+Under torchrun (N>1) every rank owns its own GPU, pool and seeded batches
+(weak scaling, no data-path collective); the timed region is bracketed by a
+barrier and device synchronisation and the max over ranks is taken.
+
+--impl reference times the reference algorithm on the host CPU (the C
+restatement in oracle/, all host threads) on the same workload; the
+reference itself is pure Python/torch and cannot be installed on the GPU box.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+L, H, D, BS = 24, 2, 64, 16
+TOKEN_LAYER_BYTES = 2 * H * D * 2  # K+V of one token in one layer, bf16: 512 B
+TOKEN_BYTES = L * TOKEN_LAYER_BYTES  # 12,288 B
+METRIC = "KV-cache scatter/handoff GB/s vs HBM peak; handoff µs per seq at 1–8 B200"
+
+
+# ---------------------------------------------------------------------------
+# workloads (seeded; shared with the full-size tests)
+# ---------------------------------------------------------------------------
+
+
+def config2_lengths(seed: int, n_seqs: int = 64, total: int = 8192) -> np.ndarray:
+    """Lengths U[32,256], rescaled so they sum to exactly `total`."""
+    rng = np.random.default_rng(seed)
+    raw = rng.integers(32, 257, size=n_seqs).astype(np.float64)
+    lens = np.floor(raw * total / raw.sum()).astype(np.int64)
+    lens[: total - int(lens.sum())] += 1
+    return lens
+
+
+def config2_batch(seed: int, block_offset: int = 0, num_blocks: int = 65536):
+    """Slots and host K/V for one config-2 batch.
+
+    Block tables are consecutive slices of one seeded permutation of the pool,
+    starting at block_offset (so batches with different offsets never share a
+    destination block).
+    """
+    lens = config2_lengths(seed)
+    perm = np.random.default_rng(12345).permutation(num_blocks)
+    nblk = -(-lens // BS)
+    slots, cur = [], block_offset
+    for n, nb in zip(lens, nblk):
+        ids = perm[cur : cur + nb]
+        pos = np.arange(n)
+        slots.append(ids[pos // BS] * BS + pos % BS)
+        cur += nb
+    slots = np.concatenate(slots).astype(np.int64)
+    g = torch.Generator().manual_seed(seed)
+    T = int(lens.sum())
+    k = torch.randn(L, T, H, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(L, T, H, D, generator=g).to(torch.bfloat16)
+    return lens, slots, k, v, cur - block_offset
+
+
+def config3_lengths(seed: int = 3, n: int = 32) -> np.ndarray:
+    return np.random.default_rng(seed).integers(512, 2049, size=n).astype(np.int64)
+
+
+def scatter_bytes(n_tokens: int, layers: int = L) -> int:
+    """Algorithmic bytes of one scatter: read + write of every token-layer, plus 8 B of slot per token."""
+    return 2 * n_tokens * layers * TOKEN_LAYER_BYTES + 8 * n_tokens
+
+
+# ---------------------------------------------------------------------------
+# measurement helpers
+# ---------------------------------------------------------------------------
+
+
+class ClockSampler:
+    """Poll SM clock and throttle reasons through NVML while the timed region runs."""
+
+    REASONS = {
+        "sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80, "applications_clocks_setting": 0x2,
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.002) -> None:
+        self.samples: list[int] = []
+        self.reasons: set[str] = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._period = period_s
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            idx = int(vis.split(",")[device_index]) if vis else device_index
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self._nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # NVML missing: report no clocks rather than fail the bench
+            self._nv = None
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _sample(self) -> None:
+        nv = self._nv
+        self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+        mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+        for name, bit in self.REASONS.items():
+            if mask & bit:
+                self.reasons.add(name)
+
+    def _run(self) -> None:
+        while not self._stop.is_set():
+            self._sample()
+            time.sleep(self._period)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc) -> None:
+        if self._nv is not None:
+            self._stop.set()
+            self._t.join()
+            if not self.samples:
+                self._sample()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml unavailable"]}
+        return {"sm_mhz": int(statistics.median(self.samples)), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def load_peaks() -> tuple[float, str]:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def load_traffic(kernel: str, workload: str):
+    """Per-launch DRAM bytes from the committed ncu summary (profiles/traffic.txt), or None."""
+    path = os.path.join(ROOT, "profiles", "traffic.txt")
+    try:
+        for line in open(path):
+            parts = line.split()
+            if len(parts) >= 3 and parts[0] == kernel and parts[1] == workload:
+                return int(float(parts[2]))
+    except OSError:
+        pass
+    return None
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int, device) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier(device_ids=[device.index])
+    torch.cuda.synchronize(device)
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (oracle on host cores)
+# ---------------------------------------------------------------------------
+
+
+def cpu_scatter_passes(seconds: float, min_passes: int = 2, threads: int | None = None):
+    """Time full config-2 scatters with the C oracle; returns (GB/s, passes, threads, per-pass s)."""
+    from oracle import kv_oracle
+
+    threads = threads or kv_oracle.max_threads()
+    lens, slots, k, v, _ = config2_batch(seed=0)
+    pool_k = torch.empty(L, 65536, H, BS, D, dtype=torch.bfloat16)  # 6 GiB virtual, touched sparsely
+    pool_v = torch.empty_like(pool_k)
+    kv_oracle.scatter_slots(k, v, slots, pool_k, pool_v, BS, threads=threads)  # first touch
+    n, t0 = 0, time.perf_counter()
+    while True:
+        kv_oracle.scatter_slots(k, v, slots, pool_k, pool_v, BS, threads=threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if n >= min_passes and el >= seconds:
+            break
+    return scatter_bytes(int(lens.sum())) * n / el / 1e9, n, threads, el / n
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+
+def run_ours(args, world: int, rank: int, local: int) -> dict | None:
+    import augur_b200 as ab
+    from augur_b200 import _lib, _ops, batched
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    n_sets = 4
+    pool = ab.PagedKVCache(keys=torch.empty(L, 65536, H, BS, D, dtype=torch.bfloat16, device=device),
+                           values=torch.empty(L, 65536, H, BS, D, dtype=torch.bfloat16, device=device),
+                           block_size=BS, allocator=ab.BlockAllocator(65536))
+    sets, offset = [], 0
+    host_sets = []
+    for s in range(n_sets):
+        lens, slots, k, v, used = config2_batch(seed=1000 * rank + s, block_offset=offset)
+        offset += used
+        host_sets.append((slots, k, v))
+        sets.append((torch.from_numpy(slots).to(device), k.to(device), v.to(device)))
+    T = int(sets[0][0].shape[0])
+    step_bytes = scatter_bytes(T)
+
+    def step(i: int, stream=None) -> None:
+        sl, k, v = sets[i % n_sets]
+        batched.write_paged_kv_batch(pool, k, v, sl, stream=stream)
+
+    # warm-up (eager), then capture one rotation in a CUDA graph
+    for i in range(max(3, args.warmup)):
+        step(i)
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    cap_stream = torch.cuda.Stream(device)
+    cap_stream.wait_stream(torch.cuda.current_stream(device))
+    launches_before = _ops.launch_count
+    with torch.cuda.graph(graph, stream=cap_stream):
+        for i in range(n_sets):
+            step(i)
+    launches_per_replay = _ops.launch_count - launches_before
+    for _ in range(2):
+        graph.replay()
+    torch.cuda.synchronize(device)
+
+    K = args.steps
+    replays, rem = divmod(K, n_sets)
+    rem_graph = None
+    if rem:
+        rem_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(rem_graph, stream=cap_stream):
+            for i in range(rem):
+                step(i)
+        rem_graph.replay()
+    torch.cuda.synchronize(device)
+
+    barrier(world, device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record()
+        for _ in range(replays):
+            graph.replay()
+        if rem_graph is not None:
+            rem_graph.replay()
+        end.record()
+        torch.cuda.synchronize(device)
+    ms = start.elapsed_time(end)
+    barrier(world, device)
+    ms_max = max_over_ranks(ms, world, device)
+    gpu_launches = replays * launches_per_replay + (rem if rem_graph is not None else 0)
+    value = world * step_bytes * K / (ms_max / 1e3) / 1e9
+    per_launch_s = (ms / 1e3) / K
+    achieved = step_bytes / per_launch_s / 1e9
+    status = _ops.read_status(device)
+    if status != _lib.OK:
+        raise RuntimeError(f"device status {status} after the timed region")
+
+    # ---- e2e: public API, pinned host inputs copied every step, status read back
+    pinned = [(torch.from_numpy(s).pin_memory(), k.pin_memory(), v.pin_memory()) for s, k, v in host_sets]
+    dev_bufs = [(torch.empty_like(sets[0][0]), torch.empty_like(sets[0][1]), torch.empty_like(sets[0][2]))]
+    status_word = _ops.status_word(device)
+    status_host = torch.empty(1, dtype=torch.int32).pin_memory()
+    e2e_steps = max(3, min(K, 40))
+
+    def e2e_step(i: int) -> None:
+        hs, hk, hv = pinned[i % n_sets]
+        ds, dk, dv = dev_bufs[0]
+        ds.copy_(hs, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        batched.write_paged_kv_batch(pool, dk, dv, ds)
+        status_host.copy_(status_word, non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
+    barrier(world, device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(e2e_steps):
+        e2e_step(i)
+    e1.record()
+    torch.cuda.synchronize(device)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world, device)
+    if int(status_host.item()) != _lib.OK:
+        raise RuntimeError("device status error in the e2e region")
+    h2d = int(sets[0][0].numel() * 8 + sets[0][1].numel() * 2 * 2)
+    e2e = {"value": round(world * step_bytes * e2e_steps / (e2e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "steps": e2e_steps,
+           "path": "augur_b200.batched.write_paged_kv_batch (ctypes -> augur_kv_scatter)"}
+    del pinned, dev_bufs
+    graph.reset()
+    if rem_graph is not None:
+        rem_graph.reset()
+    del sets
+
+    extra = {}
+    if not args.skip_extras:
+        extra = run_extras(device)
+    del pool
+    torch.cuda.empty_cache()
+
+    if rank != 0:
+        return None
+    peak, peak_kind = load_peaks()
+    roofline = {
+        "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+        "frac": round(achieved / peak, 4), "peak_source": f"hbm_gbs of {peak_kind}",
+        "traffic": load_traffic("scatter_vec_kernel", "config2"),
+        "algorithmic_bytes_per_launch": step_bytes, "kernel": "scatter_vec_kernel<16,true,4>",
+        "launch_us": round(per_launch_s * 1e6, 2),
+    }
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": round(ms_max / K, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) K/V, seeded block tables)",
+        "config": {"workload": "paged scatter: 64 seqs / 8192 tokens x 24 layers, 2 KV heads x 64, "
+                               "block 16, 65536-block pool (config 2)",
+                   "tokens_per_step": T, "bytes_per_step": step_bytes,
+                   "l2": "4 rotating seeded batches with disjoint blocks: 805 MB touched per rotation > 126 MB L2",
+                   "parallelism": f"sequence-sharded dp{world} (one pool per GPU)",
+                   "timed": "CUDA graph replays of one launch per step, CUDA events"},
+        "e2e": e2e, "gpu_launches": gpu_launches, "roofline": roofline, "clocks": clocks.summary(),
+        "extra": extra,
+    }
+    if world == 1 and not args.skip_cpu:
+        gbs, passes, threads, per = cpu_scatter_passes(args.cpu_seconds)
+        line["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                                "sample": f"{passes} full config-2 scatters (8192 tokens x 24 layers), "
+                                          f"{per * 1e3:.1f} ms each, C oracle with {threads} threads"}
+    return line
+
+
+def run_extras(device) -> dict:
+    """Config 3 handoff + decode append and config 4 fork/COW, timed with CUDA events."""
+    import augur_b200 as ab
+    from augur_b200 import _lib, _ops, batched
+
+    out = {}
+    # ---- config 3: contiguous -> paged handoff of 32 prompts, then 256 decode appends
+    lens = config3_lengths()
+    B, Lmax = len(lens), int(lens.max())
+    g = torch.Generator(device=device).manual_seed(3)
+    src = ab.KVCache(keys=torch.randn(L, B, H, Lmax, D, generator=g, device=device).to(torch.bfloat16),
+                     values=torch.randn(L, B, H, Lmax, D, generator=g, device=device).to(torch.bfloat16))
+    NB = 8192
+    perm = np.random.default_rng(33).permutation(NB)
+    tables, cur = [], 0
+    for n in lens:
+        nb = -(-int(n) // BS) + 256 // BS + 1
+        tables.append(ab.SequenceBlockTable(block_ids=perm[cur : cur + nb].tolist(), block_size=BS))
+        cur += nb
+    pool = ab.PagedKVCache(keys=torch.empty(L, NB, H, BS, D, dtype=torch.bfloat16, device=device),
+                           values=torch.empty(L, NB, H, BS, D, dtype=torch.bfloat16, device=device),
+                           block_size=BS, allocator=ab.BlockAllocator(NB))
+    runs = batched.handoff_contiguous_to_paged(src, pool, tables, lens)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    tok = int(lens.sum())
+    hbytes = 2 * tok * TOKEN_BYTES + runs.numel() * 4
+    for name, flags in (("bulk", _lib.COPY_BULK), ("vector", _lib.COPY_VECTOR)):
+        times = []
+        for _ in range(7):
+            flush.fill_(1)  # evict L2 between repetitions
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            batched.copy_runs_between(src.keys, src.values, "contiguous", pool.keys, pool.values, "paged",
+                                      runs, BS, flags=flags)
+            b.record()
+            torch.cuda.synchronize(device)
+            times.append(a.elapsed_time(b))
+        ms = statistics.median(times[2:])
+        out[f"handoff_{name}"] = {"us_per_seq": round(ms * 1e3 / B, 3), "ms": round(ms, 4),
+                                  "GBps": round(hbytes / (ms / 1e3) / 1e9, 1), "seqs": B, "tokens": tok}
+    # decode append: 256 steps of one token per sequence, all layers, captured in one graph
+    for t, n in zip(tables, lens):
+        t.seq_len = int(n)
+    steps = 256
+    slot_rows = []
+    for _ in range(steps):
+        slot_rows.append(batched.decode_slot_mapping(tables, pool.allocator))
+    slot_t = torch.from_numpy(np.stack(slot_rows)).to(device)
+    nk = torch.randn(steps, L, B, H, D, generator=g, device=device).to(torch.bfloat16)
+    nv = torch.randn(steps, L, B, H, D, generator=g, device=device).to(torch.bfloat16)
+    for s in range(3):
+        batched.append_decode(pool, None, nk[s], nv[s], slot_mapping=slot_t[s])
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream(device)
+    cs.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.graph(graph, stream=cs):
+        for s in range(steps):
+            batched.append_decode(pool, None, nk[s], nv[s], slot_mapping=slot_t[s])
+    graph.replay()
+    torch.cuda.synchronize(device)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    graph.replay()
+    b.record()
+    torch.cuda.synchronize(device)
+    ms = a.elapsed_time(b)
+    abytes = scatter_bytes(B)
+    out["decode_append"] = {"us_per_step": round(ms * 1e3 / steps, 3), "steps": steps, "seqs": B,
+                            "GBps": round(abytes * steps / (ms / 1e3) / 1e9, 1),
+                            "timed": "one CUDA graph of 256 append launches"}
+    graph.reset()
+    del src, nk, nv
+
+    # ---- config 4: 1000-token prefix (62 full blocks + 8 rows) forked 256 ways, COW, 128-token suffix
+    for prefix_len in (1024, 1000):
+        alloc = ab.BlockAllocator(NB)
+        pool4 = ab.PagedKVCache(keys=pool.keys, values=pool.values, block_size=BS, allocator=alloc)
+        parent = ab.SequenceBlockTable.empty(BS)
+        sm = batched.prefill_slot_mapping([parent], [prefix_len], alloc)[0]
+        pk = torch.randn(L, prefix_len, H, D, generator=g, device=device).to(torch.bfloat16)
+        batched.write_paged_kv_batch(pool4, pk, pk, torch.from_numpy(sm).to(device))
+        forks = batched.fork_prefix(pool4, parent, 256)
+        torch.cuda.synchronize(device)
+        a, b, c = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        a.record()
+        copied = batched.cow_partial_blocks(pool4, forks)
+        b.record()
+        suffix_sm = batched.prefill_slot_mapping(forks, [128] * 256, alloc,
+                                                 start_positions=[prefix_len] * 256).reshape(-1)
+        sk = torch.randn(L, 256 * 128, H, D, generator=g, device=device).to(torch.bfloat16)
+        sm_t = torch.from_numpy(suffix_sm).to(device)
+        torch.cuda.synchronize(device)
+        c0 = torch.cuda.Event(enable_timing=True)
+        c0.record()
+        batched.write_paged_kv_batch(pool4, sk, sk, sm_t)
+        c.record()
+        torch.cuda.synchronize(device)
+        out[f"prefix_fork_{prefix_len}"] = {
+            "forks": 256, "cow_blocks": copied, "cow_ms_incl_host": round(a.elapsed_time(b), 4),
+            "suffix_GBps": round(scatter_bytes(256 * 128) / (c0.elapsed_time(c) / 1e3) / 1e9, 1)}
+        del sk, pk
+    if _ops.read_status(device) != _lib.OK:
+        raise RuntimeError("device status error in the extra workloads")
+    del pool
+    return out
+
+
+# ---------------------------------------------------------------------------
+# reference arm
+# ---------------------------------------------------------------------------
+
+
+def run_reference(args, world: int, rank: int) -> dict | None:
+    if rank != 0:
+        return None
+    from oracle import kv_oracle
+
+    threads = kv_oracle.max_threads()
+    lens, slots, k, v, _ = config2_batch(seed=0)
+    pool_k = torch.empty(L, 65536, H, BS, D, dtype=torch.bfloat16)
+    pool_v = torch.empty_like(pool_k)
+    for _ in range(max(1, args.warmup)):
+        kv_oracle.scatter_slots(k, v, slots, pool_k, pool_v, BS, threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        kv_oracle.scatter_slots(k, v, slots, pool_k, pool_v, BS, threads=threads)
+    el = time.perf_counter() - t0
+    step_bytes = scatter_bytes(int(lens.sum()))
+    gbs = step_bytes * args.steps / el / 1e9
+    sample = (f"{args.steps} full config-2 scatters (8192 tokens x 24 layers) in host memory, "
+              f"reference per-token write_paged_kv loop restated in C (oracle/kv_oracle.c)")
+    return {
+        "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(el * 1e3 / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": "paged scatter: 64 seqs / 8192 tokens x 24 layers, 2 KV heads x 64, "
+                               "block 16, 65536-block pool (config 2)", "parallelism": "host CPU"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--skip-extras", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world, rank, local = dist_env()
+    if args.impl == "reference":
+        line = run_reference(args, world, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    try:
+        line = run_ours(args, world, rank, local)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

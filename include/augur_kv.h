@@ -1,0 +1,130 @@
+/*
+ * augur_kv.h — C ABI of libaugur_kv.so, the sm_100a data-movement layer for
+ * augur's KV caches (contiguous cache, paged cache, prefix cache).
+ *
+ * Every entry point takes raw device pointers, element strides as int64 host
+ * arrays, int32/int64 device index arrays and the caller's cudaStream_t (as
+ * void*). Nothing here allocates, synchronises or keeps state between calls
+ * except the thread-local text returned by augur_kv_last_error(). All work is
+ * stream-ordered on the given stream. Validation that needs host data (shapes,
+ * position ranges, allocator state) is the host wrapper's job; the kernels
+ * still bounds-check every index they dereference and, instead of touching
+ * memory out of range, record AUGUR_KV_EBOUNDS in the optional device status
+ * word (int32, first error wins) and skip that row.
+ *
+ * Layout vocabulary (reference shapes, augur/kv_cache.py:27-33 and
+ * augur/paged_kv_cache.py:152-158):
+ *   contiguous cache  [layers, batch, kv_heads, max_seq, head_dim]
+ *   paged pool        [layers, num_blocks, kv_heads, block_size, head_dim]
+ * A "row" is head_dim contiguous elements of one (layer, token, head) of K or
+ * V. A "slot" addresses one token position of a cache: slot = major *
+ * rows_per_major + row, where major is the block id (paged pool) or the batch
+ * row (contiguous cache, rows_per_major = max_seq).
+ */
+#ifndef AUGUR_KV_H
+#define AUGUR_KV_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes returned by every entry point and written to status words. */
+#define AUGUR_KV_OK 0
+#define AUGUR_KV_EINVAL 1   /* bad argument: null pointer, size, dtype, stride, alignment */
+#define AUGUR_KV_EBOUNDS 2  /* an index addressed a slot/block/row outside its tensor */
+#define AUGUR_KV_ECUDA 3    /* a CUDA runtime error; augur_kv_last_error() has the text */
+#define AUGUR_KV_ETIMEOUT 4 /* a bounded device-side wait gave up */
+
+/* Element types. Same-type copies are byte copies; mixed types convert through
+ * fp32 with round-to-nearest-even, as torch's Tensor.copy_ does. */
+#define AUGUR_KV_F32 0
+#define AUGUR_KV_F16 1
+#define AUGUR_KV_BF16 2
+
+/* Flags for augur_kv_copy_runs. */
+#define AUGUR_KV_COPY_AUTO 0   /* TMA bulk path when every address is 16-byte aligned, else vector path */
+#define AUGUR_KV_COPY_VECTOR 1 /* force the 16/8/4/2/1-byte vector path */
+#define AUGUR_KV_COPY_BULK 2   /* require the TMA bulk path (EINVAL if not aligned) */
+
+/* Library version, (major << 16) | minor. */
+int augur_kv_version(void);
+
+/* Text of the last error raised on this host thread ("" when none). */
+const char* augur_kv_last_error(void);
+
+/*
+ * augur_kv_scatter — token scatter through a slot index: prefill K/V scatter
+ * into the paged pool, the per-step decode append, and the contiguous-cache
+ * write.
+ *
+ * Replaces the per-row index_put loop of write_kv (augur/kv_cache.py:103-106)
+ * and the per-token loop of write_paged_kv (augur/paged_kv_cache.py:188-192);
+ * with n_layers > 1 it is one launch for what the reference does in one call
+ * per layer from attention (augur/attention.py:60,64-71).
+ *
+ * Source token t (0 <= t < n_tokens) of layer l, kv k (0 = K, 1 = V), head h:
+ *   row = t / tokens_per_row, col = t % tokens_per_row
+ *   src[k] + l*S[0] + row*S[1] + col*S[2] + h*S[3]     (S = src_k/v_strides)
+ * Its destination slot:
+ *   slot = row * index_row_base + index[row*index_strides[0] + col*index_strides[1]]
+ *   dst[k] + l*D[0] + (slot / rows_per_major)*D[1] + (slot % rows_per_major)*D[2] + h*D[3]
+ * A negative index skips the token (padding). index_row_base = 0 means the
+ * index holds absolute slots (paged pool); index_row_base = rows_per_major
+ * means it holds positions within row `row` (contiguous cache, row = batch).
+ * An index >= rows_per_major with index_row_base > 0, or a slot >=
+ * num_majors*rows_per_major, is an EBOUNDS error for that token.
+ * head_dim elements are contiguous on both sides. src_v / dst_v may be NULL
+ * (then only K moves). All strides are in elements of their own tensor.
+ */
+int augur_kv_scatter(const void* src_k, const void* src_v,
+                     const int64_t* src_k_strides, /* [4] layer, row, col, head */
+                     const int64_t* src_v_strides, /* [4] */
+                     int64_t tokens_per_row, int32_t src_dtype,
+                     void* dst_k, void* dst_v,
+                     const int64_t* dst_strides, /* [4] layer, major, row, head */
+                     int64_t rows_per_major, int64_t num_majors, int32_t dst_dtype,
+                     const int64_t* index,         /* device */
+                     const int64_t* index_strides, /* [2] row, col */
+                     int64_t index_row_base,
+                     int64_t n_tokens, int32_t n_layers, int32_t n_heads, int32_t head_dim,
+                     int32_t* status, /* device int32 or NULL */
+                     void* stream);
+
+/*
+ * augur_kv_copy_runs — copy runs of consecutive rows between two caches, all
+ * layers, K and V, every head, in one launch. This is the block mover behind:
+ *   - read_paged_kv, the logical-order gather (augur/paged_kv_cache.py:195-221)
+ *   - copy_prefix_into_cache (augur/prefix_cache.py:53-75)
+ *   - the contiguous->paged prefill handoff, which the reference expresses as
+ *     write_paged_kv of cache.keys[l, b, :, :n_b] (augur/paged_kv_cache.py:167-192)
+ *   - copy-on-write of a shared prefix block (no reference function; its
+ *     result equals write_paged_kv of the copied rows into the new block).
+ *
+ * runs is a device int32 array [n_runs][5] = {src_major, src_row, dst_major,
+ * dst_row, n_rows}. Run r, layer l, kv k, head h copies n_rows rows:
+ *   src[k] + l*S[0] + src_major*S[1] + (src_row + i)*S[2] + h*S[3]
+ *   -> dst[k] + l*D[0] + dst_major*D[1] + (dst_row + i)*D[2] + h*D[3]
+ * for 0 <= i < n_rows. Rows must be dense (S[2] == D[2] == head_dim) for the
+ * bulk path; other strides use the vector path. Bounds: src_major <
+ * src_majors, src_row + n_rows <= src_rows_per_major, likewise for dst, and
+ * n_rows <= max_rows; a run that fails them is skipped with EBOUNDS.
+ * max_rows * head_dim * elem_size must be <= 16384 bytes.
+ */
+int augur_kv_copy_runs(const void* src_k, const void* src_v,
+                       const int64_t* src_strides, /* [4] layer, major, row, head */
+                       int64_t src_majors, int64_t src_rows_per_major, int32_t src_dtype,
+                       void* dst_k, void* dst_v,
+                       const int64_t* dst_strides, /* [4] */
+                       int64_t dst_majors, int64_t dst_rows_per_major, int32_t dst_dtype,
+                       const int32_t* runs, /* device [n_runs][5] */
+                       int64_t n_runs, int32_t max_rows,
+                       int32_t n_layers, int32_t n_heads, int32_t head_dim,
+                       int32_t flags, int32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AUGUR_KV_H */

@@ -1,0 +1,274 @@
+"""CPU oracle for augur's KV-cache data movement — TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import
+this module; it is the checker, never the thing measured or shipped, and
+augur_b200/ never imports it.
+
+It restates semioz/augur's cache algorithm:
+  * host bookkeeping in plain Python, statement for statement the reference's
+    order of effects: RefBlockAllocator (augur/paged_kv_cache.py:10-22),
+    RefBlockTable (:88-139), ref_block_hash (:84-85);
+  * data movement through liboracle_kv.so (kv_oracle.c), one C function per
+    reference loop, on torch CPU tensors.
+
+Parity pin: tests/test_oracle_pins.py checks every function here against the
+known-answer cases of the reference's own tests (tests/test_kv_cache.py,
+tests/test_paged_kv_cache.py, tests/test_prefix_cache.py) and against golden
+fixtures produced by running the reference itself (tests/golden/make_golden.py).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+import subprocess
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle_kv.so")
+
+_DTYPES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
+_lib: ctypes.CDLL | None = None
+
+
+def build(force: bool = False) -> str:
+    """Compile liboracle_kv.so with the committed Makefile (gcc, pthreads)."""
+    src = os.path.join(HERE, "kv_oracle.c")
+    if force or not os.path.exists(LIB_PATH) or os.path.getmtime(src) > os.path.getmtime(LIB_PATH):
+        subprocess.run(["make", "-s", "-C", HERE, "-B" if force else "liboracle_kv.so"], check=True)
+    return LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        build()
+        l = ctypes.CDLL(LIB_PATH)
+        P, I64, I32, I64P, I32P = (ctypes.c_void_p, ctypes.c_int64, ctypes.c_int,
+                                   ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int32))
+        l.oracle_write_kv.argtypes = [P, I64P, I32, P, I64P, I32, I64, I64P, I64P, I64, I64, I64, I64]
+        l.oracle_write_paged_tokens.argtypes = [P, I64P, I32, P, I64P, I32, I64, I64P, I64P, I64, I64, I64]
+        l.oracle_read_paged.argtypes = [P, I64P, I32, I64, I64P, I64, I64, P, I64P, I64, I64]
+        l.oracle_copy_prefix.argtypes = [P, I64P, I32, P, I64P, I32, I64, I64, I64, I64, I64]
+        l.oracle_scatter_slots.argtypes = [P, P, I64P, P, P, I64P, I64, I64P, I64, I64, I64, I64, I64, I32]
+        l.oracle_copy_runs.argtypes = [P, P, I64P, P, P, I64P, I64, I32P, I64, I64, I64, I64, I32]
+        l.oracle_max_threads.restype = ctypes.c_int
+        for fn in ("oracle_write_kv", "oracle_write_paged_tokens", "oracle_read_paged",
+                   "oracle_copy_prefix", "oracle_scatter_slots", "oracle_copy_runs"):
+            getattr(l, fn).restype = None
+        _lib = l
+    return _lib
+
+
+def max_threads() -> int:
+    return int(lib().oracle_max_threads())
+
+
+def _i64(vals) -> ctypes.Array:
+    vals = [int(v) for v in vals]
+    return (ctypes.c_int64 * max(1, len(vals)))(*vals)
+
+
+def _cpu(t: torch.Tensor) -> torch.Tensor:
+    if t.device.type != "cpu":
+        raise ValueError("the oracle runs on CPU tensors")
+    if t.stride(-1) != 1:
+        raise ValueError("the oracle needs head_dim contiguous")
+    return t
+
+
+def _i64_ptr(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.POINTER(ctypes.c_int64))
+
+
+# ---------------------------------------------------------------------------
+# restated host bookkeeping
+# ---------------------------------------------------------------------------
+
+
+class RefBlockAllocator:
+    """augur/paged_kv_cache.py:10-22: list free list, pop(0) / insert(0, ...)."""
+
+    def __init__(self, num_blocks: int) -> None:
+        if num_blocks <= 0:
+            raise ValueError("num_blocks must be positive")
+        self.free_blocks = list(range(num_blocks))
+
+    def allocate(self) -> int:
+        if not self.free_blocks:
+            raise RuntimeError("no free KV cache blocks")
+        return self.free_blocks.pop(0)
+
+    def free(self, block_id: int) -> None:
+        self.free_blocks.insert(0, block_id)
+
+
+class RefBlockTable:
+    """augur/paged_kv_cache.py:88-139."""
+
+    def __init__(self, block_ids: list[int], block_size: int, seq_len: int = 0) -> None:
+        self.block_ids = list(block_ids)
+        self.block_size = block_size
+        self.seq_len = seq_len
+
+    def ensure_position(self, position: int, allocator: RefBlockAllocator) -> None:
+        if position < 0:
+            raise ValueError("position must be non-negative")
+        required = position // self.block_size + 1
+        while len(self.block_ids) < required:
+            self.block_ids.append(allocator.allocate())
+        self.seq_len = max(self.seq_len, position + 1)
+
+    def free(self, allocator: RefBlockAllocator) -> None:
+        for block_id in reversed(self.block_ids):
+            allocator.free(block_id)
+        self.block_ids.clear()
+        self.seq_len = 0
+
+    def position_to_block_offset(self, position: int) -> tuple[int, int]:
+        if position < 0:
+            raise ValueError("position must be non-negative")
+        logical = position // self.block_size
+        if logical >= len(self.block_ids):
+            raise ValueError("position exceeds block table capacity")
+        return self.block_ids[logical], position % self.block_size
+
+
+def ref_block_hash(parent_hash: int | None, block_tokens) -> int:
+    """augur/paged_kv_cache.py:84-85: Python hash of (parent hash, token tuple)."""
+    return hash((parent_hash, tuple(block_tokens)))
+
+
+def ref_match_prefix(blocks: dict, token_ids: list[int], block_size: int) -> tuple[list[int], int]:
+    """augur/paged_kv_cache.py:63-82 over a {(parent, tokens): (hash, block)} dict."""
+    parent: int | None = None
+    ids: list[int] = []
+    for b in range(len(token_ids) // block_size):
+        entry = blocks.get((parent, tuple(token_ids[b * block_size : (b + 1) * block_size])))
+        if entry is None:
+            break
+        parent, block_id = entry
+        ids.append(block_id)
+    return ids, len(ids) * block_size
+
+
+# ---------------------------------------------------------------------------
+# composed data movement (torch CPU tensors)
+# ---------------------------------------------------------------------------
+
+
+def write_kv(cache_k, cache_v, layer: int, position_ids, key, value) -> None:
+    """augur/kv_cache.py:103-106 for already-validated positions."""
+    pos = np.ascontiguousarray(position_ids.to(torch.int64).numpy())
+    pstr = _i64([s // 8 for s in pos.strides])
+    batch, heads, seq, head_dim = key.shape
+    for src, dst in ((key, cache_k), (value, cache_v)):
+        src, dst = _cpu(src), _cpu(dst)
+        lib().oracle_write_kv(src.data_ptr(), _i64(src.stride()), _DTYPES[src.dtype], dst.data_ptr(),
+                              _i64(dst.stride()), _DTYPES[dst.dtype], layer, _i64_ptr(pos), pstr,
+                              batch, heads, seq, head_dim)
+
+
+def write_paged_kv(pool_k, pool_v, allocator: RefBlockAllocator, layer: int, table: RefBlockTable,
+                   positions: list[int], key, value) -> None:
+    """augur/paged_kv_cache.py:188-192: per token ensure_position, resolve, copy.
+
+    Like the reference, tokens before a failing one are written and the
+    error is raised afterwards.
+    """
+    blocks, offsets, err = [], [], None
+    for p in positions:
+        try:
+            table.ensure_position(p, allocator)
+            blk, off = table.position_to_block_offset(p)
+        except (ValueError, RuntimeError) as exc:
+            err = exc
+            break
+        blocks.append(blk)
+        offsets.append(off)
+    n = len(blocks)
+    if n:
+        b = np.asarray(blocks, dtype=np.int64)
+        o = np.asarray(offsets, dtype=np.int64)
+        heads, head_dim = key.shape[1], key.shape[3]
+        for src, dst in ((key, pool_k), (value, pool_v)):
+            src, dst = _cpu(src), _cpu(dst)
+            lib().oracle_write_paged_tokens(src.data_ptr(), _i64(src.stride()), _DTYPES[src.dtype],
+                                            dst.data_ptr(), _i64(dst.stride()), _DTYPES[dst.dtype],
+                                            layer, _i64_ptr(b), _i64_ptr(o), n, heads, head_dim)
+    if err is not None:
+        raise err
+
+
+def read_paged_kv(pool_k, pool_v, layer: int, table: RefBlockTable, seq_len: int | None = None):
+    """augur/paged_kv_cache.py:207-221."""
+    if seq_len is None:
+        seq_len = table.seq_len
+    if seq_len <= 0:
+        raise ValueError("seq_len must be positive")
+    if math.ceil(seq_len / table.block_size) > len(table.block_ids):
+        raise ValueError("position exceeds block table capacity")
+    heads, head_dim = pool_k.shape[2], pool_k.shape[4]
+    ids = np.asarray(table.block_ids, dtype=np.int64)
+    outs = []
+    for pool in (pool_k, pool_v):
+        out = torch.empty(1, heads, seq_len, head_dim, dtype=pool.dtype)
+        lib().oracle_read_paged(_cpu(pool).data_ptr(), _i64(pool.stride()), _DTYPES[pool.dtype], layer,
+                                _i64_ptr(ids), table.block_size, seq_len, out.data_ptr(),
+                                _i64(out.stride()), heads, head_dim)
+        outs.append(out)
+    return outs[0], outs[1]
+
+
+def copy_prefix_into_cache(entry_k, entry_v, cache_k, cache_v, batch_idx: int = 0) -> None:
+    """augur/prefix_cache.py:66-73 (shape checks are the caller's)."""
+    layers, heads, prefix_len, head_dim = entry_k.shape
+    for src, dst in ((entry_k, cache_k), (entry_v, cache_v)):
+        src, dst = _cpu(src), _cpu(dst)
+        lib().oracle_copy_prefix(src.data_ptr(), _i64(src.stride()), _DTYPES[src.dtype], dst.data_ptr(),
+                                 _i64(dst.stride()), _DTYPES[dst.dtype], batch_idx, prefix_len,
+                                 layers, heads, head_dim)
+
+
+def scatter_slots(src_k, src_v, slots: np.ndarray, pool_k, pool_v, block_size: int,
+                  threads: int = 1) -> None:
+    """write_paged_kv over all layers of [layers, tokens, heads, dim] by resolved slot."""
+    layers, tokens, heads, head_dim = src_k.shape
+    slots = np.ascontiguousarray(slots, dtype=np.int64)
+    sstr = _i64((src_k.stride(0), src_k.stride(1), src_k.stride(2)))
+    pstr = _i64((pool_k.stride(0), pool_k.stride(1), pool_k.stride(2), pool_k.stride(3)))
+    assert src_v is None or src_v.stride() == src_k.stride()
+    assert pool_v is None or pool_v.stride() == pool_k.stride()
+    lib().oracle_scatter_slots(_cpu(src_k).data_ptr(), None if src_v is None else _cpu(src_v).data_ptr(),
+                               sstr, _cpu(pool_k).data_ptr(),
+                               None if pool_v is None else _cpu(pool_v).data_ptr(), pstr,
+                               src_k.element_size(), _i64_ptr(slots), block_size, layers, tokens,
+                               heads, head_dim, int(threads))
+
+
+def copy_runs(src_k, src_v, dst_k, dst_v, runs: np.ndarray, threads: int = 1) -> None:
+    """Row runs between two (layers, major, heads, rows, dim) caches of one dtype."""
+    runs = np.ascontiguousarray(runs, dtype=np.int32).reshape(-1, 5)
+    layers, _, heads, _, head_dim = src_k.shape
+    assert src_k.dtype == dst_k.dtype
+    st = lambda t: _i64((t.stride(0), t.stride(1), t.stride(2), t.stride(3)))  # noqa: E731
+    lib().oracle_copy_runs(_cpu(src_k).data_ptr(), None if src_v is None else _cpu(src_v).data_ptr(),
+                           st(src_k), _cpu(dst_k).data_ptr(),
+                           None if dst_v is None else _cpu(dst_v).data_ptr(), st(dst_k),
+                           src_k.element_size(), runs.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                           runs.shape[0], layers, heads, head_dim, int(threads))
+
+
+def poison_(t: torch.Tensor) -> torch.Tensor:
+    """Fill every byte with 0xFF (a NaN pattern for every float dtype); in place."""
+    t.view(torch.uint8).fill_(0xFF)
+    return t
+
+
+def bits(t: torch.Tensor) -> torch.Tensor:
+    """Bit view for exact comparison (NaNs and -0 compare by bits)."""
+    return t.contiguous().view(torch.int16 if t.element_size() == 2 else torch.int32)

@@ -1,0 +1,87 @@
+"""The C-ABI library loads and exports exactly what include/augur_kv.h declares (CPU only).
+
+No kernel is launched here: the calls below fail argument validation before
+any CUDA runtime call.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from augur_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "augur_kv.h")
+
+
+def declared_functions() -> list[str]:
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(augur_kv_\w+)\s*\(", text)))
+
+
+def test_header_declarations_are_exported_and_bound():
+    names = declared_functions()
+    assert names, "no declarations parsed"
+    lib = _lib.load()
+    for name in names:
+        assert hasattr(lib, name), f"{name} declared but not exported"
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+    assert set(_lib.SIGNATURES) == set(names)
+
+
+def test_status_codes_match_header():
+    text = open(HEADER).read()
+    for name in ("OK", "EINVAL", "EBOUNDS", "ECUDA", "ETIMEOUT", "F32", "F16", "BF16",
+                 "COPY_AUTO", "COPY_VECTOR", "COPY_BULK"):
+        m = re.search(rf"#define AUGUR_KV_{name} (\d+)", text)
+        assert m and int(m.group(1)) == getattr(_lib, name), name
+
+
+def test_version():
+    assert _lib.load().augur_kv_version() >> 16 == 0
+
+
+def _i64(*v):
+    return (ctypes.c_int64 * len(v))(*v)
+
+
+def test_scatter_rejects_bad_arguments_without_touching_the_device():
+    lib = _lib.load()
+    strides = _i64(0, 0, 1, 1)
+    code = lib.augur_kv_scatter(None, None, strides, strides, 1, _lib.BF16, None, None, strides,
+                                16, 1, _lib.BF16, None, _i64(0, 1), 0, 1, 1, 1, 8, None, None)
+    assert code == _lib.EINVAL
+    assert b"null pointer" in lib.augur_kv_last_error()
+    fake = ctypes.c_void_p(16)
+    code = lib.augur_kv_scatter(fake, None, strides, strides, 1, 7, fake, None, strides,
+                                16, 1, _lib.BF16, fake, _i64(0, 1), 0, 1, 1, 1, 8, None, None)
+    assert code == _lib.EINVAL and b"dtype" in lib.augur_kv_last_error()
+    code = lib.augur_kv_scatter(fake, None, strides, strides, 1, _lib.BF16, fake, None, strides,
+                                16, 1, _lib.BF16, fake, _i64(0, 1), 3, 1, 1, 1, 8, None, None)
+    assert code == _lib.EINVAL and b"index_row_base" in lib.augur_kv_last_error()
+
+
+def test_copy_runs_rejects_bad_arguments_without_touching_the_device():
+    lib = _lib.load()
+    fake = ctypes.c_void_p(16)
+    s = _i64(0, 0, 1, 1)
+    code = lib.augur_kv_copy_runs(fake, None, s, 1, 1, _lib.BF16, fake, None, s, 1, 1, _lib.BF16,
+                                  fake, 1, 1024, 1, 1, 64, 0, None, None)
+    assert code == _lib.EINVAL and b"16384" in lib.augur_kv_last_error()
+    code = lib.augur_kv_copy_runs(fake, None, s, 1, 1, _lib.BF16, fake, None, s, 1, 1, _lib.BF16,
+                                  fake, 1, 1, 1, 1, 64, 9, None, None)
+    assert code == _lib.EINVAL and b"flags" in lib.augur_kv_last_error()
+    code = lib.augur_kv_copy_runs(fake, None, s, 1, 1, _lib.F32, fake, None, s, 1, 1, _lib.BF16,
+                                  fake, 1, 1, 1, 1, 64, _lib.COPY_BULK, None, None)
+    assert code == _lib.EINVAL and b"equal dtypes" in lib.augur_kv_last_error()
+
+
+def test_missing_library_fails_loudly(monkeypatch):
+    monkeypatch.setattr(_lib, "_lib", None)
+    monkeypatch.setattr(_lib, "LIB_PATH", "/nonexistent/libaugur_kv.so")
+    with pytest.raises(_lib.KVLibraryError, match="no CPU or torch fallback"):
+        _lib.load()
