@@ -28,6 +28,8 @@
 #include <cuda_fp16.h>
 #include <stdarg.h>
 #include <stdint.h>
+
+#include <mutex>
 #include <stdio.h>
 #include <string.h>
 
@@ -74,16 +76,54 @@ int pow2_shift(int64_t v) {
 
 constexpr int kMaxDevices = 64;
 
+// Guards the per-device launch-configuration caches below; entry points are
+// otherwise stateless and may be called from several host threads.
+std::mutex g_cache_mutex;
+
 int sm_count() {
   static int cached[kMaxDevices] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  std::lock_guard<std::mutex> lock(g_cache_mutex);
   if (cached[dev] == 0) {
     int n = 0;
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
     cached[dev] = n;
   }
   return cached[dev];
+}
+
+// Resident CTAs per SM of `kernel` at `threads` threads (no dynamic shared
+// memory), from the occupancy calculator, cached per device and kernel.
+int resident_ctas(const void* kernel, int threads) {
+  struct Entry {
+    const void* k;
+    int dev;
+    int n;
+  };
+  static Entry cache[256];
+  static int used = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(g_cache_mutex);
+  for (int i = 0; i < used; ++i)
+    if (cache[i].k == kernel && cache[i].dev == dev) return cache[i].n;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, 0) != cudaSuccess || n < 1) n = 1;
+  if (used < 256) cache[used++] = Entry{kernel, dev, n};
+  return n;
+}
+
+// x extent of a 2-D (runs x planes) grid: enough CTAs of `warps` warps for
+// every run of a plane, but no more than `cap` CTAs over all planes (the
+// kernels loop over runs with a stride).
+unsigned grid_x(uint64_t n_runs, uint64_t warps, uint64_t planes, uint64_t cap) {
+  uint64_t x = (n_runs + warps - 1) / warps;
+  uint64_t lim = cap / (planes ? planes : 1);
+  if (lim < 1) lim = 1;
+  if (x > lim) x = lim;
+  if (x < 1) x = 1;
+  return unsigned(x);
 }
 
 // ---------------------------------------------------------------------------
@@ -286,6 +326,80 @@ __global__ void __launch_bounds__(256) scatter_vec_kernel(ScatterArgs a) {
   }
 }
 
+// Same-dtype scatter, fast path for a power-of-two number of vectors per
+// token-layer (UPT; 32 at the augur shape: K+V x 2 heads x 8 x 16 B).
+// Each lane owns fixed (kv, head, column) slots, computed once; a warp item is
+// TPW tokens x LU layers, so the index lookup and slot decomposition happen
+// once per token per LU layers and every lane has LU*UPL loads in flight
+// before its stores. Items enumerate (layer group, token group) with the
+// token group fastest, so neighbouring warps read neighbouring source rows.
+#ifndef AUGUR_KV_SCATTER_LU
+#define AUGUR_KV_SCATTER_LU 8  // layers per warp item for large launches
+#endif
+#ifndef AUGUR_KV_SCATTER_WAVES
+#define AUGUR_KV_SCATTER_WAVES 2  // grid = resident CTAs x this, warps stride over items
+#endif
+
+template <int VEC, int UPT, int LU>
+__global__ void __launch_bounds__(256) scatter_rows_kernel(ScatterArgs a, uint32_t n_token_groups,
+                                                           uint32_t n_items, int32_t n_layers) {
+  using T = typename VecType<VEC>::T;
+  constexpr int LANES = UPT < 32 ? UPT : 32;  // lanes per token
+  constexpr int TPW = 32 / LANES;             // tokens per warp item
+  constexpr int UPL = UPT / LANES;            // vectors per lane per token-layer
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t sub = lane / LANES;
+  const uint32_t ul = lane % LANES;
+
+  const char* sb[UPL];
+  char* db[UPL];
+  int64_t s_layer[UPL], s_row[UPL], s_col[UPL];
+#pragma unroll
+  for (int i = 0; i < UPL; ++i) {
+    const uint32_t j = ul + uint32_t(i) * LANES;
+    const uint32_t r = j >> a.sh_vpr;
+    const uint32_t v = j & uint32_t(a.vpr - 1);
+    const uint32_t kv = r >> a.sh_heads;
+    const uint32_t h = r & uint32_t(a.n_heads - 1);
+    const int64_t* ss = a.src_stride[kv];
+    sb[i] = a.src[kv] + int64_t(h) * ss[3] + int64_t(v) * VEC;
+    s_layer[i] = ss[0];
+    s_row[i] = ss[1];
+    s_col[i] = ss[2];
+    db[i] = a.dst[kv] + int64_t(h) * a.dst_stride[3] + int64_t(v) * VEC;
+  }
+  const int64_t d_layer = a.dst_stride[0], d_major = a.dst_stride[1], d_row = a.dst_stride[2];
+
+  const uint32_t warps = gridDim.x * (blockDim.x >> 5);
+  for (uint32_t w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < n_items; w += warps) {
+    const uint32_t tg = w % n_token_groups;
+    const uint32_t lg = w / n_token_groups;
+    const uint32_t t = tg * TPW + sub;
+    if (t >= a.n_tokens) continue;
+    int64_t row, col, major, off;
+    if (!scatter_resolve(a, t, row, col, major, off)) continue;
+    const int l0 = int(lg) * LU;
+    const int nl = (n_layers - l0) < LU ? (n_layers - l0) : LU;
+    T val[LU][UPL];
+#pragma unroll
+    for (int k = 0; k < LU; ++k) {
+      if (k < nl) {
+#pragma unroll
+        for (int i = 0; i < UPL; ++i)
+          val[k][i] = load_stream<VEC>(sb[i] + int64_t(l0 + k) * s_layer[i] + row * s_row[i] + col * s_col[i]);
+      }
+    }
+    const int64_t dbase = major * d_major + off * d_row;
+#pragma unroll
+    for (int k = 0; k < LU; ++k) {
+      if (k < nl) {
+#pragma unroll
+        for (int i = 0; i < UPL; ++i) store_vec<VEC>(db[i] + int64_t(l0 + k) * d_layer + dbase, val[k][i]);
+      }
+    }
+  }
+}
+
 // Mixed-dtype scatter: one element per thread, converted through fp32.
 __global__ void __launch_bounds__(256) scatter_convert_kernel(ScatterArgs a) {
   const int64_t layer = blockIdx.y;
@@ -320,7 +434,6 @@ struct RunArgs {
   int64_t src_majors, src_rpm, dst_majors, dst_rpm;
   const int32_t* runs;
   uint32_t n_runs;
-  uint32_t n_items;       // n_layers * n_kv * n_heads * n_runs
   int32_t max_rows;
   int32_t n_heads;
   int32_t n_kv;
@@ -340,15 +453,24 @@ struct RunItem {
   int32_t n_rows;
 };
 
-// Item w enumerates (layer, kv, head, run) with the run fastest, so that
-// consecutive items read consecutive source blocks of one (layer, kv, head).
-__device__ __forceinline__ bool run_resolve(const RunArgs& a, uint32_t w, RunItem& it) {
-  const uint32_t run = w % a.n_runs;
-  uint32_t rest = w / a.n_runs;
-  const uint32_t h = rest % uint32_t(a.n_heads);
-  rest /= uint32_t(a.n_heads);
-  const uint32_t kv = rest % uint32_t(a.n_kv);
-  const int64_t layer = rest / uint32_t(a.n_kv);
+// Run `run` of the (layer, kv, head) plane this CTA row works on. Grids are
+// 2-D: blockIdx.y enumerates (layer, kv, head) once per CTA, so the per-run
+// work is one descriptor read and the bounds checks.
+struct Plane {
+  int64_t layer;
+  uint32_t kv, h;
+};
+
+__device__ __forceinline__ Plane plane_of(const RunArgs& a, uint32_t y) {
+  Plane p;
+  p.h = y % uint32_t(a.n_heads);
+  const uint32_t rest = y / uint32_t(a.n_heads);
+  p.kv = rest % uint32_t(a.n_kv);
+  p.layer = rest / uint32_t(a.n_kv);
+  return p;
+}
+
+__device__ __forceinline__ bool run_resolve(const RunArgs& a, const Plane& p, uint32_t run, RunItem& it) {
   const int32_t* r = a.runs + int64_t(run) * 5;
   const int64_t sm = __ldg(r + 0), sr = __ldg(r + 1), dm = __ldg(r + 2), dr = __ldg(r + 3);
   const int32_t n = __ldg(r + 4);
@@ -358,23 +480,26 @@ __device__ __forceinline__ bool run_resolve(const RunArgs& a, uint32_t w, RunIte
     record_status(a.status, AUGUR_KV_EBOUNDS);
     return false;
   }
-  it.src = a.src[kv] + layer * a.src_stride[0] + sm * a.src_stride[1] + sr * a.src_stride[2] +
-           int64_t(h) * a.src_stride[3];
-  it.dst = a.dst[kv] + layer * a.dst_stride[0] + dm * a.dst_stride[1] + dr * a.dst_stride[2] +
-           int64_t(h) * a.dst_stride[3];
+  it.src = a.src[p.kv] + p.layer * a.src_stride[0] + sm * a.src_stride[1] + sr * a.src_stride[2] +
+           int64_t(p.h) * a.src_stride[3];
+  it.dst = a.dst[p.kv] + p.layer * a.dst_stride[0] + dm * a.dst_stride[1] + dr * a.dst_stride[2] +
+           int64_t(p.h) * a.dst_stride[3];
   it.n_rows = n;
   return true;
 }
 
-// Vector path: one warp per item, VEC-byte vectors, 4 in flight per lane.
-template <int VEC>
+// Vector path: one warp per run of one plane, VEC-byte vectors, 4 in flight
+// per lane. Dense rows (row stride == row bytes on both sides) are one
+// contiguous span; other layouts decompose each vector into (row, column).
+template <int VEC, bool DENSE>
 __global__ void __launch_bounds__(256) copy_runs_vec_kernel(RunArgs a) {
   using T = typename VecType<VEC>::T;
   const uint32_t lane = threadIdx.x & 31u;
+  const Plane p = plane_of(a, blockIdx.y);
   const uint32_t warps = gridDim.x * (blockDim.x >> 5);
-  for (uint32_t w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < a.n_items; w += warps) {
+  for (uint32_t run = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); run < a.n_runs; run += warps) {
     RunItem it;
-    if (!run_resolve(a, w, it)) continue;
+    if (!run_resolve(a, p, run, it)) continue;
     const uint32_t units = uint32_t(it.n_rows) * uint32_t(a.vpr);
     for (uint32_t q0 = 0; q0 < units; q0 += 128u) {
       T val[4];
@@ -384,16 +509,23 @@ __global__ void __launch_bounds__(256) copy_runs_vec_kernel(RunArgs a) {
         dptr[k] = nullptr;
         const uint32_t q = q0 + uint32_t(k) * 32u + lane;
         if (q >= units) continue;
-        uint32_t row, v;
-        if (a.sh_vpr >= 0) {
-          row = q >> a.sh_vpr;
-          v = q & uint32_t(a.vpr - 1);
+        int64_t so, dof;
+        if (DENSE) {
+          so = dof = int64_t(q) * VEC;
         } else {
-          row = q / uint32_t(a.vpr);
-          v = q - row * uint32_t(a.vpr);
+          uint32_t row, v;
+          if (a.sh_vpr >= 0) {
+            row = q >> a.sh_vpr;
+            v = q & uint32_t(a.vpr - 1);
+          } else {
+            row = q / uint32_t(a.vpr);
+            v = q - row * uint32_t(a.vpr);
+          }
+          so = int64_t(row) * a.src_stride[2] + int64_t(v) * VEC;
+          dof = int64_t(row) * a.dst_stride[2] + int64_t(v) * VEC;
         }
-        val[k] = load_stream<VEC>(it.src + int64_t(row) * a.src_stride[2] + int64_t(v) * VEC);
-        dptr[k] = it.dst + int64_t(row) * a.dst_stride[2] + int64_t(v) * VEC;
+        val[k] = load_stream<VEC>(it.src + so);
+        dptr[k] = it.dst + dof;
       }
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
@@ -403,13 +535,14 @@ __global__ void __launch_bounds__(256) copy_runs_vec_kernel(RunArgs a) {
   }
 }
 
-// Mixed-dtype path: one warp per item, one element per lane step.
+// Mixed-dtype path: one warp per run of one plane, one element per lane step.
 __global__ void __launch_bounds__(256) copy_runs_convert_kernel(RunArgs a) {
   const uint32_t lane = threadIdx.x & 31u;
+  const Plane p = plane_of(a, blockIdx.y);
   const uint32_t warps = gridDim.x * (blockDim.x >> 5);
-  for (uint32_t w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < a.n_items; w += warps) {
+  for (uint32_t run = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); run < a.n_runs; run += warps) {
     RunItem it;
-    if (!run_resolve(a, w, it)) continue;
+    if (!run_resolve(a, p, run, it)) continue;
     const uint32_t units = uint32_t(it.n_rows) * uint32_t(a.vpr);
     for (uint32_t q = lane; q < units; q += 32u) {
       const uint32_t row = q / uint32_t(a.vpr);
@@ -503,36 +636,86 @@ __device__ __forceinline__ void bulk_wait_read() {
 
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
-// Each warp's lane 0 runs an independent pipeline of a.stages stages over the
-// items w = gw, gw + total_warps, ...: bulk-load item c into stage c % stages
-// and, once that stage's mbarrier phase completes, bulk-store it out. A stage
-// is refilled once the store that last read it has finished reading
-// (wait_group.read 1 keeps one store in flight behind the one just issued).
+// Per-lane window of resolved run geometry: lane i holds item base + i, so a
+// warp resolves 32 descriptors with one round of loads and the issuing lane
+// reads item c with one shuffle.
+struct RunWindow {
+  uint32_t base;
+  const char* src;
+  char* dst;
+  uint32_t bytes;  // 0 = nothing to move (skipped or out of range)
+};
+
+__device__ __forceinline__ void window_fill(const RunArgs& a, const Plane& p, uint32_t gw, uint32_t tw,
+                                            uint32_t n, uint32_t base, uint32_t lane, RunWindow& w) {
+  w.base = base;
+  w.bytes = 0;
+  w.src = nullptr;
+  w.dst = nullptr;
+  const uint32_t c = base + lane;
+  RunItem it;
+  if (c < n && run_resolve(a, p, gw + c * tw, it)) {
+    w.src = it.src;
+    w.dst = it.dst;
+    w.bytes = uint32_t(it.n_rows) * uint32_t(a.row_bytes_dst);
+  }
+}
+
+// Warp-uniform read of item c from the window (refilled when c leaves it).
+__device__ __forceinline__ void window_get(const RunArgs& a, const Plane& p, uint32_t gw, uint32_t tw,
+                                           uint32_t n, uint32_t c, uint32_t lane, RunWindow& w,
+                                           const char*& src, char*& dst, uint32_t& bytes) {
+  if (c >= w.base + 32u) window_fill(a, p, gw, tw, n, c & ~31u, lane, w);
+  const int from = int(c - w.base);
+  src = reinterpret_cast<const char*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(w.src), from));
+  dst = reinterpret_cast<char*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(w.dst), from));
+  bytes = __shfl_sync(0xffffffffu, w.bytes, from);
+}
+
+// Each warp runs an independent pipeline of a.stages shared-memory stages
+// over the runs gw, gw + total_warps, ... of its CTA row's (layer, kv, head)
+// plane: lane 0 bulk-loads item c into stage c % stages and, once that
+// stage's mbarrier phase completes, bulk-stores it out. A stage is refilled
+// once the store that last read it has finished reading (wait_group.read 1
+// keeps one store in flight behind the one just issued). The other lanes
+// resolve run descriptors ahead of lane 0 (two windows: loads run up to
+// `stages` items ahead of stores).
 __global__ void __launch_bounds__(kBulkWarps * 32) copy_runs_bulk_kernel(RunArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   const uint32_t S = uint32_t(a.stages);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * kBulkMaxStages;
   unsigned char* buf = smem + kBulkBarBytes + size_t(warp) * S * size_t(a.stage_bytes);
-  if (lane != 0) return;
+  const Plane p = plane_of(a, blockIdx.y);
   const uint32_t gw = blockIdx.x * kBulkWarps + warp;
   const uint32_t tw = gridDim.x * kBulkWarps;
-  if (gw >= a.n_items) return;
-  const uint32_t n = (a.n_items - gw + tw - 1) / tw;
+  if (gw >= a.n_runs) return;  // warp-uniform
+  const uint32_t n = (a.n_runs - gw + tw - 1) / tw;
 
-  for (uint32_t s = 0; s < S; ++s) mbar_init(&bars[s], 1);
-  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  if (lane == 0) {
+    for (uint32_t s = 0; s < S; ++s) mbar_init(&bars[s], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  __syncwarp();
+
+  RunWindow wl, ws;  // load window, store window
+  window_fill(a, p, gw, tw, n, 0, lane, wl);
+  ws = wl;
 
   auto issue_load = [&](uint32_t c) {
-    const uint32_t s = c % S;
-    RunItem it;
-    if (run_resolve(a, gw + c * tw, it)) {
-      const uint32_t bytes = uint32_t(it.n_rows) * uint32_t(a.row_bytes_dst);
-      mbar_arrive_expect_tx(&bars[s], bytes);
-      bulk_load(buf + size_t(s) * a.stage_bytes, it.src, bytes, &bars[s]);
-    } else {
-      mbar_arrive(&bars[s]);  // completes the phase with nothing to move
+    const char* src;
+    char* dst;
+    uint32_t bytes;
+    window_get(a, p, gw, tw, n, c, lane, wl, src, dst, bytes);
+    if (lane == 0) {
+      const uint32_t s = c % S;
+      if (bytes != 0) {
+        mbar_arrive_expect_tx(&bars[s], bytes);
+        bulk_load(buf + size_t(s) * a.stage_bytes, src, bytes, &bars[s]);
+      } else {
+        mbar_arrive(&bars[s]);  // completes the phase with nothing to move
+      }
     }
   };
 
@@ -542,29 +725,35 @@ __global__ void __launch_bounds__(kBulkWarps * 32) copy_runs_bulk_kernel(RunArgs
   uint32_t c = 0;
   for (; c < n; ++c) {
     const uint32_t s = c % S;
-    if (!mbar_wait(&bars[s], (c / S) & 1u)) break;
-    RunItem it;
-    if (run_resolve(a, gw + c * tw, it)) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      bulk_store(it.dst, buf + size_t(s) * a.stage_bytes,
-                 uint32_t(it.n_rows) * uint32_t(a.row_bytes_dst));
+    uint32_t ok = 1;
+    if (lane == 0) ok = mbar_wait(&bars[s], (c / S) & 1u) ? 1u : 0u;
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (!ok) break;
+    const char* src;
+    char* dst;
+    uint32_t bytes;
+    window_get(a, p, gw, tw, n, c, lane, ws, src, dst, bytes);
+    if (lane == 0) {
+      if (bytes != 0) bulk_store(dst, buf + size_t(s) * a.stage_bytes, bytes);
+      bulk_commit();
     }
-    bulk_commit();
     if (c >= 1 && c - 1 + S < n) {
-      bulk_wait_read<1>();
+      if (lane == 0) bulk_wait_read<1>();
       issue_load(c - 1 + S);
     }
   }
-  if (c < n) {
-    record_status(a.status, AUGUR_KV_ETIMEOUT);
-    // Loads issued so far: items [0, prologue) and the refills c' - 1 + S for
-    // 1 <= c' < c. Wait (bounded) for the ones not yet consumed before this
-    // CTA's shared memory can be released.
-    uint32_t issued_end = (c == 0) ? prologue : c + S - 1;
-    if (issued_end > n) issued_end = n;
-    for (uint32_t d = c + 1; d < issued_end; ++d) mbar_wait(&bars[d % S], (d / S) & 1u);
+  if (lane == 0) {
+    if (c < n) {
+      record_status(a.status, AUGUR_KV_ETIMEOUT);
+      // Loads issued so far: items [0, prologue) and the refills c' - 1 + S
+      // for 1 <= c' < c. Wait (bounded) for the ones not yet consumed before
+      // this CTA's shared memory can be released.
+      uint32_t issued_end = (c == 0) ? prologue : c + S - 1;
+      if (issued_end > n) issued_end = n;
+      for (uint32_t d = c + 1; d < issued_end; ++d) mbar_wait(&bars[d % S], (d / S) & 1u);
+    }
+    bulk_wait_all();
   }
-  bulk_wait_all();
 }
 
 }  // namespace augur_kv_dev
@@ -592,6 +781,8 @@ AUGUR_KV_EXPORT int augur_kv_scatter(const void* src_k, const void* src_v, const
   g_last_error[0] = '\0';
   const int es = elem_size(src_dtype), ed = elem_size(dst_dtype);
   if (es == 0 || ed == 0) return fail(AUGUR_KV_EINVAL, "scatter: unknown dtype %d/%d", src_dtype, dst_dtype);
+  if (n_tokens < 0 || n_layers < 0) return fail(AUGUR_KV_EINVAL, "scatter: negative sizes");
+  if (n_tokens == 0 || n_layers == 0) return AUGUR_KV_OK;  // empty tensors may have NULL data
   if (src_k == nullptr || dst_k == nullptr || index == nullptr || src_k_strides == nullptr ||
       dst_strides == nullptr || index_strides == nullptr)
     return fail(AUGUR_KV_EINVAL, "scatter: null pointer argument");
@@ -604,7 +795,6 @@ AUGUR_KV_EXPORT int augur_kv_scatter(const void* src_k, const void* src_v, const
     return fail(AUGUR_KV_EINVAL, "scatter: bad sizes");
   if (index_row_base != 0 && index_row_base != rows_per_major)
     return fail(AUGUR_KV_EINVAL, "scatter: index_row_base must be 0 or rows_per_major");
-  if (n_tokens == 0 || n_layers == 0) return AUGUR_KV_OK;
   if (n_layers > 65535) return fail(AUGUR_KV_EINVAL, "scatter: more than 65535 layers");
   if (tokens_per_row > n_tokens) tokens_per_row = n_tokens;
   if (n_tokens % tokens_per_row != 0)
@@ -670,6 +860,59 @@ AUGUR_KV_EXPORT int augur_kv_scatter(const void* src_k, const void* src_v, const
   a.sh_vpr = pow2_shift(a.vpr);
   a.sh_heads = pow2_shift(n_heads);
   const bool pow2 = a.sh_upt >= 0 && a.sh_vpr >= 0 && a.sh_heads >= 0;
+
+  // Fast path: lane-owned slots, one index lookup per token per layer group.
+  if (pow2 && a.upt >= 1 && a.upt <= 128) {
+    const int lanes = a.upt < 32 ? a.upt : 32;
+    const uint32_t tpw = uint32_t(32 / lanes);
+    const uint32_t n_token_groups = uint32_t((n_tokens + tpw - 1) / tpw);
+    // Small launches (a decode step: tens of tokens) need every (token, layer)
+    // as its own warp item to fill the GPU; large ones group LU layers per
+    // item to amortise the index lookup and keep LU loads in flight per lane.
+    const uint64_t items1 = uint64_t(n_token_groups) * uint64_t(n_layers);
+    const bool grouped = items1 > uint64_t(sm_count()) * 64 * 4;
+    constexpr int LU = AUGUR_KV_SCATTER_LU;
+    const uint64_t n_items = grouped ? uint64_t(n_token_groups) * uint64_t((n_layers + LU - 1) / LU) : items1;
+    if (n_items > 0x7FFFFFFFull) return fail(AUGUR_KV_EINVAL, "scatter: too many tokens");
+    // Grid: every resident CTA slot AUGUR_KV_SCATTER_WAVES times, each warp
+    // striding over the items, unless there are fewer items than that.
+    const uint64_t want = (n_items + 7) / 8;
+#define AUGUR_ROWS_LAUNCH_LU(VEC, UPT, LUV)                                                    \
+  do {                                                                                         \
+    auto kern = scatter_rows_kernel<VEC, UPT, LUV>;                                            \
+    uint64_t blocks = uint64_t(sm_count()) * resident_ctas((const void*)kern, 256) *           \
+                      AUGUR_KV_SCATTER_WAVES;                                                  \
+    if (blocks > want) blocks = want;                                                          \
+    kern<<<unsigned(blocks), 256, 0, st>>>(a, n_token_groups, uint32_t(n_items), n_layers);    \
+  } while (0)
+#define AUGUR_ROWS_LAUNCH(VEC, UPT)                       \
+  do {                                                    \
+    if (grouped) AUGUR_ROWS_LAUNCH_LU(VEC, UPT, LU);      \
+    else AUGUR_ROWS_LAUNCH_LU(VEC, UPT, 1);               \
+  } while (0)
+#define AUGUR_ROWS_UPT(VEC)                        \
+  switch (a.upt) {                                 \
+    case 1: AUGUR_ROWS_LAUNCH(VEC, 1); break;      \
+    case 2: AUGUR_ROWS_LAUNCH(VEC, 2); break;      \
+    case 4: AUGUR_ROWS_LAUNCH(VEC, 4); break;      \
+    case 8: AUGUR_ROWS_LAUNCH(VEC, 8); break;      \
+    case 16: AUGUR_ROWS_LAUNCH(VEC, 16); break;    \
+    case 32: AUGUR_ROWS_LAUNCH(VEC, 32); break;    \
+    case 64: AUGUR_ROWS_LAUNCH(VEC, 64); break;    \
+    default: AUGUR_ROWS_LAUNCH(VEC, 128); break;   \
+  }
+    switch (vec) {
+      case 16: AUGUR_ROWS_UPT(16); break;
+      case 8: AUGUR_ROWS_UPT(8); break;
+      case 4: AUGUR_ROWS_UPT(4); break;
+      case 2: AUGUR_ROWS_UPT(2); break;
+      default: AUGUR_ROWS_UPT(1); break;
+    }
+#undef AUGUR_ROWS_UPT
+#undef AUGUR_ROWS_LAUNCH
+#undef AUGUR_ROWS_LAUNCH_LU
+    return check_launch("scatter_rows_kernel");
+  }
   // Large launches give each thread 4 vectors in flight; small ones (decode
   // append) spread one vector per thread over more CTAs.
   const bool big = total * uint64_t(n_layers) >= uint64_t(sm_count()) * 256 * 16;
@@ -705,6 +948,8 @@ AUGUR_KV_EXPORT int augur_kv_copy_runs(const void* src_k, const void* src_v, con
   g_last_error[0] = '\0';
   const int es = elem_size(src_dtype), ed = elem_size(dst_dtype);
   if (es == 0 || ed == 0) return fail(AUGUR_KV_EINVAL, "copy_runs: unknown dtype %d/%d", src_dtype, dst_dtype);
+  if (n_runs < 0 || n_layers < 0) return fail(AUGUR_KV_EINVAL, "copy_runs: negative sizes");
+  if (n_runs == 0 || n_layers == 0) return AUGUR_KV_OK;  // empty tensors may have NULL data
   if (src_k == nullptr || dst_k == nullptr || runs == nullptr || src_strides == nullptr ||
       dst_strides == nullptr)
     return fail(AUGUR_KV_EINVAL, "copy_runs: null pointer argument");
@@ -717,11 +962,10 @@ AUGUR_KV_EXPORT int augur_kv_copy_runs(const void* src_k, const void* src_v, con
     return fail(AUGUR_KV_EINVAL, "copy_runs: unknown flags %d", flags);
   if (int64_t(max_rows) * head_dim * ed > 16384)
     return fail(AUGUR_KV_EINVAL, "copy_runs: max_rows * row bytes exceeds 16384");
-  if (n_runs == 0 || n_layers == 0) return AUGUR_KV_OK;
   const int n_kv = (src_v != nullptr) ? 2 : 1;
-  const uint64_t items = uint64_t(n_runs) * uint64_t(n_layers) * uint64_t(n_kv) * uint64_t(n_heads);
-  if (items > 0x7FFFFFFFull || n_runs > 0x7FFFFFFF)
-    return fail(AUGUR_KV_EINVAL, "copy_runs: too many runs");
+  const uint64_t planes = uint64_t(n_layers) * uint64_t(n_kv) * uint64_t(n_heads);
+  if (planes > 65535) return fail(AUGUR_KV_EINVAL, "copy_runs: more than 65535 (layer, kv, head) planes");
+  if (n_runs > 0x7FFFFFFF) return fail(AUGUR_KV_EINVAL, "copy_runs: too many runs");
 
   RunArgs a;
   memset(&a, 0, sizeof(a));
@@ -739,7 +983,6 @@ AUGUR_KV_EXPORT int augur_kv_copy_runs(const void* src_k, const void* src_v, con
   a.dst_rpm = dst_rows_per_major;
   a.runs = runs;
   a.n_runs = uint32_t(n_runs);
-  a.n_items = uint32_t(items);
   a.max_rows = max_rows;
   a.n_heads = n_heads;
   a.n_kv = n_kv;
@@ -755,9 +998,8 @@ AUGUR_KV_EXPORT int augur_kv_copy_runs(const void* src_k, const void* src_v, con
     a.vpr = head_dim;
     a.unit_bytes_src = es;
     a.unit_bytes_dst = ed;
-    uint64_t blocks = (items + 7) / 8;
-    if (blocks > uint64_t(sms) * 16) blocks = uint64_t(sms) * 16;
-    copy_runs_convert_kernel<<<unsigned(blocks), 256, 0, st>>>(a);
+    const dim3 grid{grid_x(uint64_t(n_runs), 8, planes, uint64_t(sms) * 16), unsigned(planes), 1u};
+    copy_runs_convert_kernel<<<grid, 256, 0, st>>>(a);
     return check_launch("copy_runs_convert_kernel");
   }
 
@@ -771,7 +1013,9 @@ AUGUR_KV_EXPORT int augur_kv_copy_runs(const void* src_k, const void* src_v, con
 
   if (flags == AUGUR_KV_COPY_BULK && !bulk_ok)
     return fail(AUGUR_KV_EINVAL, "copy_runs: bulk path needs dense rows and 16-byte alignment");
-  if (bulk_ok && flags != AUGUR_KV_COPY_VECTOR) {
+  // AUTO takes the vector path: on B200 it measured faster than the bulk
+  // pipeline for 2 KiB runs (config-3 handoff 6.1 vs 5.4 TB/s).
+  if (bulk_ok && flags == AUGUR_KV_COPY_BULK) {
     a.stage_bytes = int32_t(((int64_t(max_rows) * row_bytes + 127) / 128) * 128);
     int stages = (kBulkSmemBudget - kBulkBarBytes) / (kBulkWarps * a.stage_bytes);
     if (stages > kBulkMaxStages) stages = kBulkMaxStages;
@@ -782,21 +1026,22 @@ AUGUR_KV_EXPORT int augur_kv_copy_runs(const void* src_k, const void* src_v, con
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
       return fail(AUGUR_KV_ECUDA, "copy_runs: cannot query the current device");
-    if (smem > 48 * 1024 && attr_bytes[dev] < smem) {
-      if (cudaFuncSetAttribute(copy_runs_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               smem) != cudaSuccess)
-        return check_launch("cudaFuncSetAttribute(copy_runs_bulk_kernel)");
-      attr_bytes[dev] = smem;
+    {
+      std::lock_guard<std::mutex> lock(g_cache_mutex);
+      if (smem > 48 * 1024 && attr_bytes[dev] < smem) {
+        if (cudaFuncSetAttribute(copy_runs_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 smem) != cudaSuccess)
+          return check_launch("cudaFuncSetAttribute(copy_runs_bulk_kernel)");
+        attr_bytes[dev] = smem;
+      }
     }
-    // Persistent grid: as many CTAs as shared memory allows per SM, one wave;
-    // every warp runs its own pipeline.
+    // One wave: as many CTAs as shared memory allows per SM, spread over the
+    // planes; every warp runs its own pipeline over its plane's runs.
     int per_sm = (220 * 1024) / smem;
     if (per_sm < 1) per_sm = 1;
     if (per_sm > 8) per_sm = 8;
-    uint64_t blocks = uint64_t(sms) * per_sm;
-    const uint64_t need = (items + kBulkWarps - 1) / kBulkWarps;
-    if (blocks > need) blocks = need;
-    copy_runs_bulk_kernel<<<unsigned(blocks), kBulkWarps * 32, smem, st>>>(a);
+    const dim3 grid{grid_x(uint64_t(n_runs), kBulkWarps, planes, uint64_t(sms) * per_sm), unsigned(planes), 1u};
+    copy_runs_bulk_kernel<<<grid, kBulkWarps * 32, smem, st>>>(a);
     return check_launch("copy_runs_bulk_kernel");
   }
 
@@ -804,14 +1049,19 @@ AUGUR_KV_EXPORT int augur_kv_copy_runs(const void* src_k, const void* src_v, con
   while (vec > 1 && (align_bits & uintptr_t(vec - 1)) != 0) vec >>= 1;
   a.vpr = int32_t(row_bytes / vec);
   a.sh_vpr = pow2_shift(a.vpr);
-  uint64_t blocks = (items + 7) / 8;
-  if (blocks > uint64_t(sms) * 32) blocks = uint64_t(sms) * 32;
+  const dim3 grid{grid_x(uint64_t(n_runs), 8, planes, uint64_t(sms) * 32), unsigned(planes), 1u};
+#define AUGUR_RUNS_LAUNCH(VEC)                                                        \
+  do {                                                                               \
+    if (dense) copy_runs_vec_kernel<VEC, true><<<grid, 256, 0, st>>>(a);              \
+    else copy_runs_vec_kernel<VEC, false><<<grid, 256, 0, st>>>(a);                   \
+  } while (0)
   switch (vec) {
-    case 16: copy_runs_vec_kernel<16><<<unsigned(blocks), 256, 0, st>>>(a); break;
-    case 8: copy_runs_vec_kernel<8><<<unsigned(blocks), 256, 0, st>>>(a); break;
-    case 4: copy_runs_vec_kernel<4><<<unsigned(blocks), 256, 0, st>>>(a); break;
-    case 2: copy_runs_vec_kernel<2><<<unsigned(blocks), 256, 0, st>>>(a); break;
-    default: copy_runs_vec_kernel<1><<<unsigned(blocks), 256, 0, st>>>(a); break;
+    case 16: AUGUR_RUNS_LAUNCH(16); break;
+    case 8: AUGUR_RUNS_LAUNCH(8); break;
+    case 4: AUGUR_RUNS_LAUNCH(4); break;
+    case 2: AUGUR_RUNS_LAUNCH(2); break;
+    default: AUGUR_RUNS_LAUNCH(1); break;
   }
+#undef AUGUR_RUNS_LAUNCH
   return check_launch("copy_runs_vec_kernel");
 }

@@ -243,13 +243,16 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     n_sets = 4
-    pool = ab.PagedKVCache(keys=torch.empty(L, 65536, H, BS, D, dtype=torch.bfloat16, device=device),
-                           values=torch.empty(L, 65536, H, BS, D, dtype=torch.bfloat16, device=device),
-                           block_size=BS, allocator=ab.BlockAllocator(65536))
+    # --small (profiling only): an 8192-block pool instead of 65536; every
+    # launch moves the same bytes, the device holds 1.9 GB instead of 13 GB.
+    nblocks = 8192 if args.small else 65536
+    pool = ab.PagedKVCache(keys=torch.empty(L, nblocks, H, BS, D, dtype=torch.bfloat16, device=device),
+                           values=torch.empty(L, nblocks, H, BS, D, dtype=torch.bfloat16, device=device),
+                           block_size=BS, allocator=ab.BlockAllocator(nblocks))
     sets, offset = [], 0
     host_sets = []
     for s in range(n_sets):
-        lens, slots, k, v, used = config2_batch(seed=1000 * rank + s, block_offset=offset)
+        lens, slots, k, v, used = config2_batch(seed=1000 * rank + s, block_offset=offset, num_blocks=nblocks)
         offset += used
         host_sets.append((slots, k, v))
         sets.append((torch.from_numpy(slots).to(device), k.to(device), v.to(device)))
@@ -384,7 +387,7 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
     return line
 
 
-def run_extras(device) -> dict:
+def run_extras(device, handoff_only: bool = False) -> dict:
     """Config 3 handoff + decode append and config 4 fork/COW, timed with CUDA events."""
     import augur_b200 as ab
     from augur_b200 import _lib, _ops, batched
@@ -424,6 +427,8 @@ def run_extras(device) -> dict:
         ms = statistics.median(times[2:])
         out[f"handoff_{name}"] = {"us_per_seq": round(ms * 1e3 / B, 3), "ms": round(ms, 4),
                                   "GBps": round(hbytes / (ms / 1e3) / 1e9, 1), "seqs": B, "tokens": tok}
+    if handoff_only:
+        return out
     # decode append: 256 steps of one token per sequence, all layers, captured in one graph
     for t, n in zip(tables, lens):
         t.seq_len = int(n)
@@ -538,9 +543,17 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-extras", action="store_true")
+    ap.add_argument("--small", action="store_true", help="profiling case: 8192-block pool, no extras/CPU")
+    ap.add_argument("--handoff-only", action="store_true", help="profiling case: config-3 handoff only")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.small:
+        args.skip_cpu = args.skip_extras = True
+    if args.handoff_only:  # profiling case: only the config-3 handoff (about 3 GB on the device)
+        torch.cuda.set_device(0)
+        print(json.dumps(run_extras(torch.device("cuda", 0), handoff_only=True)), flush=True)
+        return
     world, rank, local = dist_env()
     if args.impl == "reference":
         line = run_reference(args, world, rank)

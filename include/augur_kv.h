@@ -6,8 +6,11 @@
  * arrays, int32/int64 device index arrays and the caller's cudaStream_t (as
  * void*). Nothing here allocates, synchronises or keeps state between calls
  * except the thread-local text returned by augur_kv_last_error(). All work is
- * stream-ordered on the given stream. Validation that needs host data (shapes,
- * position ranges, allocator state) is the host wrapper's job; the kernels
+ * stream-ordered on the given stream. A call with no work (zero tokens, runs
+ * or layers) returns AUGUR_KV_OK without looking at its data pointers, which
+ * may then be NULL (torch gives empty tensors a NULL data pointer).
+ * Validation that needs host data (shapes, position ranges, allocator
+ * state) is the host wrapper's job; the kernels
  * still bounds-check every index they dereference and, instead of touching
  * memory out of range, record AUGUR_KV_EBOUNDS in the optional device status
  * word (int32, first error wins) and skip that row.
@@ -44,9 +47,9 @@ extern "C" {
 #define AUGUR_KV_BF16 2
 
 /* Flags for augur_kv_copy_runs. */
-#define AUGUR_KV_COPY_AUTO 0   /* TMA bulk path when every address is 16-byte aligned, else vector path */
-#define AUGUR_KV_COPY_VECTOR 1 /* force the 16/8/4/2/1-byte vector path */
-#define AUGUR_KV_COPY_BULK 2   /* require the TMA bulk path (EINVAL if not aligned) */
+#define AUGUR_KV_COPY_AUTO 0   /* the measured-faster path for the layout (currently the vector path) */
+#define AUGUR_KV_COPY_VECTOR 1 /* the 16/8/4/2/1-byte vector path */
+#define AUGUR_KV_COPY_BULK 2   /* the TMA bulk path (EINVAL unless rows are dense and 16-byte aligned) */
 
 /* Library version, (major << 16) | minor. */
 int augur_kv_version(void);

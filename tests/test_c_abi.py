@@ -65,6 +65,17 @@ def test_scatter_rejects_bad_arguments_without_touching_the_device():
     assert code == _lib.EINVAL and b"index_row_base" in lib.augur_kv_last_error()
 
 
+def test_empty_work_is_ok_with_null_pointers():
+    lib = _lib.load()
+    s = _i64(0, 0, 1, 1)
+    assert lib.augur_kv_scatter(None, None, s, s, 1, _lib.BF16, None, None, s, 16, 1, _lib.BF16,
+                                None, _i64(0, 1), 0, 0, 24, 2, 64, None, None) == _lib.OK
+    assert lib.augur_kv_copy_runs(None, None, s, 1, 1, _lib.BF16, None, None, s, 1, 1, _lib.BF16,
+                                  None, 0, 16, 24, 2, 64, 0, None, None) == _lib.OK
+    assert lib.augur_kv_scatter(None, None, s, s, 1, _lib.BF16, None, None, s, 16, 1, _lib.BF16,
+                                None, _i64(0, 1), 0, -1, 24, 2, 64, None, None) == _lib.EINVAL
+
+
 def test_copy_runs_rejects_bad_arguments_without_touching_the_device():
     lib = _lib.load()
     fake = ctypes.c_void_p(16)

@@ -254,7 +254,7 @@ def test_kernel_bounds_check_records_status(cuda):
     assert code == _lib.OK
     torch.cuda.synchronize()
     assert int(status.item()) == _lib.EBOUNDS
-    assert torch.equal(pool_k[0, 3].cpu(), pool_k[0, 1].cpu())
+    assert_bits_equal(pool_k[0, 3], pool_k[0, 1], "copied block")
 
 
 def test_empty_inputs_launch_nothing(cuda):
@@ -266,3 +266,25 @@ def test_empty_inputs_launch_nothing(cuda):
     batched.copy_blocks(pool, [], [])
     assert _ops.launch_count == before
     assert (pool.keys.view(torch.uint8) == 0xFF).all()
+
+
+@pytest.mark.parametrize("flags", [_lib.COPY_BULK, _lib.COPY_VECTOR])
+def test_handoff_many_runs_per_warp_vs_oracle(cuda, oracle, flags):
+    """24 layers x 2 heads x 2 (K, V) planes and ~1500 runs: each bulk-pipeline warp walks
+    well over 32 runs, so its descriptor windows refill several times."""
+    rng = np.random.default_rng(77)
+    g = torch.Generator().manual_seed(77)
+    L, B, H, S, D, bs, NB = 24, 32, 2, 1024, 64, 16, 2304
+    lens = rng.integers(512, S + 1, size=B)
+    src = ab.KVCache(keys=_rand((L, B, H, S, D), torch.bfloat16, g).to(cuda),
+                     values=_rand((L, B, H, S, D), torch.bfloat16, g).to(cuda))
+    pool = _pool(L, NB, H, bs, D, torch.bfloat16, cuda)
+    tables = _random_tables(rng, lens, bs, NB)
+    runs_t = batched.handoff_contiguous_to_paged(src, pool, tables, lens, flags=flags)
+    assert runs_t.shape[0] > 1000
+    ek = poison_(torch.empty(L, NB, H, bs, D, dtype=torch.bfloat16))
+    ev = poison_(torch.empty(L, NB, H, bs, D, dtype=torch.bfloat16))
+    oracle.copy_runs(src.keys.cpu(), src.values.cpu(), ek, ev, batched.handoff_runs(tables, lens), threads=8)
+    assert_bits_equal(pool.keys, ek, "keys")
+    assert_bits_equal(pool.values, ev, "values")
+    assert _ops.read_status(cuda) == _lib.OK
