@@ -54,7 +54,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _P, _I64P, _I64, _I64, _I32, _P, _P, _I64P, _I64, _I64, _I32, _P, _I64, _I32,
          _I32, _I32, _I32, _I32, _P, _P],
     ),
+    "augur_kv_copy_runs_noalloc": (
+        ctypes.c_int,
+        [_P, _P, _I64P, _I64, _I64, _I32, _P, _P, _I64P, _I64, _I64, _I32, _P, _I64, _I32,
+         _I32, _I32, _I32, _I32, _P, _P],
+    ),
 }
+
+NOALLOC_MAX_RUNS = 65536
 
 
 class KVLibraryError(RuntimeError):

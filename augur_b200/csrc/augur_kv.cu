@@ -1065,3 +1065,70 @@ AUGUR_KV_EXPORT int augur_kv_copy_runs(const void* src_k, const void* src_v, con
 #undef AUGUR_RUNS_LAUNCH
   return check_launch("copy_runs_vec_kernel");
 }
+
+// ---------------------------------------------------------------------------
+// augur_kv_copy_runs_noalloc: the run copy for callers that cannot allocate
+// device memory. The run descriptors, which augur_kv_copy_runs reads from a
+// device buffer the caller allocated, are staged instead in this file-scope
+// array: AUGUR_KV_NOALLOC_MAX_RUNS x 5 int32 (1.25 MiB), which every GPU that
+// loads this library holds until the process exits. All calls share it; a
+// call overwrites exactly the n_runs entries its kernel reads, so nothing in
+// it needs clearing, and calls whose copies overlap on the GPU (different
+// streams) race on it.
+// ---------------------------------------------------------------------------
+
+static __device__ __align__(256) int32_t g_noalloc_runs[AUGUR_KV_NOALLOC_MAX_RUNS * 5];
+
+namespace augur_kv_dev {
+
+// Device address of g_noalloc_runs for the current device, looked up once per
+// device (the first call on a device) with cudaGetSymbolAddress. Host code
+// must never pass &g_noalloc_runs itself: on the host that name is only a
+// stand-in for the device symbol.
+int noalloc_runs_ptr(int32_t** out) {
+  static void* cached[kMaxDevices] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return fail(AUGUR_KV_ECUDA, "copy_runs_noalloc: cannot query the current device");
+  std::lock_guard<std::mutex> lock(g_cache_mutex);
+  if (cached[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_runs);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(AUGUR_KV_ECUDA, "copy_runs_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    cached[dev] = p;
+  }
+  *out = static_cast<int32_t*>(cached[dev]);
+  return AUGUR_KV_OK;
+}
+
+}  // namespace augur_kv_dev
+
+AUGUR_KV_EXPORT int augur_kv_copy_runs_noalloc(
+    const void* src_k, const void* src_v, const int64_t* src_strides, int64_t src_majors,
+    int64_t src_rows_per_major, int32_t src_dtype, void* dst_k, void* dst_v, const int64_t* dst_strides,
+    int64_t dst_majors, int64_t dst_rows_per_major, int32_t dst_dtype, const int32_t* host_runs,
+    int64_t n_runs, int32_t max_rows, int32_t n_layers, int32_t n_heads, int32_t head_dim, int32_t flags,
+    int32_t* status, void* stream) {
+  g_last_error[0] = '\0';
+  if (n_runs < 0) return fail(AUGUR_KV_EINVAL, "copy_runs_noalloc: negative n_runs");
+  if (n_runs > AUGUR_KV_NOALLOC_MAX_RUNS)
+    return fail(AUGUR_KV_EINVAL,
+                "copy_runs_noalloc: %lld runs exceed the fixed scratch of %d runs; split the call "
+                "or use augur_kv_copy_runs with a caller-allocated run buffer",
+                (long long)n_runs, AUGUR_KV_NOALLOC_MAX_RUNS);
+  if (n_runs == 0 || n_layers == 0) return AUGUR_KV_OK;
+  if (host_runs == nullptr) return fail(AUGUR_KV_EINVAL, "copy_runs_noalloc: null host_runs");
+  int32_t* scratch = nullptr;
+  const int rc = noalloc_runs_ptr(&scratch);
+  if (rc != AUGUR_KV_OK) return rc;
+  // Stream-ordered staging of the descriptors, then the same launch as
+  // augur_kv_copy_runs reading them from the scratch array.
+  const cudaError_t e = cudaMemcpyAsync(scratch, host_runs, size_t(n_runs) * 5 * sizeof(int32_t),
+                                        cudaMemcpyHostToDevice, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess)
+    return fail(AUGUR_KV_ECUDA, "copy_runs_noalloc: staging runs: %s", cudaGetErrorString(e));
+  return augur_kv_copy_runs(src_k, src_v, src_strides, src_majors, src_rows_per_major, src_dtype, dst_k,
+                            dst_v, dst_strides, dst_majors, dst_rows_per_major, dst_dtype, scratch, n_runs,
+                            max_rows, n_layers, n_heads, head_dim, flags, status, stream);
+}

@@ -126,6 +126,46 @@ int augur_kv_copy_runs(const void* src_k, const void* src_v,
                        int32_t n_layers, int32_t n_heads, int32_t head_dim,
                        int32_t flags, int32_t* status, void* stream);
 
+/*
+ * augur_kv_copy_runs_noalloc — augur_kv_copy_runs for callers that cannot
+ * allocate device memory. No counterpart in the reference (augur allocates
+ * through torch).
+ *
+ * augur_kv_copy_runs reads its run list from a device buffer the caller must
+ * allocate. Some callers cannot call cudaMalloc: an engine whose device memory
+ * is one up-front reservation carved into cache blocks by its own allocator
+ * (an extra allocation would fail or break its accounting), or a plain C/C++
+ * host without a device allocator of its own. This variant takes the run list
+ * in HOST memory (same [n_runs][5] layout) and stages it in a fixed array
+ * inside the library (a file-scope __device__ array of
+ * AUGUR_KV_NOALLOC_MAX_RUNS runs, 1.25 MiB, held by every GPU that loads the
+ * library until the process exits); the caller still passes the caches
+ * themselves. It calls no cudaMalloc, cudaFree or other allocating routine.
+ *
+ * - n_runs > AUGUR_KV_NOALLOC_MAX_RUNS is rejected with AUGUR_KV_EINVAL.
+ * - The first call on each device looks up the array's device address
+ *   (cudaGetSymbolAddress); make that first call before any stream capture.
+ * - host_runs is read by a stream-ordered host-to-device copy: pageable memory
+ *   may be reused when the call returns; pinned memory must stay unchanged
+ *   until the stream has passed this call.
+ * - Every call shares the one array. Calls whose work overlaps on the GPU
+ *   (issued on different streams without ordering) race on it.
+ * Everything else (arguments, bounds checks, status word) is as for
+ * augur_kv_copy_runs.
+ */
+#define AUGUR_KV_NOALLOC_MAX_RUNS 65536
+
+int augur_kv_copy_runs_noalloc(const void* src_k, const void* src_v,
+                               const int64_t* src_strides, /* [4] */
+                               int64_t src_majors, int64_t src_rows_per_major, int32_t src_dtype,
+                               void* dst_k, void* dst_v,
+                               const int64_t* dst_strides, /* [4] */
+                               int64_t dst_majors, int64_t dst_rows_per_major, int32_t dst_dtype,
+                               const int32_t* host_runs, /* HOST [n_runs][5] */
+                               int64_t n_runs, int32_t max_rows,
+                               int32_t n_layers, int32_t n_heads, int32_t head_dim,
+                               int32_t flags, int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
