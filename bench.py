@@ -361,8 +361,8 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
     roofline = {
         "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
         "frac": round(achieved / peak, 4), "peak_source": f"hbm_gbs of {peak_kind}",
-        "traffic": load_traffic("scatter_vec_kernel", "config2"),
-        "algorithmic_bytes_per_launch": step_bytes, "kernel": "scatter_vec_kernel<16,true,4>",
+        "traffic": load_traffic("scatter_rows_kernel", "config2"),
+        "algorithmic_bytes_per_launch": step_bytes, "kernel": "scatter_rows_kernel<16,32,8>",
         "launch_us": round(per_launch_s * 1e6, 2),
     }
     line = {
