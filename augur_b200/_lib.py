@@ -59,9 +59,13 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _P, _I64P, _I64, _I64, _I32, _P, _P, _I64P, _I64, _I64, _I32, _P, _I64, _I32,
          _I32, _I32, _I32, _I32, _P, _P],
     ),
+    "augur_kv_ipc_export": (ctypes.c_int, [_P, _P, _I64P]),
+    "augur_kv_ipc_open": (ctypes.c_int, [_P, _I64, ctypes.POINTER(ctypes.c_void_p)]),
+    "augur_kv_ipc_close": (ctypes.c_int, [_P, _I64]),
 }
 
 NOALLOC_MAX_RUNS = 65536
+IPC_HANDLE_BYTES = 64
 
 
 class KVLibraryError(RuntimeError):

@@ -98,6 +98,18 @@ def _ptr(t: Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+def keep_until_done(stream: torch.cuda.Stream, *tensors: Tensor | None) -> None:
+    """Keep device tensors used by work on `stream` from being reused before it runs.
+
+    Torch's caching allocator orders reuse on the stream a tensor was
+    allocated on; for launches on another stream the tensor is recorded there.
+    """
+    for t in tensors:
+        if t is not None and t.device.type == "cuda":
+            if stream != torch.cuda.current_stream(t.device):
+                t.record_stream(stream)
+
+
 def scatter(
     *,
     src_k: Tensor,
@@ -154,6 +166,7 @@ def scatter(
     _lib.check(code, "augur_kv_scatter")
     if n_tokens > 0 and n_layers > 0:
         launch_count += 1
+        keep_until_done(st, index, src_k, src_v)
 
 
 def copy_runs(
@@ -211,6 +224,7 @@ def copy_runs(
     _lib.check(code, "augur_kv_copy_runs")
     if runs.shape[0] > 0 and n_layers > 0:
         launch_count += 1
+        keep_until_done(st, runs, src_k, src_v)
 
 
 def max_rows_for(head_dim: int, elem_size: int, cap_rows: int = 64, cap_bytes: int = 8192) -> int:

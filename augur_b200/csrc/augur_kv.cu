@@ -1067,6 +1067,76 @@ AUGUR_KV_EXPORT int augur_kv_copy_runs(const void* src_k, const void* src_v, con
 }
 
 // ---------------------------------------------------------------------------
+// Peer memory (CUDA IPC) for pushing blocks to another process's GPU
+// ---------------------------------------------------------------------------
+
+namespace augur_kv_dev {
+
+// cuMemGetAddressRange through the runtime's driver entry point, so the
+// library needs no link-time dependency on libcuda.
+typedef int (*MemGetAddressRangeFn)(unsigned long long*, size_t*, unsigned long long);
+
+int allocation_base(const void* ptr, const char** base) {
+  static MemGetAddressRangeFn fn = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_cache_mutex);
+    if (fn == nullptr) {
+      void* f = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) != cudaSuccess ||
+          q != cudaDriverEntryPointSuccess || f == nullptr)
+        return fail(AUGUR_KV_ECUDA, "ipc: cuMemGetAddressRange entry point unavailable");
+      fn = reinterpret_cast<MemGetAddressRangeFn>(f);
+    }
+  }
+  unsigned long long b = 0;
+  size_t size = 0;
+  const int rc = fn(&b, &size, reinterpret_cast<unsigned long long>(ptr));
+  if (rc != 0 || b == 0) return fail(AUGUR_KV_EINVAL, "ipc: %p is not inside a device allocation (%d)", ptr, rc);
+  *base = reinterpret_cast<const char*>(b);
+  return AUGUR_KV_OK;
+}
+
+}  // namespace augur_kv_dev
+
+AUGUR_KV_EXPORT int augur_kv_ipc_export(const void* dev_ptr, void* handle_out, int64_t* offset_out) {
+  g_last_error[0] = '\0';
+  if (dev_ptr == nullptr || handle_out == nullptr || offset_out == nullptr)
+    return fail(AUGUR_KV_EINVAL, "ipc_export: null pointer argument");
+  static_assert(sizeof(cudaIpcMemHandle_t) == AUGUR_KV_IPC_HANDLE_BYTES, "IPC handle size");
+  const char* base = nullptr;
+  const int rc = allocation_base(dev_ptr, &base);
+  if (rc != AUGUR_KV_OK) return rc;
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<char*>(base));
+  if (e != cudaSuccess) return fail(AUGUR_KV_ECUDA, "ipc_export: cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+  memcpy(handle_out, &h, sizeof(h));
+  *offset_out = static_cast<const char*>(dev_ptr) - base;
+  return AUGUR_KV_OK;
+}
+
+AUGUR_KV_EXPORT int augur_kv_ipc_open(const void* handle, int64_t offset, void** dev_ptr_out) {
+  g_last_error[0] = '\0';
+  if (handle == nullptr || dev_ptr_out == nullptr || offset < 0)
+    return fail(AUGUR_KV_EINVAL, "ipc_open: bad argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(AUGUR_KV_ECUDA, "ipc_open: cudaIpcOpenMemHandle: %s", cudaGetErrorString(e));
+  *dev_ptr_out = static_cast<char*>(base) + offset;
+  return AUGUR_KV_OK;
+}
+
+AUGUR_KV_EXPORT int augur_kv_ipc_close(void* dev_ptr, int64_t offset) {
+  g_last_error[0] = '\0';
+  if (dev_ptr == nullptr || offset < 0) return fail(AUGUR_KV_EINVAL, "ipc_close: bad argument");
+  const cudaError_t e = cudaIpcCloseMemHandle(static_cast<char*>(dev_ptr) - offset);
+  if (e != cudaSuccess) return fail(AUGUR_KV_ECUDA, "ipc_close: cudaIpcCloseMemHandle: %s", cudaGetErrorString(e));
+  return AUGUR_KV_OK;
+}
+
+// ---------------------------------------------------------------------------
 // augur_kv_copy_runs_noalloc: the run copy for callers that cannot allocate
 // device memory. The run descriptors, which augur_kv_copy_runs reads from a
 // device buffer the caller allocated, are staged instead in this file-scope

@@ -1,0 +1,148 @@
+"""Disaggregated prefill -> decode: push finished KV blocks to another GPU's pool.
+
+A decode rank exports its block pool (export_pool); a prefill rank opens it
+(open_pool: the pool's memory is mapped into the prefill GPU's address space
+with CUDA IPC, peer access enabled as needed) and pushes blocks with
+push_blocks: one augur_kv_copy_runs launch on the prefill GPU that reads its
+local blocks and stores 16-byte vectors straight into the peer pool over
+NVLink, every layer, K and V. Block ids on the destination come from the
+decode rank's own allocator; tables travel as host data.
+
+No reference counterpart: augur runs in one process on one device. The
+result is defined as equal, byte for byte, to writing the same tokens into
+the destination pool locally (tests/test_gpu_peer.py checks exactly that).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from collections.abc import Sequence
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib, _ops
+from .batched import split_runs
+from .paged_kv_cache import PagedKVCache
+
+
+@dataclass
+class ExportedPool:
+    """Picklable description of a pool another process can open."""
+
+    key_handle: bytes
+    key_offset: int
+    value_handle: bytes
+    value_offset: int
+    shape: tuple[int, ...]
+    stride: tuple[int, ...]
+    dtype: str
+    device_index: int
+    block_size: int
+
+
+def _export(t: torch.Tensor) -> tuple[bytes, int]:
+    lib = _lib.load()
+    handle = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
+    off = ctypes.c_int64(0)
+    with _ops._DeviceGuard(t.device):
+        _lib.check(lib.augur_kv_ipc_export(t.data_ptr(), handle, ctypes.byref(off)), "augur_kv_ipc_export")
+    return handle.raw, int(off.value)
+
+
+def export_pool(cache: PagedKVCache) -> ExportedPool:
+    _ops.require_cuda("export_pool", cache.keys, cache.values)
+    if cache.keys.stride() != cache.values.stride():
+        raise ValueError("keys and values must share one layout")
+    kh, ko = _export(cache.keys)
+    vh, vo = _export(cache.values)
+    return ExportedPool(kh, ko, vh, vo, tuple(cache.keys.shape), tuple(cache.keys.stride()),
+                        str(cache.keys.dtype).replace("torch.", ""), cache.keys.device.index,
+                        cache.block_size)
+
+
+class PeerPool:
+    """Another process's pool, mapped into this process's current CUDA device.
+
+    Keys and values may live in one allocation (torch's caching allocator
+    packs small tensors into shared segments); each distinct allocation is
+    opened once and both addresses are derived from it.
+    """
+
+    def __init__(self, exported: ExportedPool, device: torch.device) -> None:
+        self.exported = exported
+        self.device = device
+        self.shape = exported.shape
+        self.stride = exported.stride
+        self.dtype = getattr(torch, exported.dtype)
+        self.block_size = exported.block_size
+        self._bases: dict[bytes, int] = {}
+        lib = _lib.load()
+        with _ops._DeviceGuard(device):
+            for h in {exported.key_handle, exported.value_handle}:
+                out = ctypes.c_void_p()
+                _lib.check(lib.augur_kv_ipc_open(h, 0, ctypes.byref(out)), "augur_kv_ipc_open")
+                self._bases[h] = int(out.value)
+        self.keys_ptr = self._bases[exported.key_handle] + exported.key_offset
+        self.values_ptr = self._bases[exported.value_handle] + exported.value_offset
+
+    def close(self) -> None:
+        lib = _lib.load()
+        with _ops._DeviceGuard(self.device):
+            for h, base in list(self._bases.items()):
+                _lib.check(lib.augur_kv_ipc_close(base, 0), "augur_kv_ipc_close")
+                del self._bases[h]
+        self.keys_ptr = self.values_ptr = 0
+
+
+def open_pool(exported: ExportedPool, device: torch.device | None = None) -> PeerPool:
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    return PeerPool(exported, device)
+
+
+def push_runs(src: PagedKVCache, dst: PeerPool, runs: np.ndarray, stream: torch.cuda.Stream | None = None) -> int:
+    """Copy row runs {src_block, src_row, dst_block, dst_row, n_rows} from a local pool into the peer pool.
+
+    One launch on this process's device; returns the payload bytes moved.
+    """
+    L, NB, H, bs, D = src.keys.shape
+    if dst.shape[0] != L or dst.shape[2] != H or dst.shape[4] != D or dst.dtype != src.keys.dtype:
+        raise ValueError("source and destination pools have different layer/head/dim/dtype")
+    max_rows = _ops.max_rows_for(D, src.keys.element_size(), cap_rows=max(bs, dst.block_size))
+    runs = split_runs(np.asarray(runs, dtype=np.int64).reshape(-1, 5), max_rows)
+    if runs.shape[0] == 0:
+        return 0
+    lib = _lib.load()
+    device = src.keys.device
+    runs_t = torch.from_numpy(np.ascontiguousarray(runs)).to(device)
+    st = stream if stream is not None else torch.cuda.current_stream(device)
+    sk = src.keys
+    s_str = (sk.stride(0), sk.stride(1), sk.stride(3), sk.stride(2))
+    d = dst.stride
+    d_str = (d[0], d[1], d[3], d[2])
+    with _ops._DeviceGuard(device):
+        code = lib.augur_kv_copy_runs(
+            sk.data_ptr(), src.values.data_ptr(), _lib.i64_array(s_str), NB, bs, _ops.dtype_code(sk),
+            dst.keys_ptr, dst.values_ptr, _lib.i64_array(d_str), dst.shape[1], dst.shape[3],
+            _ops.dtype_code(sk), runs_t.data_ptr(), runs_t.shape[0], max_rows, L, H, D,
+            _lib.COPY_VECTOR,  # plain stores to peer memory; no bulk/TMA path
+            _ops.status_word(device).data_ptr(), st.cuda_stream)
+    _lib.check(code, "augur_kv_copy_runs (peer push)")
+    _ops.launch_count += 1
+    _ops.keep_until_done(st, runs_t)
+    return int(runs[:, 4].sum()) * L * 2 * H * D * sk.element_size()
+
+
+def push_blocks(src: PagedKVCache, src_blocks: Sequence[int], dst: PeerPool, dst_blocks: Sequence[int],
+                n_rows: Sequence[int] | None = None, stream: torch.cuda.Stream | None = None) -> int:
+    """Push whole (or the first n_rows rows of) blocks src_blocks[i] -> dst_blocks[i]."""
+    if len(src_blocks) != len(dst_blocks):
+        raise ValueError("src_blocks and dst_blocks must have the same length")
+    n = len(src_blocks)
+    runs = np.zeros((n, 5), dtype=np.int64)
+    runs[:, 0] = np.asarray(src_blocks, dtype=np.int64)
+    runs[:, 2] = np.asarray(dst_blocks, dtype=np.int64)
+    runs[:, 4] = src.block_size if n_rows is None else np.asarray(n_rows, dtype=np.int64)
+    return push_runs(src, dst, runs, stream=stream)

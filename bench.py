@@ -498,6 +498,199 @@ def run_extras(device, handoff_only: bool = False) -> dict:
 
 
 # ---------------------------------------------------------------------------
+# box scale-out (config 5): 2048 sequences sharded by LPT, strong scaling
+# ---------------------------------------------------------------------------
+
+
+def run_box(args, world: int, rank: int, local: int) -> dict | None:
+    """Each rank: prefill scatter of its LPT shard + 128 decode appends; total work fixed."""
+    import augur_b200 as ab
+    from augur_b200 import _lib, _ops, batched, sharding
+
+    device = torch.device("cuda", local)
+    lens_all = sharding.box_lengths(n_seqs=args.box_seqs)
+    mine = sharding.lpt_assign(lens_all, world)[rank]
+    lens = lens_all[mine]
+    appends = 128
+    nblk = int(sum(-(-(int(n) + appends) // BS) for n in lens))
+    pool = ab.PagedKVCache(keys=torch.empty(L, nblk, H, BS, D, dtype=torch.bfloat16, device=device),
+                           values=torch.empty(L, nblk, H, BS, D, dtype=torch.bfloat16, device=device),
+                           block_size=BS, allocator=ab.BlockAllocator(nblk))
+    T = int(lens.sum())
+    # per-sequence seeds: sequence i carries the same K/V whatever the number of ranks
+    k = torch.empty(L, T, H, D, dtype=torch.bfloat16, device=device)
+    v = torch.empty_like(k)
+    g = torch.Generator(device=device)
+    pos = 0
+    for i, n in zip(mine, lens):
+        g.manual_seed(50_000 + int(i))
+        k[:, pos : pos + n].copy_(torch.randn(L, int(n), H, D, generator=g, device=device))
+        v[:, pos : pos + n].copy_(torch.randn(L, int(n), H, D, generator=g, device=device))
+        pos += int(n)
+    tables = [ab.SequenceBlockTable.empty(BS) for _ in lens]
+    sm = batched.prefill_slot_mapping(tables, lens, pool.allocator)
+    flat = torch.from_numpy(np.concatenate([sm[b, :n] for b, n in enumerate(lens)])).to(device)
+    dec_slots = torch.from_numpy(np.stack([batched.decode_slot_mapping(tables, pool.allocator)
+                                           for _ in range(appends)])).to(device)
+    nk = torch.randn(appends, L, len(lens), H, D, device=device).to(torch.bfloat16)
+
+    def step() -> None:
+        batched.write_paged_kv_batch(pool, k, v, flat)
+        for s in range(appends):
+            batched.append_decode(pool, None, nk[s], nk[s], slot_mapping=dec_slots[s])
+
+    for _ in range(max(1, args.warmup)):
+        step()
+    torch.cuda.synchronize(device)
+    barrier(world, device)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = _ops.launch_count
+    with ClockSampler(local) as clocks:
+        a.record()
+        for _ in range(args.steps):
+            step()
+        b.record()
+        torch.cuda.synchronize(device)
+    ms = a.elapsed_time(b)
+    launches = _ops.launch_count - launches0
+    if _ops.read_status(device) != _lib.OK:
+        raise RuntimeError("device status error in the box workload")
+    barrier(world, device)
+    ms_max = max_over_ranks(ms, world, device)
+    total_tokens = int(lens_all.sum())
+    step_bytes_total = scatter_bytes(total_tokens) + appends * scatter_bytes(args.box_seqs)
+    if rank != 0:
+        return None
+    peak, peak_kind = load_peaks()
+    per_gpu = step_bytes_total / world / (ms_max / args.steps / 1e3) / 1e9
+    return {
+        "metric": "KV prefill scatter + 128 decode appends GB/s (box scale-out)",
+        "value": round(step_bytes_total * args.steps / (ms_max / 1e3) / 1e9, 2), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (per-sequence seeds)",
+        "config": {"workload": f"{args.box_seqs} seqs, lognormal(ln 1024, 0.8) clipped [64, 8192], "
+                               f"{total_tokens} tokens, LPT-sharded over {world} GPUs; step = prefill "
+                               "scatter of every shard + 128 decode appends",
+                   "bytes_per_step": step_bytes_total, "tokens_rank0": T, "seqs_rank0": len(lens),
+                   "l2": "inputs larger than L2"},
+        "gpu_launches": launches, "clocks": clocks.summary(),
+        "roofline": {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s per GPU",
+                     "frac": round(per_gpu / peak, 4), "peak_source": f"hbm_gbs of {peak_kind}"},
+    }
+
+
+# ---------------------------------------------------------------------------
+# disaggregated mode: prefill ranks push finished blocks to decode ranks
+# ---------------------------------------------------------------------------
+
+NVLINK_PEER_GBS = 770.0  # measured peer copy per direction on this B200 pool (900 nominal)
+
+
+def run_disagg(args, world: int, rank: int, local: int) -> dict | None:
+    """Ranks [0, N/2) prefill a config-2 batch and push its blocks to rank + N/2 over NVLink."""
+    import torch.distributed as dist
+
+    import augur_b200 as ab
+    from augur_b200 import _lib, _ops, batched, peer
+
+    if world < 2 or world % 2:
+        raise SystemExit("--workload disagg needs an even number of ranks >= 2")
+    device = torch.device("cuda", local)
+    half = world // 2
+    prefill = rank < half
+    partner = rank + half if prefill else rank - half
+    nblocks = 8192
+    pool = ab.PagedKVCache(keys=torch.empty(L, nblocks, H, BS, D, dtype=torch.bfloat16, device=device),
+                           values=torch.empty(L, nblocks, H, BS, D, dtype=torch.bfloat16, device=device),
+                           block_size=BS, allocator=ab.BlockAllocator(nblocks))
+    pair_seed = 7000 + min(rank, partner)
+    lens = config2_lengths(pair_seed)
+    # decode side: destination tables from its own allocator; exported with the pool
+    objs: list = [None] * world
+    mine = None
+    if not prefill:
+        pool.allocator.allocate_many(17)  # the decode pool already serves other sequences
+        dst_tables = [ab.SequenceBlockTable.empty(BS) for _ in lens]
+        batched.prefill_slot_mapping(dst_tables, lens, pool.allocator)
+        mine = (peer.export_pool(pool), [t.block_ids for t in dst_tables])
+    dist.all_gather_object(objs, mine)
+    n_sets = 4
+    if prefill:
+        exported, dst_ids = objs[partner]
+        remote = peer.open_pool(exported, device)
+        runs_sets, offset = [], 0
+        for s in range(n_sets):
+            _, slots, k, v, used = config2_batch(seed=pair_seed, block_offset=offset, num_blocks=nblocks)
+            batched.write_paged_kv_batch(pool, k.to(device), v.to(device), torch.from_numpy(slots).to(device))
+            runs, pos = [], 0
+            for n, ids in zip(lens, dst_ids):
+                for j in range(-(-int(n) // BS)):
+                    rows = min(BS, int(n) - j * BS)
+                    runs.append((int(slots[pos + j * BS]) // BS, 0, ids[j], 0, rows))
+                pos += int(n)
+            runs_sets.append(np.asarray(runs, dtype=np.int64))
+            offset += used
+        payload = int(lens.sum()) * TOKEN_BYTES
+        for i in range(max(3, args.warmup)):
+            peer.push_runs(pool, remote, runs_sets[i % n_sets])
+        torch.cuda.synchronize(device)
+    barrier(world, device)
+    ms = 0.0
+    if prefill:
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for i in range(args.steps):
+            peer.push_runs(pool, remote, runs_sets[i % n_sets])
+        b.record()
+        torch.cuda.synchronize(device)
+        ms = a.elapsed_time(b)
+        if _ops.read_status(device) != _lib.OK:
+            raise RuntimeError("device status error during the push")
+    barrier(world, device)
+    ms_max = max_over_ranks(ms, world, device)
+    # decode side: the pushed blocks must equal a local write of the pair's batch
+    # (the rotating source sets hold the same seeded K/V in different blocks)
+    ok = 1.0
+    if not prefill:
+        _, _, k, v, _ = config2_batch(seed=pair_seed, block_offset=0, num_blocks=nblocks)
+        ref = ab.PagedKVCache(keys=torch.zeros_like(pool.keys), values=torch.zeros_like(pool.values),
+                              block_size=BS, allocator=ab.BlockAllocator(nblocks))
+        tables = [ab.SequenceBlockTable(block_ids=list(ids), block_size=BS, seq_len=int(n))
+                  for ids, n in zip(mine[1], lens)]
+        pos = [np.arange(int(n)) for n in lens]
+        flat = np.concatenate([np.asarray(t.block_ids)[p // BS] * BS + p % BS for t, p in zip(tables, pos)])
+        batched.write_paged_kv_batch(ref, k.to(device), v.to(device), torch.from_numpy(flat).to(device))
+        gk, gv = batched.read_paged_kv_batch(pool, tables)
+        rk, rv = batched.read_paged_kv_batch(ref, tables)
+        ok = float(torch.equal(gk.view(torch.int16), rk.view(torch.int16)) and
+                   torch.equal(gv.view(torch.int16), rv.view(torch.int16)))
+        del ref
+    t = torch.tensor([ok], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    barrier(world, device)
+    if prefill:
+        remote.close()
+    barrier(world, device)
+    if rank != 0:
+        return None
+    per_pair = payload * args.steps / (ms_max / 1e3) / 1e9
+    return {
+        "metric": "KV block push GB/s over NVLink (disaggregated prefill -> decode)",
+        "value": round(per_pair * half, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{half} prefill->decode pairs, each pushing a config-2 batch "
+                               "(8192 tokens x 24 layers, whole 16-token blocks) per step",
+                   "payload_bytes_per_pair_step": payload, "bit_exact_on_decode": bool(t.item() == 1.0),
+                   "l2": "4 rotating source batches per prefill rank"},
+        "roofline": {"bound": "nvlink", "achieved": round(per_pair, 1), "peak": NVLINK_PEER_GBS,
+                     "unit": "GB/s per direction per GPU", "frac": round(per_pair / NVLINK_PEER_GBS, 4),
+                     "peak_source": "measured peer copy on this pool (900 nominal)"},
+    }
+
+
+# ---------------------------------------------------------------------------
 # reference arm
 # ---------------------------------------------------------------------------
 
@@ -534,7 +727,22 @@ def run_reference(args, world: int, rank: int) -> dict | None:
     }
 
 
+def _json_stdout():
+    """Keep stdout for the one JSON line: everything else written to fd 1
+    (library banners such as NCCL's version line included) goes to stderr."""
+    sys.stdout.flush()
+    out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+    return out
+
+
 def main() -> None:
+    json_out = _json_stdout()
+
+    def emit(line: dict) -> None:
+        json_out.write(json.dumps(line) + "\n")
+        json_out.flush()
+
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
@@ -545,6 +753,10 @@ def main() -> None:
     ap.add_argument("--skip-extras", action="store_true")
     ap.add_argument("--small", action="store_true", help="profiling case: 8192-block pool, no extras/CPU")
     ap.add_argument("--handoff-only", action="store_true", help="profiling case: config-3 handoff only")
+    ap.add_argument("--workload", choices=["scatter", "disagg", "box"], default="scatter",
+                    help="scatter: headline (config 2); disagg: NVLink block push between rank pairs; "
+                         "box: config 5, 2048 sequences sharded over the ranks (strong scaling)")
+    ap.add_argument("--box-seqs", type=int, default=2048)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -552,13 +764,13 @@ def main() -> None:
         args.skip_cpu = args.skip_extras = True
     if args.handoff_only:  # profiling case: only the config-3 handoff (about 3 GB on the device)
         torch.cuda.set_device(0)
-        print(json.dumps(run_extras(torch.device("cuda", 0), handoff_only=True)), flush=True)
+        emit(run_extras(torch.device("cuda", 0), handoff_only=True))
         return
     world, rank, local = dist_env()
     if args.impl == "reference":
         line = run_reference(args, world, rank)
         if line is not None:
-            print(json.dumps(line), flush=True)
+            emit(line)
         return
     if world > 1:
         import datetime
@@ -569,9 +781,14 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     try:
-        line = run_ours(args, world, rank, local)
+        if args.workload == "disagg":
+            line = run_disagg(args, world, rank, local)
+        elif args.workload == "box":
+            line = run_box(args, world, rank, local)
+        else:
+            line = run_ours(args, world, rank, local)
         if line is not None:
-            print(json.dumps(line), flush=True)
+            emit(line)
     finally:
         if world > 1:
             import torch.distributed as dist

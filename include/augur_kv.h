@@ -127,6 +127,27 @@ int augur_kv_copy_runs(const void* src_k, const void* src_v,
                        int32_t flags, int32_t* status, void* stream);
 
 /*
+ * Peer memory for the disaggregated mode: a decode GPU's process exports its
+ * block pool, a prefill GPU's process opens it and pushes finished blocks into
+ * it with augur_kv_copy_runs (vector path: plain 16-byte stores over NVLink).
+ * No reference counterpart (augur runs in one process on one device).
+ *
+ * augur_kv_ipc_export: handle (AUGUR_KV_IPC_HANDLE_BYTES bytes) of the device
+ *   allocation containing dev_ptr, and dev_ptr's byte offset inside it.
+ * augur_kv_ipc_open: map an exported allocation into the CURRENT device's
+ *   address space (peer access is enabled as needed) and return the address
+ *   that corresponds to `offset`. A process may not open its own allocation.
+ * augur_kv_ipc_close: unmap what augur_kv_ipc_open returned (same offset).
+ * The exporting process must keep the allocation alive until every importer
+ * has closed it.
+ */
+#define AUGUR_KV_IPC_HANDLE_BYTES 64
+
+int augur_kv_ipc_export(const void* dev_ptr, void* handle_out, int64_t* offset_out);
+int augur_kv_ipc_open(const void* handle, int64_t offset, void** dev_ptr_out);
+int augur_kv_ipc_close(void* dev_ptr, int64_t offset);
+
+/*
  * augur_kv_copy_runs_noalloc — augur_kv_copy_runs for callers that cannot
  * allocate device memory. No counterpart in the reference (augur allocates
  * through torch).
