@@ -181,6 +181,24 @@ __device__ __forceinline__ void store_vec(char* p, typename VecType<VEC>::T v) {
   *reinterpret_cast<typename VecType<VEC>::T*>(p) = v;
 }
 
+#ifndef AUGUR_KV_STORE_HINT
+#define AUGUR_KV_STORE_HINT 1  // 1: cache-streaming (.cs, evict-first) 16-byte stores in the scatter
+#endif
+
+template <int VEC>
+__device__ __forceinline__ void store_stream(char* p, typename VecType<VEC>::T v) {
+  store_vec<VEC>(p, v);
+}
+template <>
+__device__ __forceinline__ void store_stream<16>(char* p, uint4 v) {
+#if AUGUR_KV_STORE_HINT == 1
+  asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+#else
+  store_vec<16>(p, v);
+#endif
+}
+
 // Element conversion for mixed-dtype moves: through fp32, round to nearest even.
 __device__ __forceinline__ float load_as_float(const char* p, int dtype) {
   if (dtype == AUGUR_KV_F32) return *reinterpret_cast<const float*>(p);
@@ -340,8 +358,12 @@ __global__ void __launch_bounds__(256) scatter_vec_kernel(ScatterArgs a) {
 #define AUGUR_KV_SCATTER_WAVES 2  // grid = resident CTAs x this, warps stride over items
 #endif
 
+#ifndef AUGUR_KV_SCATTER_MIN_CTAS
+#define AUGUR_KV_SCATTER_MIN_CTAS 1  // __launch_bounds__ minimum resident CTAs per SM
+#endif
+
 template <int VEC, int UPT, int LU>
-__global__ void __launch_bounds__(256) scatter_rows_kernel(ScatterArgs a, uint32_t n_token_groups,
+__global__ void __launch_bounds__(256, AUGUR_KV_SCATTER_MIN_CTAS) scatter_rows_kernel(ScatterArgs a, uint32_t n_token_groups,
                                                            uint32_t n_items, int32_t n_layers) {
   using T = typename VecType<VEC>::T;
   constexpr int LANES = UPT < 32 ? UPT : 32;  // lanes per token
@@ -394,7 +416,7 @@ __global__ void __launch_bounds__(256) scatter_rows_kernel(ScatterArgs a, uint32
     for (int k = 0; k < LU; ++k) {
       if (k < nl) {
 #pragma unroll
-        for (int i = 0; i < UPL; ++i) store_vec<VEC>(db[i] + int64_t(l0 + k) * d_layer + dbase, val[k][i]);
+        for (int i = 0; i < UPL; ++i) store_stream<VEC>(db[i] + int64_t(l0 + k) * d_layer + dbase, val[k][i]);
       }
     }
   }
@@ -562,6 +584,10 @@ constexpr int kBulkWarps = 4;
 constexpr int kBulkBarBytes = 128 * ((kBulkWarps * kBulkMaxStages * 8 + 127) / 128);
 constexpr int kBulkSmemBudget = 200 * 1024;      // per CTA, of the 227 KB limit
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // bound on one mbarrier wait
+#ifndef AUGUR_KV_BULK_LAG
+#define AUGUR_KV_BULK_LAG 4  // stores allowed in flight behind the one just issued
+#endif
+constexpr int kBulkLag = AUGUR_KV_BULK_LAG;
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -737,18 +763,20 @@ __global__ void __launch_bounds__(kBulkWarps * 32) copy_runs_bulk_kernel(RunArgs
       if (bytes != 0) bulk_store(dst, buf + size_t(s) * a.stage_bytes, bytes);
       bulk_commit();
     }
-    if (c >= 1 && c - 1 + S < n) {
-      if (lane == 0) bulk_wait_read<1>();
-      issue_load(c - 1 + S);
+    // Refill the stage of item c - kBulkLag once its store has finished
+    // reading shared memory (all but the kBulkLag newest bulk groups).
+    if (c >= uint32_t(kBulkLag) && c - kBulkLag + S < n) {
+      if (lane == 0) bulk_wait_read<kBulkLag>();
+      issue_load(c - kBulkLag + S);
     }
   }
   if (lane == 0) {
     if (c < n) {
       record_status(a.status, AUGUR_KV_ETIMEOUT);
-      // Loads issued so far: items [0, prologue) and the refills c' - 1 + S
-      // for 1 <= c' < c. Wait (bounded) for the ones not yet consumed before
+      // Loads issued so far: items [0, prologue) and the refills c' - lag + S
+      // for lag <= c' < c. Wait (bounded) for the ones not yet consumed before
       // this CTA's shared memory can be released.
-      uint32_t issued_end = (c == 0) ? prologue : c + S - 1;
+      uint32_t issued_end = (c <= uint32_t(kBulkLag)) ? prologue : c - kBulkLag + S;
       if (issued_end > n) issued_end = n;
       for (uint32_t d = c + 1; d < issued_end; ++d) mbar_wait(&bars[d % S], (d / S) & 1u);
     }
@@ -1019,7 +1047,7 @@ AUGUR_KV_EXPORT int augur_kv_copy_runs(const void* src_k, const void* src_v, con
     a.stage_bytes = int32_t(((int64_t(max_rows) * row_bytes + 127) / 128) * 128);
     int stages = (kBulkSmemBudget - kBulkBarBytes) / (kBulkWarps * a.stage_bytes);
     if (stages > kBulkMaxStages) stages = kBulkMaxStages;
-    if (stages < 2) stages = 2;
+    if (stages < kBulkLag + 1) stages = kBulkLag + 1;
     a.stages = stages;
     const int smem = kBulkBarBytes + kBulkWarps * stages * a.stage_bytes;
     static int attr_bytes[kMaxDevices] = {0};
