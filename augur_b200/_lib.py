@@ -8,6 +8,7 @@ movement call raises KVLibraryError. Build it with
 from __future__ import annotations
 
 import ctypes
+import functools
 import os
 import threading
 
@@ -47,7 +48,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "augur_kv_scatter": (
         ctypes.c_int,
         [_P, _P, _I64P, _I64P, _I64, _I32, _P, _P, _I64P, _I64, _I64, _I32, _P, _I64P, _I64,
-         _I64, _I32, _I32, _I32, _P, _P],
+         _I32, _I64, _I32, _I32, _I32, _P, _P],
     ),
     "augur_kv_copy_runs": (
         ctypes.c_int,
@@ -65,6 +66,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
 }
 
 NOALLOC_MAX_RUNS = 65536
+INLINE_INDEX_MAX = 32
 IPC_HANDLE_BYTES = 64
 
 
@@ -106,9 +108,16 @@ def load() -> ctypes.CDLL:
         return lib
 
 
-def i64_array(values) -> ctypes.Array:
-    vals = [int(v) for v in values]
+@functools.lru_cache(maxsize=4096)
+def _i64_array_cached(vals: tuple) -> ctypes.Array:
     return (ctypes.c_int64 * len(vals))(*vals)
+
+
+def i64_array(values) -> ctypes.Array:
+    """A C int64 array of `values`; identical tuples share one (read-only) array."""
+    if type(values) is not tuple:
+        values = tuple(int(v) for v in values)
+    return _i64_array_cached(values)
 
 
 def check(code: int, what: str) -> None:

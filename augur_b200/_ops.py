@@ -10,6 +10,7 @@ from __future__ import annotations
 
 from collections.abc import Sequence
 
+import numpy as np
 import torch
 from torch import Tensor
 
@@ -122,7 +123,7 @@ def scatter(
     dst_strides: Sequence[int],
     rows_per_major: int,
     num_majors: int,
-    index: Tensor,
+    index: Tensor | np.ndarray,
     index_strides: Sequence[int],
     index_row_base: int,
     n_tokens: int,
@@ -131,11 +132,21 @@ def scatter(
     head_dim: int,
     stream: torch.cuda.Stream | None = None,
 ) -> None:
-    """Launch augur_kv_scatter. Strides are element strides as the header documents."""
+    """Launch augur_kv_scatter. Strides are element strides as the header documents.
+
+    `index` is an int64 CUDA tensor, or an int64 numpy array in host memory
+    holding at most INLINE_INDEX_MAX tokens' values (passed to the kernel by
+    value; src and dst dtypes must then match).
+    """
     global launch_count
-    require_cuda("KV scatter", src_k, src_v, dst_k, dst_v, index)
-    if index.dtype != torch.int64:
+    on_host = isinstance(index, np.ndarray)
+    require_cuda("KV scatter", src_k, src_v, dst_k, dst_v, None if on_host else index)
+    if index.dtype != (np.int64 if on_host else torch.int64):
         raise ValueError("scatter index must be int64")
+    if on_host:
+        index_ptr = index.ctypes.data
+    else:
+        index_ptr = index.data_ptr()
     lib = _lib.load()
     device = dst_k.device
     st = stream if stream is not None else torch.cuda.current_stream(device)
@@ -153,9 +164,10 @@ def scatter(
             int(rows_per_major),
             int(num_majors),
             dtype_code(dst_k),
-            _ptr(index),
+            index_ptr,
             _lib.i64_array(index_strides),
             int(index_row_base),
+            1 if on_host else 0,
             int(n_tokens),
             int(n_layers),
             int(n_heads),
@@ -166,7 +178,7 @@ def scatter(
     _lib.check(code, "augur_kv_scatter")
     if n_tokens > 0 and n_layers > 0:
         launch_count += 1
-        keep_until_done(st, index, src_k, src_v)
+        keep_until_done(st, None if on_host else index, src_k, src_v)
 
 
 def copy_runs(
@@ -225,6 +237,11 @@ def copy_runs(
     if runs.shape[0] > 0 and n_layers > 0:
         launch_count += 1
         keep_until_done(st, runs, src_k, src_v)
+
+
+def host_index_ok(n_tokens: int, src: Tensor, dst: Tensor) -> bool:
+    """Whether a scatter of n_tokens can take its index by value from host memory."""
+    return 0 < n_tokens <= _lib.INLINE_INDEX_MAX and src.dtype == dst.dtype
 
 
 def max_rows_for(head_dim: int, elem_size: int, cap_rows: int = 64, cap_bytes: int = 8192) -> int:

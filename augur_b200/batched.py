@@ -59,7 +59,7 @@ def write_paged_kv_batch(
     cache: PagedKVCache,
     key: Tensor,
     value: Tensor,
-    slot_mapping: Tensor,
+    slot_mapping: Tensor | np.ndarray,
     layer_idx: int | None = None,
     stream: torch.cuda.Stream | None = None,
 ) -> None:
@@ -68,11 +68,13 @@ def write_paged_kv_batch(
     key/value: ``[layers, tokens, kv_heads, head_dim]`` with layer_idx None
     (all cache layers in one launch), or ``[tokens, kv_heads, head_dim]`` for
     one layer. slot_mapping: int64 ``[tokens]`` on the cache's device,
-    slot = block_id * block_size + offset.
+    slot = block_id * block_size + offset; a host numpy array of at most 32
+    slots is passed to the kernel by value (larger ones are copied over).
     """
     if key.shape != value.shape:
         raise ValueError("key and value must have the same shape")
-    _ops.require_cuda("write_paged_kv_batch", cache.keys, cache.values, key, value, slot_mapping)
+    _ops.require_cuda("write_paged_kv_batch", cache.keys, cache.values, key, value,
+                      None if isinstance(slot_mapping, np.ndarray) else slot_mapping)
     pool_k, pool_v = cache.keys, cache.values
     if layer_idx is None:
         if key.dim() != 4 or key.shape[0] != pool_k.shape[0]:
@@ -93,9 +95,13 @@ def write_paged_kv_batch(
     _, n_tokens, num_heads, head_dim = key.shape
     if (num_heads, head_dim) != (pool_k.shape[2], pool_k.shape[4]):
         raise ValueError("key/value shape does not match cache shape")
-    if slot_mapping.shape != (n_tokens,):
+    if tuple(slot_mapping.shape) != (n_tokens,):
         raise ValueError("slot_mapping must have shape [tokens]")
-    if slot_mapping.dtype != torch.int64:
+    if isinstance(slot_mapping, np.ndarray):
+        slot_mapping = np.ascontiguousarray(slot_mapping, dtype=np.int64)
+        if not (_ops.host_index_ok(n_tokens, key, pool_k) and value.dtype == key.dtype):
+            slot_mapping = _to_device_i64(slot_mapping, pool_k.device)
+    elif slot_mapping.dtype != torch.int64:
         slot_mapping = slot_mapping.to(torch.int64)
     for sk, sv, dk, dv in _kv_pairs(key, value, pool_k, pool_v):
         _ops.scatter(
@@ -103,8 +109,8 @@ def write_paged_kv_batch(
             tokens_per_row=max(1, n_tokens),
             dst_k=dk, dst_v=dv, dst_strides=pool_strides(dk, dst_layer_view),
             rows_per_major=cache.block_size, num_majors=dk.shape[1],
-            index=slot_mapping, index_strides=(0, slot_mapping.stride(0)), index_row_base=0,
-            n_tokens=n_tokens, n_layers=n_layers, n_heads=num_heads, head_dim=head_dim,
+            index=slot_mapping, index_strides=(0, 1 if isinstance(slot_mapping, np.ndarray) else slot_mapping.stride(0)),
+            index_row_base=0, n_tokens=n_tokens, n_layers=n_layers, n_heads=num_heads, head_dim=head_dim,
             stream=stream,
         )
 
@@ -206,7 +212,11 @@ def append_decode(
     if slot_mapping is None:
         if tables is None:
             raise ValueError("append_decode needs tables or a slot_mapping")
-        slot_mapping = _to_device_i64(decode_slot_mapping(tables, cache.allocator), cache.keys.device)
+        slots = decode_slot_mapping(tables, cache.allocator)
+        if _ops.host_index_ok(len(slots), key, cache.keys) and key.dtype == value.dtype:
+            slot_mapping = slots  # few sequences: slots go to the kernel by value
+        else:
+            slot_mapping = _to_device_i64(slots, cache.keys.device)
     write_paged_kv_batch(cache, key, value, slot_mapping, stream=stream)
     return slot_mapping
 

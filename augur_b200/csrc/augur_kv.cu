@@ -35,7 +35,7 @@
 
 #include "augur_kv.h"
 
-#define AUGUR_KV_VERSION ((0 << 16) | 3)
+#define AUGUR_KV_VERSION ((0 << 16) | 4)
 
 namespace augur_kv_dev {
 
@@ -255,20 +255,23 @@ struct ScatterArgs {
   int32_t* status;
 };
 
-// Resolve token t of this launch to (source row, source col, destination
-// major, destination row). Returns false for a skipped (negative index) or
-// out-of-range token; out-of-range records EBOUNDS.
-__device__ __forceinline__ bool scatter_resolve(const ScatterArgs& a, uint32_t t, int64_t& row,
-                                                int64_t& col, int64_t& major, int64_t& off) {
+// Source (row, col) of token t of this launch.
+__device__ __forceinline__ void scatter_rowcol(const ScatterArgs& a, uint32_t t, int64_t& row, int64_t& col) {
   if (a.tokens_per_row == a.n_tokens) {
     row = 0;
     col = t;
   } else {
-    uint32_t r = t / a.tokens_per_row;
+    const uint32_t r = t / a.tokens_per_row;
     row = r;
     col = t - r * a.tokens_per_row;
   }
-  const int64_t idx = __ldg(a.index + row * a.index_stride[0] + col * a.index_stride[1]);
+}
+
+// Destination (major, row) of index value idx for a token of source row
+// `row`. Returns false for a skipped (negative) or out-of-range index;
+// out-of-range records EBOUNDS.
+__device__ __forceinline__ bool scatter_slot(const ScatterArgs& a, int64_t row, int64_t idx, int64_t& major,
+                                             int64_t& off) {
   if (idx < 0) return false;
   if (a.index_row_base > 0) {
     // contiguous cache: the index is a position inside batch row `row`
@@ -296,6 +299,15 @@ __device__ __forceinline__ bool scatter_resolve(const ScatterArgs& a, uint32_t t
     }
   }
   return true;
+}
+
+// Resolve token t through the device index array to (source row, source col,
+// destination major, destination row).
+__device__ __forceinline__ bool scatter_resolve(const ScatterArgs& a, uint32_t t, int64_t& row,
+                                                int64_t& col, int64_t& major, int64_t& off) {
+  scatter_rowcol(a, t, row, col);
+  const int64_t idx = __ldg(a.index + row * a.index_stride[0] + col * a.index_stride[1]);
+  return scatter_slot(a, row, idx, major, off);
 }
 
 // Same-dtype scatter: each thread moves ITEMS vectors of VEC bytes; a warp
@@ -419,6 +431,43 @@ __global__ void __launch_bounds__(256, AUGUR_KV_SCATTER_MIN_CTAS) scatter_rows_k
         for (int i = 0; i < UPL; ++i) store_stream<VEC>(db[i] + int64_t(l0 + k) * d_layer + dbase, val[k][i]);
       }
     }
+  }
+}
+
+// Small scatters whose index arrives by value in the kernel parameters (the
+// host passes up to AUGUR_KV_INLINE_INDEX_MAX index values; a decode-step
+// write of one or a few tokens needs no device index buffer or copy). One
+// thread per 16-byte (or narrower) unit of a token-layer, layers on
+// blockIdx.y.
+struct InlineIndex {
+  int64_t v[AUGUR_KV_INLINE_INDEX_MAX];
+};
+
+template <int VEC>
+__global__ void __launch_bounds__(256) scatter_inline_kernel(ScatterArgs a, InlineIndex ix) {
+  using T = typename VecType<VEC>::T;
+  const int64_t layer = blockIdx.y;
+  const uint32_t total = a.n_tokens * uint32_t(a.upt);
+  for (uint32_t i = blockIdx.x * 256u + threadIdx.x; i < total; i += gridDim.x * 256u) {
+    const uint32_t t = i / uint32_t(a.upt);
+    const uint32_t j = i - t * uint32_t(a.upt);
+    const uint32_t r = j / uint32_t(a.vpr);
+    const uint32_t v = j - r * uint32_t(a.vpr);
+    const uint32_t kv = r / uint32_t(a.n_heads);
+    const uint32_t h = r - kv * uint32_t(a.n_heads);
+    int64_t idx = -1;
+#pragma unroll
+    for (int q = 0; q < AUGUR_KV_INLINE_INDEX_MAX; ++q)
+      if (uint32_t(q) == t) idx = ix.v[q];
+    int64_t row, col, major, off;
+    scatter_rowcol(a, t, row, col);
+    if (!scatter_slot(a, row, idx, major, off)) continue;
+    const int64_t* ss = a.src_stride[kv];
+    const char* src = a.src[kv] + layer * ss[0] + row * ss[1] + col * ss[2] + int64_t(h) * ss[3] +
+                      int64_t(v) * VEC;
+    char* dst = a.dst[kv] + layer * a.dst_stride[0] + major * a.dst_stride[1] + off * a.dst_stride[2] +
+                int64_t(h) * a.dst_stride[3] + int64_t(v) * VEC;
+    store_vec<VEC>(dst, *reinterpret_cast<const T*>(src));
   }
 }
 
@@ -804,8 +853,8 @@ AUGUR_KV_EXPORT int augur_kv_scatter(const void* src_k, const void* src_v, const
                                 const int64_t* dst_strides, int64_t rows_per_major,
                                 int64_t num_majors, int32_t dst_dtype, const int64_t* index,
                                 const int64_t* index_strides, int64_t index_row_base,
-                                int64_t n_tokens, int32_t n_layers, int32_t n_heads,
-                                int32_t head_dim, int32_t* status, void* stream) {
+                                int32_t index_on_host, int64_t n_tokens, int32_t n_layers,
+                                int32_t n_heads, int32_t head_dim, int32_t* status, void* stream) {
   g_last_error[0] = '\0';
   const int es = elem_size(src_dtype), ed = elem_size(dst_dtype);
   if (es == 0 || ed == 0) return fail(AUGUR_KV_EINVAL, "scatter: unknown dtype %d/%d", src_dtype, dst_dtype);
@@ -827,6 +876,9 @@ AUGUR_KV_EXPORT int augur_kv_scatter(const void* src_k, const void* src_v, const
   if (tokens_per_row > n_tokens) tokens_per_row = n_tokens;
   if (n_tokens % tokens_per_row != 0)
     return fail(AUGUR_KV_EINVAL, "scatter: n_tokens must be a multiple of tokens_per_row");
+  if (index_on_host != 0 && (n_tokens > AUGUR_KV_INLINE_INDEX_MAX || src_dtype != dst_dtype))
+    return fail(AUGUR_KV_EINVAL, "scatter: a host index needs at most %d tokens and equal dtypes",
+                AUGUR_KV_INLINE_INDEX_MAX);
 
   const int n_kv = (src_v != nullptr) ? 2 : 1;
   ScatterArgs a;
@@ -884,6 +936,25 @@ AUGUR_KV_EXPORT int augur_kv_scatter(const void* src_k, const void* src_v, const
   a.upt = n_kv * n_heads * a.vpr;
   const uint64_t total = uint64_t(n_tokens) * uint64_t(a.upt);
   if (total > 0x7FFFFFFFull) return fail(AUGUR_KV_EINVAL, "scatter: too many vectors per layer");
+
+  if (index_on_host != 0) {
+    InlineIndex ix;
+    for (int q = 0; q < AUGUR_KV_INLINE_INDEX_MAX; ++q) ix.v[q] = -1;
+    for (int64_t t = 0; t < n_tokens; ++t) {
+      const int64_t row = t / tokens_per_row, col = t % tokens_per_row;
+      ix.v[t] = index[row * index_strides[0] + col * index_strides[1]];
+    }
+    const unsigned blocks = unsigned((total + 255) / 256);
+    const dim3 grid{blocks, unsigned(n_layers), 1u};
+    switch (vec) {
+      case 16: scatter_inline_kernel<16><<<grid, 256, 0, st>>>(a, ix); break;
+      case 8: scatter_inline_kernel<8><<<grid, 256, 0, st>>>(a, ix); break;
+      case 4: scatter_inline_kernel<4><<<grid, 256, 0, st>>>(a, ix); break;
+      case 2: scatter_inline_kernel<2><<<grid, 256, 0, st>>>(a, ix); break;
+      default: scatter_inline_kernel<1><<<grid, 256, 0, st>>>(a, ix); break;
+    }
+    return check_launch("scatter_inline_kernel");
+  }
   a.sh_upt = pow2_shift(a.upt);
   a.sh_vpr = pow2_shift(a.vpr);
   a.sh_heads = pow2_shift(n_heads);

@@ -12,6 +12,7 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 from torch import Tensor
 
@@ -158,9 +159,15 @@ def scatter_rows(
     No validation beyond what the kernel bounds-checks; write_kv validates first.
     """
     device = cache.keys.device
-    positions = position_ids
-    if positions.device != device or positions.dtype != torch.int64:
-        positions = positions.to(device=device, dtype=torch.int64)
+    if position_ids.device.type == "cpu" and _ops.host_index_ok(position_ids.numel(), key, cache.keys):
+        # few host positions (a decode step): passed to the kernel by value
+        positions = np.ascontiguousarray(position_ids.numpy(), dtype=np.int64)
+        index_strides = (positions.shape[1], 1)
+    else:
+        positions = position_ids
+        if positions.device != device or positions.dtype != torch.int64:
+            positions = positions.to(device=device, dtype=torch.int64)
+        index_strides = (positions.stride(0), positions.stride(1))
     key = _head_dim_contiguous(key)
     value = _head_dim_contiguous(value)
     batch, num_heads, seq, head_dim = key.shape
@@ -177,7 +184,7 @@ def scatter_rows(
         rows_per_major=cache.max_seq_len,
         num_majors=batch,
         index=positions,
-        index_strides=(positions.stride(0), positions.stride(1)),
+        index_strides=index_strides,
         index_row_base=cache.max_seq_len,
         n_tokens=batch * seq,
         n_layers=1,

@@ -331,8 +331,9 @@ def write_paged_kv(
     if n_ok:
         if block_table.block_size > cache.keys.shape[3]:
             raise IndexError("block table block_size exceeds the cache block size")
-        slots = torch.from_numpy(slots_for_positions(block_table, positions[:n_ok]))
-        slots = slots.to(device=cache.keys.device)
+        slots = slots_for_positions(block_table, positions[:n_ok])
+        if not (_ops.host_index_ok(n_ok, key, cache.keys) and key.dtype == value.dtype):
+            slots = torch.from_numpy(slots).to(device=cache.keys.device)
         scatter_slots_one_layer(cache, layer_idx, key[0], value[0], slots, block_table.block_size)
     if err is not None:
         raise err
@@ -343,12 +344,14 @@ def scatter_slots_one_layer(
     layer_idx: int,
     key: Tensor,
     value: Tensor,
-    slots: Tensor,
+    slots: Tensor | np.ndarray,
     block_size: int | None = None,
 ) -> None:
     """key/value ``[kv_heads, seq, head_dim]``: token t goes to slot slots[t] of one layer.
 
     Only the first len(slots) tokens move. A slot < 0 skips its token.
+    `slots` is an int64 CUDA tensor, or a host int64 array of at most 32
+    slots (passed by value).
     """
     device = cache.keys.device
     # torch's slice assignment in the reference accepts a source on another
@@ -370,7 +373,7 @@ def scatter_slots_one_layer(
         rows_per_major=bs,
         num_majors=kc.shape[0],
         index=slots,
-        index_strides=(0, slots.stride(0)),
+        index_strides=(0, 1 if isinstance(slots, np.ndarray) else slots.stride(0)),
         index_row_base=0,
         n_tokens=n_tokens,
         n_layers=1,

@@ -51,6 +51,9 @@ extern "C" {
 #define AUGUR_KV_COPY_VECTOR 1 /* the 16/8/4/2/1-byte vector path */
 #define AUGUR_KV_COPY_BULK 2   /* the TMA bulk path (EINVAL unless rows are dense and 16-byte aligned) */
 
+/* Largest index passed by value to augur_kv_scatter (index_on_host = 1). */
+#define AUGUR_KV_INLINE_INDEX_MAX 32
+
 /* Library version, (major << 16) | minor. */
 int augur_kv_version(void);
 
@@ -78,6 +81,11 @@ const char* augur_kv_last_error(void);
  * means it holds positions within row `row` (contiguous cache, row = batch).
  * An index >= rows_per_major with index_row_base > 0, or a slot >=
  * num_majors*rows_per_major, is an EBOUNDS error for that token.
+ * index_on_host = 0: `index` is device memory read by the kernel.
+ * index_on_host = 1: `index` is HOST memory; its n_tokens values (at most
+ * AUGUR_KV_INLINE_INDEX_MAX, equal src/dst dtypes) are read during the call
+ * and passed to the kernel by value, so a decode-step write needs no device
+ * index buffer and no host-to-device copy.
  * head_dim elements are contiguous on both sides. src_v / dst_v may be NULL
  * (then only K moves). All strides are in elements of their own tensor.
  */
@@ -88,9 +96,9 @@ int augur_kv_scatter(const void* src_k, const void* src_v,
                      void* dst_k, void* dst_v,
                      const int64_t* dst_strides, /* [4] layer, major, row, head */
                      int64_t rows_per_major, int64_t num_majors, int32_t dst_dtype,
-                     const int64_t* index,         /* device */
+                     const int64_t* index,         /* device, or host with index_on_host */
                      const int64_t* index_strides, /* [2] row, col */
-                     int64_t index_row_base,
+                     int64_t index_row_base, int32_t index_on_host,
                      int64_t n_tokens, int32_t n_layers, int32_t n_heads, int32_t head_dim,
                      int32_t* status, /* device int32 or NULL */
                      void* stream);

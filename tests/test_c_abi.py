@@ -53,15 +53,15 @@ def test_scatter_rejects_bad_arguments_without_touching_the_device():
     lib = _lib.load()
     strides = _i64(0, 0, 1, 1)
     code = lib.augur_kv_scatter(None, None, strides, strides, 1, _lib.BF16, None, None, strides,
-                                16, 1, _lib.BF16, None, _i64(0, 1), 0, 1, 1, 1, 8, None, None)
+                                16, 1, _lib.BF16, None, _i64(0, 1), 0, 0, 1, 1, 1, 8, None, None)
     assert code == _lib.EINVAL
     assert b"null pointer" in lib.augur_kv_last_error()
     fake = ctypes.c_void_p(16)
     code = lib.augur_kv_scatter(fake, None, strides, strides, 1, 7, fake, None, strides,
-                                16, 1, _lib.BF16, fake, _i64(0, 1), 0, 1, 1, 1, 8, None, None)
+                                16, 1, _lib.BF16, fake, _i64(0, 1), 0, 0, 1, 1, 1, 8, None, None)
     assert code == _lib.EINVAL and b"dtype" in lib.augur_kv_last_error()
     code = lib.augur_kv_scatter(fake, None, strides, strides, 1, _lib.BF16, fake, None, strides,
-                                16, 1, _lib.BF16, fake, _i64(0, 1), 3, 1, 1, 1, 8, None, None)
+                                16, 1, _lib.BF16, fake, _i64(0, 1), 3, 0, 1, 1, 1, 8, None, None)
     assert code == _lib.EINVAL and b"index_row_base" in lib.augur_kv_last_error()
 
 
@@ -69,11 +69,24 @@ def test_empty_work_is_ok_with_null_pointers():
     lib = _lib.load()
     s = _i64(0, 0, 1, 1)
     assert lib.augur_kv_scatter(None, None, s, s, 1, _lib.BF16, None, None, s, 16, 1, _lib.BF16,
-                                None, _i64(0, 1), 0, 0, 24, 2, 64, None, None) == _lib.OK
+                                None, _i64(0, 1), 0, 0, 0, 24, 2, 64, None, None) == _lib.OK
     assert lib.augur_kv_copy_runs(None, None, s, 1, 1, _lib.BF16, None, None, s, 1, 1, _lib.BF16,
                                   None, 0, 16, 24, 2, 64, 0, None, None) == _lib.OK
     assert lib.augur_kv_scatter(None, None, s, s, 1, _lib.BF16, None, None, s, 16, 1, _lib.BF16,
-                                None, _i64(0, 1), 0, -1, 24, 2, 64, None, None) == _lib.EINVAL
+                                None, _i64(0, 1), 0, 0, -1, 24, 2, 64, None, None) == _lib.EINVAL
+
+
+def test_host_index_limits():
+    lib = _lib.load()
+    fake = ctypes.c_void_p(16)
+    s = _i64(0, 0, 1, 1)
+    host = _i64(*range(40))
+    code = lib.augur_kv_scatter(fake, None, s, s, 33, _lib.BF16, fake, None, s, 16, 4, _lib.BF16,
+                                host, _i64(0, 1), 0, 1, 33, 1, 1, 64, None, None)
+    assert code == _lib.EINVAL and b"host index" in lib.augur_kv_last_error()
+    code = lib.augur_kv_scatter(fake, None, s, s, 2, _lib.F32, fake, None, s, 16, 4, _lib.BF16,
+                                host, _i64(0, 1), 0, 1, 2, 1, 1, 64, None, None)
+    assert code == _lib.EINVAL and b"equal dtypes" in lib.augur_kv_last_error()
 
 
 def test_copy_runs_rejects_bad_arguments_without_touching_the_device():

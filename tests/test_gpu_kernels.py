@@ -234,7 +234,7 @@ def test_kernel_bounds_check_records_status(cuda):
     code = lib.augur_kv_scatter(
         src.data_ptr(), None, i64(0, 0, H * D, D), None, 3, _lib.BF16,
         pool_k.data_ptr(), None, i64(0, pool_k.stride(1), pool_k.stride(3), pool_k.stride(2)), bs, NB,
-        _lib.BF16, slots.data_ptr(), i64(0, 1), 0, 3, 1, H, D, status.data_ptr(),
+        _lib.BF16, slots.data_ptr(), i64(0, 1), 0, 0, 3, 1, H, D, status.data_ptr(),
         torch.cuda.current_stream().cuda_stream)
     assert code == _lib.OK
     torch.cuda.synchronize()
@@ -288,3 +288,45 @@ def test_handoff_many_runs_per_warp_vs_oracle(cuda, oracle, flags):
     assert_bits_equal(pool.keys, ek, "keys")
     assert_bits_equal(pool.values, ev, "values")
     assert _ops.read_status(cuda) == _lib.OK
+
+
+@pytest.mark.parametrize("dtype, H, D", [(torch.bfloat16, 2, 64), (torch.float32, 2, 64), (torch.float16, 3, 2)])
+def test_host_index_path_matches_device_path(cuda, dtype, H, D):
+    """Up to 32 slots/positions passed by value equal the same scatter through a device index."""
+    g = torch.Generator().manual_seed(21)
+    rng = np.random.default_rng(21)
+    L, NB, bs = 4, 16, 8
+    for n in (1, 7, 32):
+        slots = rng.permutation(NB * bs)[:n].astype(np.int64)
+        slots[n // 2] = -1  # one skipped token
+        k = _rand((L, n, H, D), dtype, g).to(cuda)
+        v = _rand((L, n, H, D), dtype, g).to(cuda)
+        a, b = _pool(L, NB, H, bs, D, dtype, cuda), _pool(L, NB, H, bs, D, dtype, cuda)
+        batched.write_paged_kv_batch(a, k, v, slots)  # host index, by value
+        batched.write_paged_kv_batch(b, k, v, torch.from_numpy(slots).to(cuda))
+        assert_bits_equal(a.keys, b.keys, f"keys n={n}")
+        assert_bits_equal(a.values, b.values, f"values n={n}")
+    # contiguous cache through write_kv with host positions (by value) vs device positions
+    cfg = ab.QwenConfig(vocab_size=16, hidden_size=H * D, intermediate_size=16, num_hidden_layers=L,
+                        num_attention_heads=H, num_key_value_heads=H)
+    c1 = ab.new_kv_cache(cfg, batch_size=3, max_seq_len=20, device=cuda, dtype=dtype)
+    c2 = ab.new_kv_cache(cfg, batch_size=3, max_seq_len=20, device=cuda, dtype=dtype)
+    for c in (c1, c2):
+        poison_(c.keys)
+        poison_(c.values)
+    pos = torch.tensor([[4, 9], [0, 19], [7, 3]])
+    kk = _rand((3, H, 2, D), dtype, g).to(cuda)
+    ab.write_kv(c1, 2, pos, kk, kk)
+    ab.write_kv(c2, 2, pos.to(cuda), kk, kk)
+    assert_bits_equal(c1.keys, c2.keys, "write_kv keys")
+    assert _ops.read_status(cuda) == _lib.OK
+
+
+def test_host_index_bounds_check(cuda):
+    """An out-of-range slot passed by value is skipped and reported like a device one."""
+    pool = _pool(1, 4, 2, 4, 64, torch.bfloat16, cuda)
+    k = torch.randn(1, 2, 2, 64, device=cuda).to(torch.bfloat16)
+    batched.write_paged_kv_batch(pool, k, k, np.array([3, 16], dtype=np.int64))
+    assert _ops.read_status(cuda) == _lib.EBOUNDS
+    assert_bits_equal(pool.keys[0, 0, :, 3], k[0, 0], "valid token")
+    assert int((pool.keys.view(torch.int16) == -1).sum()) == pool.keys.numel() - 2 * 64
