@@ -27,6 +27,7 @@ BF16 = 2
 COPY_AUTO = 0
 COPY_VECTOR = 1
 COPY_BULK = 2
+COPY_FENCE_SYSTEM = 4
 
 STATUS_NAMES = {
     OK: "ok",
@@ -63,6 +64,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "augur_kv_ipc_export": (ctypes.c_int, [_P, _P, _I64P]),
     "augur_kv_ipc_open": (ctypes.c_int, [_P, _I64, ctypes.POINTER(ctypes.c_void_p)]),
     "augur_kv_ipc_close": (ctypes.c_int, [_P, _I64]),
+    "augur_kv_signal": (ctypes.c_int, [_P, _I32, _P]),
+    "augur_kv_wait": (ctypes.c_int, [_P, _I32, _I64, _P, _P]),
 }
 
 NOALLOC_MAX_RUNS = 65536

@@ -515,6 +515,7 @@ struct RunArgs {
   int32_t src_dtype, dst_dtype;
   int32_t stage_bytes;    // bulk path: bytes per pipeline stage
   int32_t stages;         // bulk path: pipeline depth per warp
+  int32_t fence_system;   // every thread ends with a system-scope fence (peer destinations)
   int32_t* status;
 };
 
@@ -604,6 +605,10 @@ __global__ void __launch_bounds__(256) copy_runs_vec_kernel(RunArgs a) {
       }
     }
   }
+  // Peer destinations: make this thread's stores visible system-wide before
+  // the kernel counts as complete, so a ready flag written by later work on
+  // the stream cannot overtake them.
+  if (a.fence_system) __threadfence_system();
 }
 
 // Mixed-dtype path: one warp per run of one plane, one element per lane step.
@@ -624,6 +629,7 @@ __global__ void __launch_bounds__(256) copy_runs_convert_kernel(RunArgs a) {
                        a.dst_dtype, f);
     }
   }
+  if (a.fence_system) __threadfence_system();
 }
 
 // --- TMA bulk path ----------------------------------------------------------
@@ -1057,8 +1063,13 @@ AUGUR_KV_EXPORT int augur_kv_copy_runs(const void* src_k, const void* src_v, con
   if (n_runs < 0 || n_layers < 0 || n_heads <= 0 || head_dim <= 0 || max_rows <= 0 ||
       src_majors < 0 || dst_majors < 0 || src_rows_per_major < 0 || dst_rows_per_major < 0)
     return fail(AUGUR_KV_EINVAL, "copy_runs: bad sizes");
-  if (flags < AUGUR_KV_COPY_AUTO || flags > AUGUR_KV_COPY_BULK)
+  if ((flags & ~(3 | AUGUR_KV_COPY_FENCE_SYSTEM)) != 0 || (flags & 3) > AUGUR_KV_COPY_BULK)
     return fail(AUGUR_KV_EINVAL, "copy_runs: unknown flags %d", flags);
+  const bool fence_system = (flags & AUGUR_KV_COPY_FENCE_SYSTEM) != 0;
+  flags &= 3;
+  if (fence_system && flags == AUGUR_KV_COPY_BULK)
+    return fail(AUGUR_KV_EINVAL, "copy_runs: the system fence is for the vector path");
+  if (fence_system) flags = AUGUR_KV_COPY_VECTOR;
   if (int64_t(max_rows) * head_dim * ed > 16384)
     return fail(AUGUR_KV_EINVAL, "copy_runs: max_rows * row bytes exceeds 16384");
   const int n_kv = (src_v != nullptr) ? 2 : 1;
@@ -1089,6 +1100,7 @@ AUGUR_KV_EXPORT int augur_kv_copy_runs(const void* src_k, const void* src_v, con
   a.src_dtype = src_dtype;
   a.dst_dtype = dst_dtype;
   a.status = status;
+  a.fence_system = fence_system ? 1 : 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int sms = sm_count();
 
@@ -1233,6 +1245,57 @@ AUGUR_KV_EXPORT int augur_kv_ipc_close(void* dev_ptr, int64_t offset) {
   const cudaError_t e = cudaIpcCloseMemHandle(static_cast<char*>(dev_ptr) - offset);
   if (e != cudaSuccess) return fail(AUGUR_KV_ECUDA, "ipc_close: cudaIpcCloseMemHandle: %s", cudaGetErrorString(e));
   return AUGUR_KV_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Ready flags between GPUs (disaggregated handoff)
+// ---------------------------------------------------------------------------
+
+namespace augur_kv_dev {
+
+// Release-store `value` to a flag that may live in another GPU's memory.
+__global__ void signal_kernel(int32_t* flag, int32_t value) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(flag), "r"(value) : "memory");
+}
+
+// Spin (acquire loads, with back-off) until *flag >= value or timeout_ns of
+// %globaltimer time have passed; on timeout record AUGUR_KV_ETIMEOUT and
+// return, so the stream moves on and the context stays usable.
+__global__ void wait_kernel(const int32_t* flag, int32_t value, int64_t timeout_ns, int32_t* status) {
+  const uint64_t t0 = global_timer_ns();
+  uint32_t backoff = 32;
+  while (true) {
+    int32_t v;
+    asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (v >= value) return;
+    if (global_timer_ns() - t0 > uint64_t(timeout_ns)) {
+      record_status(status, AUGUR_KV_ETIMEOUT);
+      return;
+    }
+    __nanosleep(backoff);
+    if (backoff < 4096) backoff <<= 1;
+  }
+}
+
+}  // namespace augur_kv_dev
+
+constexpr int64_t kMaxWaitNs = 60ll * 1000 * 1000 * 1000;  // cap on any requested wait
+
+AUGUR_KV_EXPORT int augur_kv_signal(int32_t* flag, int32_t value, void* stream) {
+  g_last_error[0] = '\0';
+  if (flag == nullptr) return fail(AUGUR_KV_EINVAL, "signal: null flag");
+  signal_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(flag, value);
+  return check_launch("signal_kernel");
+}
+
+AUGUR_KV_EXPORT int augur_kv_wait(const int32_t* flag, int32_t value, int64_t timeout_ns, int32_t* status,
+                                  void* stream) {
+  g_last_error[0] = '\0';
+  if (flag == nullptr) return fail(AUGUR_KV_EINVAL, "wait: null flag");
+  if (timeout_ns <= 0 || timeout_ns > kMaxWaitNs)
+    return fail(AUGUR_KV_EINVAL, "wait: timeout_ns must be in (0, %lld]", (long long)kMaxWaitNs);
+  wait_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(flag, value, timeout_ns, status);
+  return check_launch("wait_kernel");
 }
 
 // ---------------------------------------------------------------------------

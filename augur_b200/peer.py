@@ -29,7 +29,7 @@ from .paged_kv_cache import PagedKVCache
 
 @dataclass
 class ExportedPool:
-    """Picklable description of a pool another process can open."""
+    """Picklable description of a pool (and its ready flags) another process can open."""
 
     key_handle: bytes
     key_offset: int
@@ -40,6 +40,14 @@ class ExportedPool:
     dtype: str
     device_index: int
     block_size: int
+    flags_handle: bytes | None = None
+    flags_offset: int = 0
+    n_flags: int = 0
+
+
+def new_flags(device: torch.device, n: int = 16) -> torch.Tensor:
+    """Ready flags (int32, zero) a decode rank exports with its pool."""
+    return torch.zeros(n, dtype=torch.int32, device=device)
 
 
 def _export(t: torch.Tensor) -> tuple[bytes, int]:
@@ -51,15 +59,21 @@ def _export(t: torch.Tensor) -> tuple[bytes, int]:
     return handle.raw, int(off.value)
 
 
-def export_pool(cache: PagedKVCache) -> ExportedPool:
-    _ops.require_cuda("export_pool", cache.keys, cache.values)
+def export_pool(cache: PagedKVCache, flags: torch.Tensor | None = None) -> ExportedPool:
+    _ops.require_cuda("export_pool", cache.keys, cache.values, flags)
     if cache.keys.stride() != cache.values.stride():
         raise ValueError("keys and values must share one layout")
     kh, ko = _export(cache.keys)
     vh, vo = _export(cache.values)
+    fh, fo, nf = None, 0, 0
+    if flags is not None:
+        if flags.dtype != torch.int32 or not flags.is_contiguous():
+            raise ValueError("flags must be a contiguous int32 tensor")
+        fh, fo = _export(flags)
+        nf = flags.numel()
     return ExportedPool(kh, ko, vh, vo, tuple(cache.keys.shape), tuple(cache.keys.stride()),
                         str(cache.keys.dtype).replace("torch.", ""), cache.keys.device.index,
-                        cache.block_size)
+                        cache.block_size, fh, fo, nf)
 
 
 class PeerPool:
@@ -79,13 +93,20 @@ class PeerPool:
         self.block_size = exported.block_size
         self._bases: dict[bytes, int] = {}
         lib = _lib.load()
+        handles = {exported.key_handle, exported.value_handle}
+        if exported.flags_handle is not None:
+            handles.add(exported.flags_handle)
         with _ops._DeviceGuard(device):
-            for h in {exported.key_handle, exported.value_handle}:
+            for h in handles:
                 out = ctypes.c_void_p()
                 _lib.check(lib.augur_kv_ipc_open(h, 0, ctypes.byref(out)), "augur_kv_ipc_open")
                 self._bases[h] = int(out.value)
         self.keys_ptr = self._bases[exported.key_handle] + exported.key_offset
         self.values_ptr = self._bases[exported.value_handle] + exported.value_offset
+        self.flags_ptr = 0
+        self.n_flags = exported.n_flags
+        if exported.flags_handle is not None:
+            self.flags_ptr = self._bases[exported.flags_handle] + exported.flags_offset
 
     def close(self) -> None:
         lib = _lib.load()
@@ -93,7 +114,7 @@ class PeerPool:
             for h, base in list(self._bases.items()):
                 _lib.check(lib.augur_kv_ipc_close(base, 0), "augur_kv_ipc_close")
                 del self._bases[h]
-        self.keys_ptr = self.values_ptr = 0
+        self.keys_ptr = self.values_ptr = self.flags_ptr = 0
 
 
 def open_pool(exported: ExportedPool, device: torch.device | None = None) -> PeerPool:
@@ -127,7 +148,10 @@ def push_runs(src: PagedKVCache, dst: PeerPool, runs: np.ndarray, stream: torch.
             sk.data_ptr(), src.values.data_ptr(), _lib.i64_array(s_str), NB, bs, _ops.dtype_code(sk),
             dst.keys_ptr, dst.values_ptr, _lib.i64_array(d_str), dst.shape[1], dst.shape[3],
             _ops.dtype_code(sk), runs_t.data_ptr(), runs_t.shape[0], max_rows, L, H, D,
-            _lib.COPY_VECTOR,  # plain stores to peer memory; no bulk/TMA path
+            # plain stores to peer memory (no bulk/TMA path), each thread
+            # ending with a system-scope fence so a later signal() cannot
+            # become visible on the peer before the data
+            _lib.COPY_VECTOR | _lib.COPY_FENCE_SYSTEM,
             _ops.status_word(device).data_ptr(), st.cuda_stream)
     _lib.check(code, "augur_kv_copy_runs (peer push)")
     _ops.launch_count += 1
@@ -146,3 +170,36 @@ def push_blocks(src: PagedKVCache, src_blocks: Sequence[int], dst: PeerPool, dst
     runs[:, 2] = np.asarray(dst_blocks, dtype=np.int64)
     runs[:, 4] = src.block_size if n_rows is None else np.asarray(n_rows, dtype=np.int64)
     return push_runs(src, dst, runs, stream=stream)
+
+
+def signal(dst: PeerPool, value: int, index: int = 0, stream: torch.cuda.Stream | None = None) -> None:
+    """Release-store `value` into the peer's ready flag `index`, after the work already on `stream`."""
+    if not dst.flags_ptr:
+        raise ValueError("the peer pool was exported without ready flags")
+    if not 0 <= index < dst.n_flags:
+        raise ValueError("flag index out of range")
+    lib = _lib.load()
+    st = stream if stream is not None else torch.cuda.current_stream(dst.device)
+    with _ops._DeviceGuard(dst.device):
+        _lib.check(lib.augur_kv_signal(dst.flags_ptr + 4 * index, int(value), st.cuda_stream), "augur_kv_signal")
+    _ops.launch_count += 1
+
+
+def wait(flags: torch.Tensor, value: int, timeout_s: float = 10.0, index: int = 0,
+         stream: torch.cuda.Stream | None = None) -> None:
+    """Order work queued after this on `stream` behind flags[index] >= value (device side).
+
+    The wait gives up after timeout_s and records AUGUR_KV_ETIMEOUT in the
+    device status word (augur_b200.check_status() raises on it); it never
+    blocks the host. The signaller must run on another GPU.
+    """
+    _ops.require_cuda("wait", flags)
+    if flags.dtype != torch.int32 or not 0 <= index < flags.numel():
+        raise ValueError("flags must be int32 and index inside it")
+    lib = _lib.load()
+    device = flags.device
+    st = stream if stream is not None else torch.cuda.current_stream(device)
+    with _ops._DeviceGuard(device):
+        _lib.check(lib.augur_kv_wait(flags[index:].data_ptr(), int(value), int(timeout_s * 1e9),
+                                     _ops.status_word(device).data_ptr(), st.cuda_stream), "augur_kv_wait")
+    _ops.launch_count += 1

@@ -50,6 +50,11 @@ extern "C" {
 #define AUGUR_KV_COPY_AUTO 0   /* the measured-faster path for the layout (currently the vector path) */
 #define AUGUR_KV_COPY_VECTOR 1 /* the 16/8/4/2/1-byte vector path */
 #define AUGUR_KV_COPY_BULK 2   /* the TMA bulk path (EINVAL unless rows are dense and 16-byte aligned) */
+/* OR-able: every thread ends with a system-scope fence, so the copy's stores
+ * into another GPU's memory are performed before the kernel completes and a
+ * ready flag written by later work on the stream cannot overtake them
+ * (vector path; used for peer pushes). */
+#define AUGUR_KV_COPY_FENCE_SYSTEM 4
 
 /* Largest index passed by value to augur_kv_scatter (index_on_host = 1). */
 #define AUGUR_KV_INLINE_INDEX_MAX 32
@@ -154,6 +159,23 @@ int augur_kv_copy_runs(const void* src_k, const void* src_v,
 int augur_kv_ipc_export(const void* dev_ptr, void* handle_out, int64_t* offset_out);
 int augur_kv_ipc_open(const void* handle, int64_t offset, void** dev_ptr_out);
 int augur_kv_ipc_close(void* dev_ptr, int64_t offset);
+
+/*
+ * Ready flags for the disaggregated handoff (no reference counterpart).
+ * augur_kv_signal: a one-thread kernel on `stream` release-stores `value` to
+ *   the int32 at `flag` (system scope; the flag may be another GPU's memory
+ *   opened with augur_kv_ipc_open). Stream order puts it after the push.
+ * augur_kv_wait: a one-thread kernel on `stream` that spins with acquire
+ *   loads until *flag >= value, for at most timeout_ns (0 < timeout_ns <=
+ *   60 s) of %globaltimer time; on timeout it writes AUGUR_KV_ETIMEOUT to the
+ *   status word and returns, so later work on the stream runs and the
+ *   context stays usable. Work queued after the wait on the same stream is
+ *   ordered after the flag (or the timeout).
+ * A signaller and its waiter must run on different GPUs: two launches on one
+ * GPU are not guaranteed to run at the same time.
+ */
+int augur_kv_signal(int32_t* flag, int32_t value, void* stream);
+int augur_kv_wait(const int32_t* flag, int32_t value, int64_t timeout_ns, int32_t* status, void* stream);
 
 /*
  * augur_kv_copy_runs_noalloc — augur_kv_copy_runs for callers that cannot

@@ -36,7 +36,7 @@ def test_header_declarations_are_exported_and_bound():
 def test_status_codes_match_header():
     text = open(HEADER).read()
     for name in ("OK", "EINVAL", "EBOUNDS", "ECUDA", "ETIMEOUT", "F32", "F16", "BF16",
-                 "COPY_AUTO", "COPY_VECTOR", "COPY_BULK"):
+                 "COPY_AUTO", "COPY_VECTOR", "COPY_BULK", "COPY_FENCE_SYSTEM"):
         m = re.search(rf"#define AUGUR_KV_{name} (\d+)", text)
         assert m and int(m.group(1)) == getattr(_lib, name), name
 

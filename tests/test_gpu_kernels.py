@@ -330,3 +330,28 @@ def test_host_index_bounds_check(cuda):
     assert _ops.read_status(cuda) == _lib.EBOUNDS
     assert_bits_equal(pool.keys[0, 0, :, 3], k[0, 0], "valid token")
     assert int((pool.keys.view(torch.int16) == -1).sum()) == pool.keys.numel() - 2 * 64
+
+
+def test_wait_times_out_and_context_stays_usable(cuda):
+    """A wait on a flag nothing sets gives up after its bound, reports ETIMEOUT, and the GPU carries on."""
+    import time
+
+    from augur_b200 import peer
+
+    flags = peer.new_flags(cuda)
+    t0 = time.perf_counter()
+    peer.wait(flags, 1, timeout_s=0.3)
+    assert _ops.read_status(cuda) == _lib.ETIMEOUT
+    assert 0.25 < time.perf_counter() - t0 < 10.0
+    # already satisfied: no timeout
+    flags.fill_(5)
+    peer.wait(flags, 3, timeout_s=0.3)
+    assert _ops.read_status(cuda) == _lib.OK
+    # the context still runs kernels
+    pool = _pool(1, 4, 2, 4, 64, torch.bfloat16, cuda)
+    k = torch.randn(1, 1, 2, 64, device=cuda).to(torch.bfloat16)
+    batched.write_paged_kv_batch(pool, k, k, np.array([5], dtype=np.int64))
+    assert _ops.read_status(cuda) == _lib.OK
+    assert_bits_equal(pool.keys[0, 1, :, 1], k[0, 0], "write after timeout")
+    with pytest.raises(_lib.KVLibraryError):
+        peer.wait(flags, 1, timeout_s=0.0)

@@ -1,11 +1,14 @@
 """Disaggregated prefill -> decode push between two GPUs (two processes).
 
-Rank 1 (decode) exports its block pool and the destination blocks its own
-allocator picked; rank 0 (prefill) scatters seeded K/V into its local pool,
-opens rank 1's pool through CUDA IPC and pushes the blocks with one kernel
-(plain stores over NVLink). Rank 1 then compares its whole pool, bit for
-bit, with the same tokens written locally through write_paged_kv_batch:
-pushed rows must match and every other row must still hold the poison.
+Rank 1 (decode) exports its block pool, a ready flag and the destination
+blocks its own allocator picked, and queues a device-side wait on the flag
+followed by a gather of those blocks; rank 0 (prefill) scatters seeded K/V
+into its local pool, opens rank 1's pool through CUDA IPC, pushes the blocks
+with one kernel (plain stores over NVLink) and signals the flag. Rank 1 then
+compares its whole pool, bit for bit, with the same tokens written locally
+through write_paged_kv_batch (pushed rows must match, every other row must
+still hold the poison), and the gather that waited on the flag must have
+seen the pushed data.
 Needs two GPUs; skipped on one.
 """
 
@@ -71,9 +74,20 @@ def _worker(rank: int, port: int, q) -> None:
             pool.allocator.allocate_many(5)  # decode pool already holds other work
             dst_tables = [ab.SequenceBlockTable.empty(BS) for _ in lens]
             batched.prefill_slot_mapping(dst_tables, lens, pool.allocator)
-            obj = [(peer.export_pool(pool), [t.block_ids for t in dst_tables])]
+            flags = peer.new_flags(dev)
+            obj = [(peer.export_pool(pool, flags), [t.block_ids for t in dst_tables])]
         dist.broadcast_object_list(obj, src=1)
         exported, dst_ids = obj[0]
+        if rank == 1:
+            # queue, before the push has happened, a device-side wait for the
+            # prefill rank's ready flag and then a gather of the pushed blocks
+            w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            w0.record()
+            peer.wait(flags, 1, timeout_s=30.0)
+            w1.record()
+            early = batched.read_paged_kv_batch(
+                pool, [ab.SequenceBlockTable(block_ids=list(ids), block_size=BS, seq_len=int(n))
+                       for ids, n in zip(dst_ids, lens)])
         # 2. the prefill rank scatters locally, then pushes block by block into the peer pool
         if rank == 0:
             src_tables = [ab.SequenceBlockTable.empty(BS) for _ in lens]
@@ -88,6 +102,7 @@ def _worker(rank: int, port: int, q) -> None:
                     dst_b.append(ids[j])
                     rows.append(min(BS, int(n) - j * BS))
             moved = peer.push_blocks(pool, src_b, remote, dst_b, rows)
+            peer.signal(remote, 1)  # stream-ordered after the push
             torch.cuda.synchronize(dev)
             assert _ops.read_status(dev) == _lib.OK
         dist.barrier()  # push complete
@@ -101,7 +116,17 @@ def _worker(rank: int, port: int, q) -> None:
             torch.cuda.synchronize(dev)
             same_k = torch.equal(pool.keys.view(torch.int16), ref.keys.view(torch.int16))
             same_v = torch.equal(pool.values.view(torch.int16), ref.values.view(torch.int16))
-            q.put(("decode", bool(same_k), bool(same_v), int(lens.sum())))
+            # the gather queued behind the device wait saw the pushed data
+            # (valid rows of each sequence; rows past a length are not written)
+            rk, rv = batched.read_paged_kv_batch(ref, tables, seq_lens=[int(n) for n in lens])
+            same_early = all(
+                torch.equal(early[0][:, b, :, :n].view(torch.int16), rk[:, b, :, :n].view(torch.int16))
+                and torch.equal(early[1][:, b, :, :n].view(torch.int16), rv[:, b, :, :n].view(torch.int16))
+                for b, n in enumerate(int(x) for x in lens))
+            status = _ops.read_status(dev)
+            q.put(("decode", {"same_k": bool(same_k), "same_v": bool(same_v), "same_early": bool(same_early),
+                              "status": status, "wait_ms": w0.elapsed_time(w1), "flag": int(flags[0].item())},
+                   int(lens.sum())))
         dist.barrier()  # checks done; the importer may unmap now
         if rank == 0:
             remote.close()
@@ -127,6 +152,8 @@ def test_push_blocks_between_two_gpus():
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    same_k, same_v, tokens = got["decode"]
-    assert same_k and same_v
+    checks, tokens = got["decode"]
+    msg = " ".join(f"{k}={v}" for k, v in checks.items())
+    assert checks["same_k"] and checks["same_v"], msg
+    assert checks["same_early"] and checks["status"] == 0 and checks["flag"] == 1, msg
     assert got["prefill"][0] == tokens * L * 2 * H * D * 2
