@@ -29,6 +29,9 @@ COPY_VECTOR = 1
 COPY_BULK = 2
 COPY_FENCE_SYSTEM = 4
 
+ATTN_AUTO = 0
+ATTN_GENERIC = 1
+
 STATUS_NAMES = {
     OK: "ok",
     EINVAL: "invalid argument",
@@ -64,6 +67,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "augur_kv_ipc_export": (ctypes.c_int, [_P, _P, _I64P]),
     "augur_kv_ipc_open": (ctypes.c_int, [_P, _I64, ctypes.POINTER(ctypes.c_void_p)]),
     "augur_kv_ipc_close": (ctypes.c_int, [_P, _I64]),
+    "augur_kv_paged_decode_attention": (
+        ctypes.c_int,
+        [_P, _I64P, _P, _P, _I64P, _I64, _I32, _P, _I64, _I64, _P, _I32, _I32, _I32, _I32, _I32, _I32,
+         _P, _I64P, _I32, _P, _P],
+    ),
     "augur_kv_signal": (ctypes.c_int, [_P, _I32, _P]),
     "augur_kv_wait": (ctypes.c_int, [_P, _I32, _I64, _P, _P]),
 }

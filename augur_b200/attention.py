@@ -1,0 +1,121 @@
+"""Decode attention that reads the paged KV pool in place.
+
+augur's attention gathers the whole cached sequence out of the pool position
+by position (read_paged_kv, augur/attention.py:72), repeats each KV head for
+its query heads (:75-76) and runs q.k^T, a float32 softmax and P.V eagerly
+(:78-86), one sequence and one layer at a time. paged_decode_attention does
+the same computation for a decode step of a whole batch in one launch per
+layer (augur_kv_paged_decode_attention), reading every K/V row once straight
+from its block. Results match the reference's within floating-point
+tolerance: the kernels round where the reference rounds (scores and
+probabilities in the cache dtype, softmax in float32) but sum in another
+order.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Sequence
+
+import numpy as np
+import torch
+from torch import Tensor
+
+from . import _lib, _ops
+from .paged_kv_cache import PagedKVCache, SequenceBlockTable
+
+
+class DecodeTables:
+    """Device copy of a batch's block tables and lengths, reusable across layers.
+
+    blocks: int32 [batch, max_blocks] (unused entries -1), lens: int32 [batch].
+    """
+
+    def __init__(self, tables: Sequence[SequenceBlockTable], device: torch.device,
+                 seq_lens: Sequence[int] | None = None) -> None:
+        lens = [t.seq_len for t in tables] if seq_lens is None else [int(n) for n in seq_lens]
+        if len(lens) != len(tables):
+            raise ValueError("seq_lens and tables must have the same length")
+        width = max([len(t.block_ids) for t in tables] + [1])
+        host = np.full((len(tables), width), -1, dtype=np.int32)
+        for b, t in enumerate(tables):
+            if lens[b] < 0 or -(-lens[b] // t.block_size) > len(t.block_ids):
+                raise ValueError("position exceeds block table capacity")
+            host[b, : len(t.block_ids)] = t.block_ids
+        self.block_size = tables[0].block_size if tables else 1
+        if any(t.block_size != self.block_size for t in tables):
+            raise ValueError("all block tables must share one block_size")
+        self.blocks = torch.from_numpy(host).to(device)
+        self.lens = torch.tensor(lens, dtype=torch.int32).to(device)
+        self.max_seq_len = max(lens, default=0)
+        self.batch = len(tables)
+
+
+def paged_decode_attention(
+    q: Tensor,
+    cache: PagedKVCache,
+    layer_idx: int,
+    tables: Sequence[SequenceBlockTable] | DecodeTables,
+    out: Tensor | None = None,
+    generic: bool = False,
+    stream: torch.cuda.Stream | None = None,
+) -> Tensor:
+    """Attention of each sequence's decode query over its cached K/V (one layer).
+
+    q: ``[batch, n_q_heads, head_dim]`` or ``[batch, n_q_heads, 1, head_dim]``
+    (after RoPE), in the cache dtype. tables: one SequenceBlockTable per
+    sequence (its seq_len positions are attended) or a prepared DecodeTables.
+    Returns the attention output in q's shape (before the output projection,
+    heads not yet concatenated). generic=True forces the CUDA-core kernel.
+    """
+    squeeze = q.dim() == 4
+    if squeeze:
+        if q.shape[2] != 1:
+            raise ValueError("paged_decode_attention takes one query token per sequence")
+        q3 = q[:, :, 0, :]
+    elif q.dim() == 3:
+        q3 = q
+    else:
+        raise ValueError("q must be [batch, heads, head_dim] or [batch, heads, 1, head_dim]")
+    _ops.require_cuda("paged_decode_attention", q3, cache.keys, cache.values)
+    if not 0 <= layer_idx < cache.keys.shape[0]:
+        raise ValueError("layer_idx is outside the cache layer range")
+    L, NB, Hkv, bs, D = cache.keys.shape
+    B, Hq, Dq = q3.shape
+    if Dq != D or Hq % Hkv != 0:
+        raise ValueError("query shape does not match the cache (head_dim, or heads not a multiple of KV heads)")
+    if q3.dtype != cache.keys.dtype:
+        raise ValueError("query and cache dtypes differ")
+    if q3.stride(-1) != 1:
+        q3 = q3.contiguous()
+    dt = tables if isinstance(tables, DecodeTables) else DecodeTables(tables, cache.keys.device)
+    if dt.batch != B:
+        raise ValueError("one block table per sequence is required")
+    if dt.block_size != bs:
+        raise ValueError("block table block_size must equal the cache block size")
+    if out is None:
+        out3 = torch.empty(B, Hq, D, dtype=q3.dtype, device=q3.device)
+    else:
+        out3 = out[:, :, 0, :] if out.dim() == 4 else out
+    if B == 0:
+        return out if out is not None else (out3.unsqueeze(2) if squeeze else out3)
+    kc, vc = cache.keys[layer_idx], cache.values[layer_idx]
+    if kc.stride() != vc.stride():
+        raise ValueError("keys and values must share one layout")
+    lib = _lib.load()
+    device = kc.device
+    st = stream if stream is not None else torch.cuda.current_stream(device)
+    with _ops._DeviceGuard(device):
+        code = lib.augur_kv_paged_decode_attention(
+            q3.data_ptr(), _lib.i64_array((q3.stride(0), q3.stride(1))),
+            kc.data_ptr(), vc.data_ptr(), _lib.i64_array((kc.stride(0), kc.stride(1), kc.stride(2))),
+            NB, bs, dt.blocks.data_ptr(), dt.blocks.stride(0), dt.blocks.shape[1],
+            dt.lens.data_ptr(), dt.max_seq_len, B, Hq, Hkv, D, _ops.dtype_code(q3),
+            out3.data_ptr(), _lib.i64_array((out3.stride(0), out3.stride(1))),
+            _lib.ATTN_GENERIC if generic else _lib.ATTN_AUTO,
+            _ops.status_word(device).data_ptr(), st.cuda_stream)
+    _lib.check(code, "augur_kv_paged_decode_attention")
+    _ops.launch_count += 1
+    _ops.keep_until_done(st, q3, dt.blocks, dt.lens)
+    if out is not None:
+        return out
+    return out3.unsqueeze(2) if squeeze else out3

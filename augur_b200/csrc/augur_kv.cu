@@ -34,6 +34,7 @@
 #include <string.h>
 
 #include "augur_kv.h"
+#include "common.cuh"
 
 #define AUGUR_KV_VERSION ((0 << 16) | 4)
 
@@ -73,8 +74,6 @@ int pow2_shift(int64_t v) {
   while ((int64_t(1) << s) < v) ++s;
   return s;
 }
-
-constexpr int kMaxDevices = 64;
 
 // Guards the per-device launch-configuration caches below; entry points are
 // otherwise stateless and may be called from several host threads.
@@ -129,10 +128,6 @@ unsigned grid_x(uint64_t n_runs, uint64_t warps, uint64_t planes, uint64_t cap) 
 // ---------------------------------------------------------------------------
 // Device helpers
 // ---------------------------------------------------------------------------
-
-__device__ __forceinline__ void record_status(int32_t* status, int code) {
-  if (status != nullptr) atomicCAS(status, 0, code);
-}
 
 template <int VEC> struct VecType;
 template <> struct VecType<16> { using T = uint4; };

@@ -17,8 +17,8 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.dirname(HERE)
 ROOT = os.path.dirname(PKG)
-SOURCES = [os.path.join(HERE, "augur_kv.cu")]
-HEADERS = [os.path.join(ROOT, "include", "augur_kv.h")]
+SOURCES = [os.path.join(HERE, "augur_kv.cu"), os.path.join(HERE, "augur_attn.cu")]
+HEADERS = [os.path.join(ROOT, "include", "augur_kv.h"), os.path.join(HERE, "common.cuh")]
 OUTPUT = os.path.join(PKG, "libaugur_kv.so")
 
 NVCC_FLAGS = [

@@ -140,6 +140,44 @@ int augur_kv_copy_runs(const void* src_k, const void* src_v,
                        int32_t flags, int32_t* status, void* stream);
 
 /*
+ * augur_kv_paged_decode_attention — attention of one decode query per
+ * sequence over its paged K/V, one layer, every sequence of the batch in one
+ * launch. Replaces, for a decode step, read_paged_kv (the position-by-position
+ * gather, augur/paged_kv_cache.py:195-221) plus the GQA repeat, the two
+ * matmuls and the float32 softmax of augur/attention.py:72-86.
+ *
+ *   q       element (b, h, d) at q + b*q_strides[0] + h*q_strides[1] + d
+ *           (n_q_heads rows per sequence, after RoPE)
+ *   pools   one layer of the K and V pools: (block, kv_head, row, d) at
+ *           pool + block*pool_strides[0] + kv_head*pool_strides[1]
+ *           + row*pool_strides[2] + d
+ *   tables  device int32 [batch][tables_stride]: logical block j of sequence
+ *           b is block tables[b*tables_stride + j], j < max_blocks
+ *   seq_lens device int32 [batch]; positions [0, seq_lens[b]) are attended;
+ *           max_seq_len bounds them (host-known)
+ *   out     element (b, h, d) at out + b*out_strides[0] + h*out_strides[1] + d
+ * Query head h reads KV head h / (n_q_heads / n_kv_heads). The result equals
+ * the reference's within floating-point tolerance (same rounding points,
+ * different summation order). A block id outside [0, num_blocks) or a
+ * position past max_blocks records AUGUR_KV_EBOUNDS and reads as zeros.
+ * flags: AUGUR_KV_ATTN_AUTO picks the tensor-core kernel for bf16/fp16,
+ * head_dim 64 or 128, <= 16 query heads per KV head; AUGUR_KV_ATTN_GENERIC
+ * forces the CUDA-core kernel (any dtype; max_seq_len <= ~51,000).
+ */
+#define AUGUR_KV_ATTN_AUTO 0
+#define AUGUR_KV_ATTN_GENERIC 1
+
+int augur_kv_paged_decode_attention(const void* q, const int64_t* q_strides, /* [2] */
+                                    const void* k_pool, const void* v_pool,
+                                    const int64_t* pool_strides, /* [3] block, head, row */
+                                    int64_t num_blocks, int32_t block_size,
+                                    const int32_t* block_tables, int64_t tables_stride, int64_t max_blocks,
+                                    const int32_t* seq_lens, int32_t max_seq_len, int32_t batch,
+                                    int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim, int32_t dtype,
+                                    void* out, const int64_t* out_strides, /* [2] */
+                                    int32_t flags, int32_t* status, void* stream);
+
+/*
  * Peer memory for the disaggregated mode: a decode GPU's process exports its
  * block pool, a prefill GPU's process opens it and pushes finished blocks into
  * it with augur_kv_copy_runs (vector path: plain 16-byte stores over NVLink).

@@ -272,3 +272,26 @@ def poison_(t: torch.Tensor) -> torch.Tensor:
 def bits(t: torch.Tensor) -> torch.Tensor:
     """Bit view for exact comparison (NaNs and -0 compare by bits)."""
     return t.contiguous().view(torch.int16 if t.element_size() == 2 else torch.int32)
+
+
+# ---------------------------------------------------------------------------
+# decode attention over a paged cache (floating point; torch on CPU)
+# ---------------------------------------------------------------------------
+
+
+def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    """Attention of one decode query per sequence, restating augur/attention.py:74-86.
+
+    q [B, Hq, 1, D] (after RoPE), k / v [B, Hkv, S, D] (the cache gathered in
+    logical order, read_paged_kv). K/V heads are repeated for the query heads
+    of their group; scores are q k^T / sqrt(D) in the input dtype; the
+    softmax runs in float32 and its result is cast back before the product
+    with V. The decode query is the last position, so the causal mask
+    (attention.py:80-81) hides nothing.
+    """
+    groups = q.shape[1] // k.shape[1]
+    k = k.repeat_interleave(groups, dim=1)
+    v = v.repeat_interleave(groups, dim=1)
+    scores = torch.matmul(q, k.transpose(-2, -1)) / math.sqrt(q.shape[-1])
+    probs = torch.softmax(scores, dim=-1, dtype=torch.float32).to(q.dtype)
+    return torch.matmul(probs, v)

@@ -242,6 +242,60 @@ def fork_case(ref, g):
             "prefix_values": pv, "suffix_keys": sk, "suffix_values": sv, "reads": reads}
 
 
+def attention_cases(ref, g):
+    """Decode-step paged attention through the reference's own attention() (augur/attention.py:22-92).
+
+    augur's GQA shape (14 query heads, 2 KV heads, head_dim 64), one layer,
+    block size 16. The prompt is prefilled through attention() with a paged
+    cache, then one decode token; the o-projection is the identity, so the
+    output is the attention core (heads concatenated). Stored: the rotated
+    decode query, the pool, the block table and the reference output.
+    """
+    import torch.nn.functional as F
+    from einops import rearrange
+
+    from augur.attention import attention
+    from augur.rope import apply_rope
+
+    P = ref.paged_kv_cache
+    W = ref.weights
+    cases = {}
+    for name, dtype, seq in (("f32", torch.float32, 37), ("bf16", torch.bfloat16, 300)):
+        cfg = ref.config.QwenConfig(vocab_size=16, hidden_size=896, intermediate_size=16,
+                                    num_hidden_layers=1, num_attention_heads=14, num_key_value_heads=2)
+        D, Hq, Hkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
+        w = W.Attention(
+            q=W.Linear((torch.randn(Hq * D, 896, generator=g) * 0.06).to(dtype),
+                       (torch.randn(Hq * D, generator=g) * 0.1).to(dtype)),
+            k=W.Linear((torch.randn(Hkv * D, 896, generator=g) * 0.06).to(dtype),
+                       (torch.randn(Hkv * D, generator=g) * 0.1).to(dtype)),
+            v=W.Linear((torch.randn(Hkv * D, 896, generator=g) * 0.06).to(dtype)),
+            o=W.Linear(torch.eye(896, dtype=dtype)),
+        )
+        x = torch.randn(1, seq, 896, generator=g).to(dtype)
+        state = P.PagedKVCacheState(
+            cache=P.new_paged_kv_cache(cfg, num_blocks=-(-seq // 16) + 3, block_size=16,
+                                       device=torch.device("cpu"), dtype=dtype),
+            block_table=P.SequenceBlockTable.empty(block_size=16),
+        )
+        state.cache.allocator.allocate()  # the pool already holds another block
+        pos = torch.arange(seq).unsqueeze(0)
+        attention(x[:, : seq - 1], w, cfg, pos[:, : seq - 1], paged_cache=state, layer_idx=0)
+        out = attention(x[:, seq - 1 :], w, cfg, pos[:, seq - 1 :], paged_cache=state, layer_idx=0)
+        q = rearrange(F.linear(x[:, seq - 1 :], w.q.weight, w.q.bias),
+                      "batch seq (heads head_dim) -> batch heads seq head_dim", heads=Hq, head_dim=D)
+        k_last = rearrange(F.linear(x[:, seq - 1 :], w.k.weight, w.k.bias),
+                           "batch seq (heads head_dim) -> batch heads seq head_dim", heads=Hkv, head_dim=D)
+        q, _ = apply_rope(q, k_last, pos[:, seq - 1 :], cfg.rope_theta)
+        kk, vv = P.read_paged_kv(state.cache, 0, state.block_table)
+        cases[name] = {"q": q.contiguous(), "keys": state.cache.keys.clone(), "values": state.cache.values.clone(),
+                       "block_ids": list(state.block_table.block_ids), "seq_len": state.block_table.seq_len,
+                       "k": kk.clone(), "v": vv.clone(),
+                       "out": out.view(1, 1, Hq, D).permute(0, 2, 1, 3).contiguous(),
+                       "n_kv_heads": Hkv}
+    return cases
+
+
 def bookkeeping_scripts(ref):
     P = ref.paged_kv_cache
     alloc = P.BlockAllocator(num_blocks=12)
@@ -347,6 +401,7 @@ def main() -> None:
     ap.add_argument("--skip-config1", action="store_true")
     args = ap.parse_args()
     sys.path.insert(0, os.path.join(args.reference, "src"))
+    import augur.attention  # noqa: F401
     import augur.config
     import augur.kv_cache
     import augur.model
@@ -371,6 +426,7 @@ def main() -> None:
         "fork": fork_case(Ref, g),
         "bookkeeping": bookkeeping_scripts(Ref),
     }
+    cases["attention"] = attention_cases(Ref, torch.Generator().manual_seed(4321))
     torch.save(cases, os.path.join(HERE, "reference_cases.pt"))
     if not args.skip_config1:
         torch.save(config1(Ref), os.path.join(HERE, "config1_writes.pt"))

@@ -308,3 +308,17 @@ def test_copy_prefix_validation():
         ab.copy_prefix_into_cache(bad, cache)
     with pytest.raises(ValueError, match="needs CUDA tensors"):
         ab.copy_prefix_into_cache(entry, cache)
+
+
+def test_paged_decode_attention_refuses_cpu_and_bad_shapes():
+    from augur_b200.attention import DecodeTables, paged_decode_attention
+
+    cfg = ab.QwenConfig()
+    cpu = ab.new_paged_kv_cache(cfg, num_blocks=2, block_size=16, device=torch.device("cpu"), dtype=torch.bfloat16)
+    t = ab.SequenceBlockTable(block_ids=[0], block_size=16, seq_len=3)
+    with pytest.raises(ValueError, match="needs CUDA tensors"):
+        paged_decode_attention(torch.zeros(1, 14, 64, dtype=torch.bfloat16), cpu, 0, [t])
+    with pytest.raises(ValueError, match="one query token"):
+        paged_decode_attention(torch.zeros(1, 14, 2, 64, dtype=torch.bfloat16), cpu, 0, [t])
+    with pytest.raises(ValueError, match="block table capacity"):
+        DecodeTables([ab.SequenceBlockTable(block_ids=[0], block_size=16, seq_len=17)], torch.device("cpu"))

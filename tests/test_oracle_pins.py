@@ -271,3 +271,11 @@ def test_golden_config1_replay(oracle, config1_golden):
     assert c["seq_len"] == 160
     assert hashlib.sha256(ck.numpy().tobytes()).hexdigest() == c["sha256_keys"]
     assert hashlib.sha256(cv.numpy().tobytes()).hexdigest() == c["sha256_values"]
+
+
+@pytest.mark.parametrize("case", ["f32", "bf16"])
+def test_golden_decode_attention(oracle, golden, case):
+    """The oracle's attention equals the reference's own attention() on its paged cache."""
+    c = golden["attention"][case]
+    got = oracle.decode_attention(c["q"], c["k"], c["v"])
+    assert_bits_equal(got, c["out"], "attention output")
