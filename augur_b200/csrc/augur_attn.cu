@@ -58,6 +58,8 @@ struct AttnArgs {
   const int32_t* seq_lens;
   int32_t batch, hq, hkv, groups, head_dim;
   float sqrt_d;
+  float inv_sqrt_d;     // 1 / sqrt_d, used when multiplying by it equals dividing
+  int32_t scale_exact;  // sqrt_d is a power of two
   char* out;
   int64_t out_stride_b, out_stride_h;  // bytes
   int32_t dtype;
@@ -181,13 +183,16 @@ constexpr int kTile = 16;  // tokens per tile
 
 template <int D>
 struct MmaSmem {
+  static constexpr int kStages = 3;             // tiles in flight per warp
   static constexpr int kRowBytes = D * 2 + 16;  // padded: ldmatrix rows hit distinct banks
   static constexpr int kTileBytes = kTile * kRowBytes;
-  static constexpr int kPipe = kAttnWarps * 2 /*stages*/ * 2 /*K,V*/ * kTileBytes;
+  static constexpr int kPipe = kAttnWarps * kStages * 2 /*K,V*/ * kTileBytes;
+  // after the token loop the warps' partial results reuse the pipeline buffers
   static constexpr int kPartO = kAttnWarps * 16 * D * 4;
   static constexpr int kPartML = kAttnWarps * 16 * 4;
+  static_assert(kPartO + 2 * kPartML <= kPipe, "partials must fit in the pipeline buffers");
   static constexpr int kCtaO = 16 * D * 4;
-  static constexpr int kBytes = kPipe + kPartO + 2 * kPartML + kCtaO + 2 * 16 * 4;
+  static constexpr int kBytes = kPipe + kCtaO + (2 * 16 + kAttnWarps * 16 + 3 * 8 * 16 + 16) * 4;
 };
 
 template <typename T, int D>
@@ -196,12 +201,17 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_mma_kernel(AttnAr
   constexpr int CHUNKS = D * 2 / 16;  // 16-byte pieces per row
   constexpr int DT = MmaType<T>::dtype;
   extern __shared__ __align__(128) unsigned char smem[];
-  float* part_o = reinterpret_cast<float*>(smem + SM::kPipe);
-  float* part_m = reinterpret_cast<float*>(smem + SM::kPipe + SM::kPartO);
+  float* part_o = reinterpret_cast<float*>(smem);  // aliases the pipeline after the loop
+  float* part_m = reinterpret_cast<float*>(smem + SM::kPartO);
   float* part_l = part_m + kAttnWarps * 16;
-  float* cta_o = part_l + kAttnWarps * 16;
+  float* cta_o = reinterpret_cast<float*>(smem + SM::kPipe);
   float* cta_m = cta_o + 16 * D;
   float* cta_l = cta_m + 16;
+  float* fac = cta_l + 16;            // [warps][16] rescale factors
+  float* rm = fac + kAttnWarps * 16;  // [8 ranks][16] gathered row maxima
+  float* rl = rm + 8 * 16;            // [8][16] gathered row sums
+  float* rf = rl + 8 * 16;            // [8][16] rescale factors per rank
+  float* rL = rf + 8 * 16;            // [16] combined row sums
 
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = int(cluster.block_rank());
@@ -238,37 +248,53 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_mma_kernel(AttnAr
   for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float mrow[2] = {kNegInf, kNegInf}, lrow[2] = {0.f, 0.f};
 
-  unsigned char* wbuf = smem + warp * (2 * 2 * SM::kTileBytes);
-  auto load_tile = [&](int tile, int stage) {
+  constexpr int NST = SM::kStages;
+  unsigned char* wbuf = smem + warp * (NST * 2 * SM::kTileBytes);
+  // Each lane copies a fixed 16-byte column (part) of RPL rows of every
+  // tile, for K and V alike: one table lookup per row serves both.
+  constexpr int RPL = CHUNKS / 2;           // rows per lane per tile
+  constexpr int ROW_STEP = 32 / CHUNKS;     // row distance between a lane's rows
+  const int part = lane % CHUNKS;
+  const int row_base = lane / CHUNKS;
+  auto load_tile = [&](int tile, int st) {
+    unsigned char* kdst = wbuf + (st * 2 + 0) * SM::kTileBytes + part * 16;
+    unsigned char* vdst = wbuf + (st * 2 + 1) * SM::kTileBytes + part * 16;
 #pragma unroll
-    for (int c = lane; c < 2 * kTile * CHUNKS; c += 32) {
-      const int kvsel = c >= kTile * CHUNKS ? 1 : 0;
-      const int cc = c - kvsel * kTile * CHUNKS;
-      const int r = cc / CHUNKS, part = cc - (cc / CHUNKS) * CHUNKS;
+    for (int i = 0; i < RPL; ++i) {
+      const int r = row_base + i * ROW_STEP;
       const int pos = tile * kTile + r;
-      unsigned char* dst = wbuf + (stage * 2 + kvsel) * SM::kTileBytes + r * SM::kRowBytes + part * 16;
-      const char* src = kvsel ? a.v : a.k;
+      const char* kp = a.k;
+      const char* vp = a.v;
       int bytes = 0;
       if (pos < S) {
-        const char* rp = row_addr(a, kvsel ? a.v : a.k, b, hk, pos);
-        if (rp != nullptr) {
-          src = rp + part * 16;
+        const char* rk = row_addr(a, a.k, b, hk, pos);
+        if (rk != nullptr) {
+          kp = rk + part * 16;
+          vp = a.v + (rk - a.k) + part * 16;
           bytes = 16;
         }
       }
-      cp_async16(dst, src, bytes);
+      cp_async16(kdst + r * SM::kRowBytes, kp, bytes);
+      cp_async16(vdst + r * SM::kRowBytes, vp, bytes);
     }
     cp_async_commit();
   };
 
-  int stage = 0;
-  int tile = tile0 + warp;
-  if (tile < tile1) load_tile(tile, 0);
-  for (; tile < tile1; tile += kAttnWarps) {
-    if (tile + kAttnWarps < tile1) load_tile(tile + kAttnWarps, stage ^ 1);
+  const int my_first = tile0 + warp;
+  const int n_my = my_first < tile1 ? (tile1 - my_first + kAttnWarps - 1) / kAttnWarps : 0;
+#pragma unroll
+  for (int i = 0; i < NST - 1; ++i) {
+    if (i < n_my) load_tile(my_first + i * kAttnWarps, i);
     else cp_async_commit();
-    cp_async_wait<1>();
+  }
+  for (int it = 0; it < n_my; ++it) {
+    const int nxt = it + NST - 1;
+    if (nxt < n_my) load_tile(my_first + nxt * kAttnWarps, nxt % NST);
+    else cp_async_commit();
+    cp_async_wait<NST - 1>();
     __syncwarp();
+    const int tile = my_first + it * kAttnWarps;
+    const int stage = it % NST;
     const unsigned char* Ks = wbuf + (stage * 2 + 0) * SM::kTileBytes;
     const unsigned char* Vs = wbuf + (stage * 2 + 1) * SM::kTileBytes;
 
@@ -291,7 +317,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_mma_kernel(AttnAr
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int pos = tile * kTile + nt * 8 + 2 * t + (j & 1);
-        float x = round_to(round_to(s[nt][j], DT) / a.sqrt_d, DT);
+        const float r = round_to(s[nt][j], DT);
+        float x = round_to(a.scale_exact ? r * a.inv_sqrt_d : r / a.sqrt_d, DT);
         s[nt][j] = pos < S ? x : kNegInf;
       }
     }
@@ -352,9 +379,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_mma_kernel(AttnAr
       }
     }
     __syncwarp();  // every lane is done with this stage before it is refilled
-    stage ^= 1;
   }
   cp_async_wait<0>();
+  __syncthreads();  // every warp is done with the pipeline buffers the partials reuse
 
   // warps -> CTA
 #pragma unroll
@@ -372,48 +399,66 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_mma_kernel(AttnAr
     part_l[warp * 16 + g + 8] = lrow[1];
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
-    const int row = i / D, d = i - row * D;
+  // warps -> CTA: rescale factors once per (warp, row), then the 16 x D sums
+  if (int(threadIdx.x) < G) {
+    const int row = threadIdx.x;
     float M = kNegInf;
     for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, part_m[w * 16 + row]);
-    float L = 0.f, O = 0.f;
-    if (M != kNegInf) {
-      for (int w = 0; w < kAttnWarps; ++w) {
-        const float mw = part_m[w * 16 + row];
-        if (mw == kNegInf) continue;
-        const float f = expf(mw - M);
-        L += part_l[w * 16 + row] * f;
-        O += part_o[(w * 16 + row) * D + d] * f;
-      }
+    float L = 0.f;
+    for (int w = 0; w < kAttnWarps; ++w) {
+      const float mw = part_m[w * 16 + row];
+      const float f = (mw == kNegInf) ? 0.f : expf(mw - M);
+      fac[w * 16 + row] = f;
+      L += part_l[w * 16 + row] * f;
     }
-    cta_o[row * D + d] = O;
-    if (d == 0) {
-      cta_m[row] = M;
-      cta_l[row] = L;
-    }
+    cta_m[row] = M;
+    cta_l[row] = L;
   }
-  // CTAs of the cluster -> rank 0, through distributed shared memory
+  __syncthreads();
+  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+    const int row = i / D, d = i - row * D;
+    float O = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) O += part_o[(w * 16 + row) * D + d] * fac[w * 16 + row];
+    cta_o[row * D + d] = O;
+  }
+  // CTAs of the cluster, through distributed shared memory: every rank reads
+  // all ranks' (m, l), then combines and writes its own slice of the outputs
   cluster.sync();
-  if (rank == 0) {
+  if (int(threadIdx.x) < G * nsplit) {
+    const int row = threadIdx.x % G, r = threadIdx.x / G;
+    rm[r * 16 + row] = cluster.map_shared_rank(cta_m, r)[row];
+    rl[r * 16 + row] = cluster.map_shared_rank(cta_l, r)[row];
+  }
+  __syncthreads();
+  if (int(threadIdx.x) < G) {
+    const int row = threadIdx.x;
+    float M = kNegInf;
+    for (int r = 0; r < nsplit; ++r) M = fmaxf(M, rm[r * 16 + row]);
+    float L = 0.f;
+    for (int r = 0; r < nsplit; ++r) {
+      const float mr = rm[r * 16 + row];
+      const float f = (mr == kNegInf) ? 0.f : expf(mr - M);
+      rf[r * 16 + row] = f;
+      L += rl[r * 16 + row] * f;
+    }
+    rL[row] = L;
+  }
+  __syncthreads();
+  {
+    const int total = G * D;
+    const int chunk = (total + nsplit - 1) / nsplit;
+    const int i0 = rank * chunk, i1 = min(total, i0 + chunk);
     char* ob = a.out + int64_t(b) * a.out_stride_b;
-    for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
       const int row = i / D, d = i - row * D;
-      float M = kNegInf;
-      for (int r = 0; r < nsplit; ++r) M = fmaxf(M, cluster.map_shared_rank(cta_m, r)[row]);
-      float L = 0.f, O = 0.f;
-      if (M != kNegInf) {
-        for (int r = 0; r < nsplit; ++r) {
-          const float mr = cluster.map_shared_rank(cta_m, r)[row];
-          if (mr == kNegInf) continue;
-          const float f = expf(mr - M);
-          L += cluster.map_shared_rank(cta_l, r)[row] * f;
-          O += cluster.map_shared_rank(cta_o, r)[row * D + d] * f;
-        }
-      }
+      float O = 0.f;
+      for (int r = 0; r < nsplit; ++r) O += cluster.map_shared_rank(cta_o, r)[row * D + d] * rf[r * 16 + row];
+      const float L = rL[row];
       store_elem(ob + int64_t(hk * G + row) * a.out_stride_h + d * 2, DT, L > 0.f ? O / L : 0.f);
     }
   }
-  cluster.sync();  // keep every CTA's shared memory alive until rank 0 has read it
+  cluster.sync();  // keep every CTA's shared memory alive until all ranks have read it
 }
 
 // ---------------------------------------------------------------------------
@@ -571,6 +616,11 @@ AUGUR_KV_EXPORT int augur_kv_paged_decode_attention(
   a.groups = n_q_heads / n_kv_heads;
   a.head_dim = head_dim;
   a.sqrt_d = sqrtf(float(head_dim));
+  {
+    int e = 0;
+    a.scale_exact = frexpf(a.sqrt_d, &e) == 0.5f ? 1 : 0;  // power of two: x * (1/s) == x / s
+    a.inv_sqrt_d = 1.0f / a.sqrt_d;
+  }
   a.out = static_cast<char*>(out);
   a.out_stride_b = out_strides[0] * es;
   a.out_stride_h = out_strides[1] * es;
@@ -589,8 +639,9 @@ AUGUR_KV_EXPORT int augur_kv_paged_decode_attention(
     // split each sequence over a cluster of CTAs: enough CTAs to cover the
     // SMs, at least one 16-token tile per warp, at most 8 (portable clusters)
     const int tiles = (max_seq_len + kTile - 1) / kTile;
-    int nsplit = int((2 * sm_count() + batch * n_kv_heads - 1) / (batch * n_kv_heads));
-    const int by_len = (tiles + kAttnWarps - 1) / kAttnWarps;
+    const int64_t units = int64_t(batch) * n_kv_heads;
+    int nsplit = int((4 * int64_t(sm_count()) + units - 1) / units);  // about 4 CTAs per SM
+    const int by_len = (tiles + kAttnWarps - 1) / kAttnWarps;            // at least one tile per warp
     if (nsplit > by_len) nsplit = by_len;
     if (nsplit > 8) nsplit = 8;
     if (nsplit < 1) nsplit = 1;

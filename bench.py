@@ -387,7 +387,54 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
     return line
 
 
-def run_extras(device, handoff_only: bool = False) -> dict:
+def bench_decode_attention(device, pool, tables) -> dict:
+    """paged_decode_attention for every layer of one decode step, graph-captured, L2 cold.
+
+    Algorithmic bytes: every cached K and V row of every sequence read once
+    (24 layers x sum(seq_len) x 512 B) plus the queries and outputs.
+    """
+    from augur_b200.attention import DecodeTables, paged_decode_attention
+
+    B = len(tables)
+    Hq = 14
+    dt = DecodeTables(tables, device)
+    g = torch.Generator(device=device).manual_seed(5)
+    qs = torch.randn(L, B, Hq, D, generator=g, device=device).to(torch.bfloat16)
+    outs = torch.empty_like(qs)
+
+    def step() -> None:
+        for layer in range(L):
+            paged_decode_attention(qs[layer], pool, layer, dt, out=outs[layer])
+
+    step()
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream(device)
+    cs.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.graph(graph, stream=cs):
+        step()
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    times = []
+    for _ in range(7):
+        flush.fill_(1)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        graph.replay()
+        b.record()
+        torch.cuda.synchronize(device)
+        times.append(a.elapsed_time(b))
+    graph.reset()
+    ms = statistics.median(times[2:])
+    tokens = int(sum(t.seq_len for t in tables))
+    kv_bytes = L * tokens * TOKEN_LAYER_BYTES + 2 * qs.numel() * 2
+    peak, kind = load_peaks()
+    gbs = kv_bytes / (ms / 1e3) / 1e9
+    return {"us_per_step_all_layers": round(ms * 1e3, 2), "us_per_layer": round(ms * 1e3 / L, 2),
+            "seqs": B, "cached_tokens": tokens, "GBps": round(gbs, 1), "frac_of_hbm_peak": round(gbs / peak, 4),
+            "kernel": "attn_decode_mma_kernel<bf16,64>", "timed": "CUDA graph of 24 per-layer launches, L2 flushed"}
+
+
+def run_extras(device, handoff_only: bool = False, attention_only: bool = False) -> dict:
     """Config 3 handoff + decode append and config 4 fork/COW, timed with CUDA events."""
     import augur_b200 as ab
     from augur_b200 import _lib, _ops, batched
@@ -462,6 +509,12 @@ def run_extras(device, handoff_only: bool = False) -> dict:
                             "timed": "one CUDA graph of 256 append launches"}
     graph.reset()
     del src, nk, nv
+
+    # ---- decode attention reading the pool in place: one decode step of the
+    # 32 sequences (each n + 256 tokens long now) across all 24 layers
+    out["decode_attention"] = bench_decode_attention(device, pool, tables)
+    if attention_only:
+        return out
 
     # ---- config 4: 1000-token prefix (62 full blocks + 8 rows) forked 256 ways, COW, 128-token suffix
     for prefix_len in (1024, 1000):
@@ -753,6 +806,8 @@ def main() -> None:
     ap.add_argument("--skip-extras", action="store_true")
     ap.add_argument("--small", action="store_true", help="profiling case: 8192-block pool, no extras/CPU")
     ap.add_argument("--handoff-only", action="store_true", help="profiling case: config-3 handoff only")
+    ap.add_argument("--attention-only", action="store_true",
+                    help="profiling case: config-3 cache, then decode attention over all layers")
     ap.add_argument("--workload", choices=["scatter", "disagg", "box"], default="scatter",
                     help="scatter: headline (config 2); disagg: NVLink block push between rank pairs; "
                          "box: config 5, 2048 sequences sharded over the ranks (strong scaling)")
@@ -765,6 +820,10 @@ def main() -> None:
     if args.handoff_only:  # profiling case: only the config-3 handoff (about 3 GB on the device)
         torch.cuda.set_device(0)
         emit(run_extras(torch.device("cuda", 0), handoff_only=True))
+        return
+    if args.attention_only:  # profiling case: config-3 handoff + appends, then decode attention
+        torch.cuda.set_device(0)
+        emit(run_extras(torch.device("cuda", 0), attention_only=True))
         return
     world, rank, local = dist_env()
     if args.impl == "reference":
