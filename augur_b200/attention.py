@@ -24,6 +24,29 @@ from . import _lib, _ops
 from .paged_kv_cache import PagedKVCache, SequenceBlockTable
 
 
+# Zero-initialised workspaces of the split kernel, one per (device, stream):
+# launches on one stream run in order, so they can share one.
+_workspaces: dict[tuple[int, int], Tensor] = {}
+
+
+def _workspace(lib, device: torch.device, st: torch.cuda.Stream, sizes: tuple) -> tuple[int, int, Tensor | None]:
+    """(pointer, bytes, tensor) of a workspace large enough for these sizes."""
+    need = int(lib.augur_kv_paged_decode_attention_workspace(*sizes))
+    if need < 0:
+        _lib.check(_lib.EINVAL, "augur_kv_paged_decode_attention_workspace")
+    if need == 0:
+        return 0, 0, None
+    key = (device.index, st.cuda_stream)
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < need:
+        with torch.cuda.stream(st):
+            ws = torch.zeros(need, dtype=torch.uint8, device=device)
+        if not torch.cuda.is_current_stream_capturing():
+            # memory allocated during a graph capture belongs to that graph
+            _workspaces[key] = ws
+    return ws.data_ptr(), ws.numel(), ws
+
+
 class DecodeTables:
     """Device copy of a batch's block tables and lengths, reusable across layers.
 
@@ -104,18 +127,20 @@ def paged_decode_attention(
     lib = _lib.load()
     device = kc.device
     st = stream if stream is not None else torch.cuda.current_stream(device)
+    flags = _lib.ATTN_GENERIC if generic else _lib.ATTN_AUTO
+    dcode = _ops.dtype_code(q3)
     with _ops._DeviceGuard(device):
+        ws_ptr, ws_bytes, ws = _workspace(lib, device, st, (B, Hq, Hkv, D, dt.max_seq_len, dcode, flags))
         code = lib.augur_kv_paged_decode_attention(
             q3.data_ptr(), _lib.i64_array((q3.stride(0), q3.stride(1))),
             kc.data_ptr(), vc.data_ptr(), _lib.i64_array((kc.stride(0), kc.stride(1), kc.stride(2))),
             NB, bs, dt.blocks.data_ptr(), dt.blocks.stride(0), dt.blocks.shape[1],
-            dt.lens.data_ptr(), dt.max_seq_len, B, Hq, Hkv, D, _ops.dtype_code(q3),
-            out3.data_ptr(), _lib.i64_array((out3.stride(0), out3.stride(1))),
-            _lib.ATTN_GENERIC if generic else _lib.ATTN_AUTO,
-            _ops.status_word(device).data_ptr(), st.cuda_stream)
+            dt.lens.data_ptr(), dt.max_seq_len, B, Hq, Hkv, D, dcode,
+            out3.data_ptr(), _lib.i64_array((out3.stride(0), out3.stride(1))), flags,
+            ws_ptr, ws_bytes, _ops.status_word(device).data_ptr(), st.cuda_stream)
     _lib.check(code, "augur_kv_paged_decode_attention")
     _ops.launch_count += 1
-    _ops.keep_until_done(st, q3, dt.blocks, dt.lens)
+    _ops.keep_until_done(st, q3, dt.blocks, dt.lens, *([ws] if ws is not None else []))
     if out is not None:
         return out
     return out3.unsqueeze(2) if squeeze else out3

@@ -7,14 +7,17 @@
 // softmax (augur/attention.py:72-86). Here one launch covers every sequence
 // of the batch for one layer, reading each K/V row of the pool once:
 //
-//  * attn_decode_mma_kernel (bf16 / fp16, head_dim 64 or 128, <= 16 query
-//    heads per KV head): one cluster of up to 8 CTAs per (sequence, KV head)
-//    splits the sequence; each warp walks 16-token tiles staged in shared
-//    memory with cp.async, computes the group's scores and the P.V product
-//    with mma.sync m16n8k16 (the group's query heads are the 16 rows, the
-//    tile's tokens the columns), and keeps an online softmax. Warps combine
-//    in shared memory, CTAs of the cluster through distributed shared memory
-//    into rank 0, which writes the output; no global scratch.
+//  * attn_decode_split_kernel (bf16 / fp16, head_dim 64 or 128, <= 16 query
+//    heads per KV head): sequences are cut into chunks of equal size (a
+//    multiple of warps x 32 tokens) that each CTA derives on the device from
+//    seq_lens so the work items, (sequence, KV head, chunk) triples numbered
+//    in order, fill the grid of resident CTAs once; one item per CTA. Each
+//    warp stages 32 tokens of K and V in shared memory with cp.async and
+//    runs both products transposed on mma.sync m16n8k16 (tokens, not the
+//    few query heads of a group, fill the 16 rows) around an online softmax.
+//    Chunks of one sequence combine through a caller-provided workspace: the
+//    last CTA to arrive (an atomic counter; no CTA ever waits) merges the
+//    partials and writes the output.
 //  * attn_decode_generic_kernel (any dtype / shape): one CTA per (sequence,
 //    query head), scores of the whole sequence in shared memory, then the
 //    reference's order of operations: max, exp, sum, normalise, P.V.
@@ -22,14 +25,17 @@
 // Rounding follows the reference where it rounds: scores are rounded to the
 // cache dtype after q.k and again after the division by sqrt(head_dim)
 // (the bf16/fp16 matmul output and the scalar division both produce the
-// dtype); probabilities are rounded before the product with V; the output
-// is rounded once. Summation order differs, so results agree within a
-// floating-point tolerance, not bit for bit.
+// dtype; for bf16 with sqrt(head_dim) a power of two the division is an
+// exact scaling of a bf16 value, so the second rounding changes nothing and
+// the split kernel skips it); probabilities are rounded before the product
+// with V; the output is rounded once. The split kernel evaluates exp as
+// 2^(x log2 e) with the ex2.approx instruction (relative error about 2^-22,
+// far below the bf16/fp16 rounding that follows). Summation order differs,
+// so results agree within a floating-point tolerance, not bit for bit.
 //
 // The decode query sits at the last position of its sequence, so the causal
 // mask hides nothing; tokens at or past seq_len are never read.
 
-#include <cooperative_groups.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -37,10 +43,10 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <algorithm>
+
 #include "augur_kv.h"
 #include "common.cuh"
-
-namespace cg = cooperative_groups;
 
 namespace augur_kv_dev {
 
@@ -63,7 +69,14 @@ struct AttnArgs {
   char* out;
   int64_t out_stride_b, out_stride_h;  // bytes
   int32_t dtype;
-  int32_t max_seq;  // generic kernel: shared-memory score capacity
+  int32_t max_seq;   // max_seq_len: bound on seq_lens (generic kernel: score capacity)
+  int32_t bs_shift;  // log2(block_size) when it is a power of two, else -1
+  // split kernel
+  int32_t chunk;  // tokens per chunk, a multiple of 128
+  int32_t nch;    // chunk slots per (sequence, KV head) in the workspace
+  int32_t* ws_cnt;
+  float* ws_ml;
+  float* ws_o;
   int32_t* status;
 };
 
@@ -178,236 +191,457 @@ __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-constexpr int kAttnWarps = 4;
-constexpr int kTile = 16;  // tokens per tile
+constexpr int kStageTok = 32;       // tokens a warp stages and processes at a time
+constexpr int kMaxChunks = 256;     // chunks per (sequence, KV head)
+constexpr int kMaxSeq = 1 << 30;    // longest sequence a launch accepts
 
+// Launch shape of the split kernel for one head_dim: warps per CTA, one
+// 32-token stage buffer (K and V rows, padded so ldmatrix rows hit distinct
+// banks) per warp; chunks are multiples of warps x 32 tokens.
 template <int D>
-struct MmaSmem {
-  static constexpr int kStages = 3;             // tiles in flight per warp
-  static constexpr int kRowBytes = D * 2 + 16;  // padded: ldmatrix rows hit distinct banks
-  static constexpr int kTileBytes = kTile * kRowBytes;
-  static constexpr int kPipe = kAttnWarps * kStages * 2 /*K,V*/ * kTileBytes;
-  // after the token loop the warps' partial results reuse the pipeline buffers
-  static constexpr int kPartO = kAttnWarps * 16 * D * 4;
-  static constexpr int kPartML = kAttnWarps * 16 * 4;
-  static_assert(kPartO + 2 * kPartML <= kPipe, "partials must fit in the pipeline buffers");
-  static constexpr int kCtaO = 16 * D * 4;
-  static constexpr int kBytes = kPipe + kCtaO + (2 * 16 + kAttnWarps * 16 + 3 * 8 * 16 + 16) * 4;
+struct SplitCfg {
+  static constexpr int kWarps = D == 64 ? 8 : 4;
+  static constexpr int kThreads = kWarps * 32;
+  static constexpr int kChunkUnit = kWarps * kStageTok;
+  static constexpr int kRowBytes = D * 2 + 16;
+  static constexpr int kStageBytes = kStageTok * kRowBytes;  // K or V of one stage
+  static constexpr int kWarpStage = 2 * kStageBytes;
+  static constexpr int kPipe = kWarps * kWarpStage;
+  // after the token loop the warps' partial results reuse the stage buffers
+  static constexpr int kPO = D + 4;  // floats per partial row: the transposing stores hit distinct banks
+  static constexpr int kPartO = kWarps * 16 * kPO * 4;
+  static constexpr int kPartML = kWarps * 16 * 4;
+  static_assert(kPartO + 2 * kPartML <= kPipe, "partials must fit in the stage buffers");
+  static_assert(2 * kMaxChunks * 16 * 4 <= kPipe, "chunk maxima and sums must fit in the stage buffers");
+  static constexpr int kTail = (kWarps * 16 + 16 + 16 + 8) * 4;  // fac, cta_m, cta_l, flag, item
+  static constexpr int kBytes = kPipe + kTail;
 };
 
-template <typename T, int D>
-__global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_mma_kernel(AttnArgs a) {
-  using SM = MmaSmem<D>;
-  constexpr int CHUNKS = D * 2 / 16;  // 16-byte pieces per row
+__device__ __forceinline__ float ex2(float x) {  // 2^x; ex2(-inf) = 0
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// atomicAdd with acquire-release semantics at GPU scope; returns the old value.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int32_t* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+// Transpose an 8x8 matrix of 16-bit values held as the mma fragment layout.
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+// Round two floats to the cache dtype and back (what a tensor of that dtype holds).
+template <typename T>
+__device__ __forceinline__ float2 round2(float x, float y);
+template <>
+__device__ __forceinline__ float2 round2<__nv_bfloat16>(float x, float y) {
+  return __bfloat1622float2(__floats2bfloat162_rn(x, y));
+}
+template <>
+__device__ __forceinline__ float2 round2<__half>(float x, float y) {
+  return __half22float2(__floats2half2_rn(x, y));
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ int warp_sum(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// C is a power of two (a power-of-two chunk unit times 2^j)
+__device__ __forceinline__ int chunks_of(int S, int C) { return max(1, (S + C - 1) >> (__ffs(C) - 1)); }
+
+// Work items are (sequence, KV head, chunk) triples numbered sequence-major,
+// then KV head, then chunk, so the chunks of one (sequence, KV head) are
+// consecutive. Every CTA (each warp on its own, no shared state) derives the
+// same plan from seq_lens: the smallest chunk size C = a.chunk * 2^j for
+// which the items fit in the grid (one wave when the host sized the grid to
+// the resident CTAs), or C >= max_seq_len (one chunk per sequence).
+struct Plan {
+  int C, total;
+};
+
+__device__ __forceinline__ int seq_len_at(const AttnArgs& a, int b) {
+  return min(max(0, __ldg(a.seq_lens + b)), a.max_seq);
+}
+
+__device__ Plan make_plan(const AttnArgs& a, int lane) {
+  Plan p;
+  p.C = a.chunk;
+  const int64_t units = int64_t(a.batch) * a.hkv;
+  if (units >= int64_t(gridDim.x) || p.C >= a.max_seq) {  // one chunk per sequence
+    p.C = max(p.C, a.max_seq);
+    p.total = int(units);
+    return p;
+  }
+  for (;;) {
+    int cnt = 0;
+    for (int b = lane; b < a.batch; b += 32) cnt += chunks_of(seq_len_at(a, b), p.C);
+    p.total = warp_sum(cnt) * a.hkv;
+    if (p.total <= int(gridDim.x) || p.C >= a.max_seq) return p;
+    p.C *= 2;
+  }
+}
+
+struct Item {
+  int b, hk, chunk, nch, first;  // first: item number of chunk 0 of (b, hk)
+};
+
+__device__ Item locate(const AttnArgs& a, const Plan& p, int item, int lane) {
+  Item it;
+  if (p.C >= a.max_seq) {  // every sequence is one chunk
+    it.b = item / a.hkv;
+    it.hk = item - it.b * a.hkv;
+    it.chunk = 0;
+    it.nch = 1;
+    it.first = item;
+    return it;
+  }
+  int run = 0;  // items of the sequences before this group of 32
+  for (int b0 = 0;; b0 += 32) {
+    const int b = b0 + lane;
+    const int c = b < a.batch ? chunks_of(seq_len_at(a, b), p.C) * a.hkv : 0;
+    int incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const unsigned hit = __ballot_sync(0xffffffffu, c > 0 && item >= run + incl - c && item < run + incl);
+    if (hit != 0u) {
+      const int src = __ffs(hit) - 1;
+      const int base = run + __shfl_sync(0xffffffffu, incl - c, src);
+      it.nch = __shfl_sync(0xffffffffu, c, src) / a.hkv;
+      it.b = b0 + src;
+      const int rel = item - base;
+      it.hk = rel / it.nch;
+      it.chunk = rel - it.hk * it.nch;
+      it.first = base + it.hk * it.nch;
+      return it;
+    }
+    run += __shfl_sync(0xffffffffu, incl, 31);
+  }
+}
+
+// One work item per CTA: a chunk of C tokens of one (sequence, KV head).
+// Each warp takes every kWarps-th 32-token stage of the chunk and stages its
+// K and V rows in shared memory with cp.async (one block-table entry per lane
+// per stage, shared by shuffle). Both products run transposed on mma.sync
+// m16n8k16 so the stage's tokens, not the few query heads of the group, fill
+// the 16 rows: S^T = K Q^T (16 tokens x 8 heads per tile), then, after an
+// online softmax in base 2 on the columns, O^T += V^T P^T (16 dims x 8 heads)
+// with P^T moved into the B-operand layout by movmatrix. NT = 1 serves up to
+// 8 query heads per KV head, NT = 2 up to 16. Warps combine in shared memory.
+// A sequence of one chunk writes its output directly; otherwise each CTA
+// writes its unnormalised partial (o, m, l) to the workspace slot of its item
+// and the last CTA of the (sequence, KV head) to arrive (atomic counter, no
+// waiting) combines them and resets the counter.
+template <typename T, int D, int NT>
+__global__ void __launch_bounds__(SplitCfg<D>::kThreads, (D == 64 && NT == 1) ? 3 : 1)
+    attn_decode_split_kernel(AttnArgs a) {
+  using CF = SplitCfg<D>;
+  constexpr int W = CF::kWarps;
   constexpr int DT = MmaType<T>::dtype;
+  constexpr int PARTS = D * 2 / 16;         // 16-byte pieces per row
+  constexpr int ROW_STEP = 32 / PARTS;      // row distance between a lane's rows
+  constexpr int RPL = kStageTok / ROW_STEP; // rows per lane per stage
+  constexpr int PO = CF::kPO;
   extern __shared__ __align__(128) unsigned char smem[];
-  float* part_o = reinterpret_cast<float*>(smem);  // aliases the pipeline after the loop
-  float* part_m = reinterpret_cast<float*>(smem + SM::kPartO);
-  float* part_l = part_m + kAttnWarps * 16;
-  float* cta_o = reinterpret_cast<float*>(smem + SM::kPipe);
-  float* cta_m = cta_o + 16 * D;
+  float* part_o = reinterpret_cast<float*>(smem);  // [warp][16 heads][PO], aliases the stage buffers
+  float* part_m = reinterpret_cast<float*>(smem + CF::kPartO);
+  float* part_l = part_m + W * 16;
+  float* fac = reinterpret_cast<float*>(smem + CF::kPipe);  // [warps][16]
+  float* cta_m = fac + W * 16;
   float* cta_l = cta_m + 16;
-  float* fac = cta_l + 16;            // [warps][16] rescale factors
-  float* rm = fac + kAttnWarps * 16;  // [8 ranks][16] gathered row maxima
-  float* rl = rm + 8 * 16;            // [8][16] gathered row sums
-  float* rf = rl + 8 * 16;            // [8][16] rescale factors per rank
-  float* rL = rf + 8 * 16;            // [16] combined row sums
+  int* last_flag = reinterpret_cast<int*>(cta_l + 16);
 
-  cg::cluster_group cluster = cg::this_cluster();
-  const int rank = int(cluster.block_rank());
-  const int nsplit = int(cluster.num_blocks());
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int hk = blockIdx.y, b = blockIdx.z;
+  // Launched as a programmatic dependent of the previous kernel on the
+  // stream: wait for it to finish (its writes visible) before reading inputs.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // warp 0 plans and finds this CTA's item; the others read it from shared memory
+  int* shared_item = last_flag + 1;  // [6]: C, b, hk, chunk, nch, first (b = -1: no item)
+  if (warp == 0) {
+    const Plan pl = make_plan(a, lane);
+    if (lane == 0) shared_item[1] = -1;
+    if (int(blockIdx.x) < pl.total) {
+      const Item itm = locate(a, pl, blockIdx.x, lane);
+      if (lane == 0) {
+        shared_item[0] = pl.C;
+        shared_item[1] = itm.b;
+        shared_item[2] = itm.hk;
+        shared_item[3] = itm.chunk;
+        shared_item[4] = itm.nch;
+        shared_item[5] = itm.first;
+      }
+    }
+  }
+  __syncthreads();
+  if (shared_item[1] < 0) return;
+  const int plan_C = shared_item[0], b = shared_item[1], hk = shared_item[2], chunk = shared_item[3];
+  const int my_nch = shared_item[4], item_first = shared_item[5];
+  const int S = seq_len_at(a, b);
+  if (chunk == 0 && threadIdx.x == 0 && __ldg(a.seq_lens + b) > a.max_seq)
+    record_status(a.status, AUGUR_KV_EBOUNDS);  // the host sized the launch with max_seq_len
+  const int tok0 = chunk * plan_C, tok1 = min(S, tok0 + plan_C);
   const int G = a.groups;
-  const int S = max(0, __ldg(a.seq_lens + b));
 
-  const int tiles = (S + kTile - 1) / kTile;
-  const int per_cta = (tiles + nsplit - 1) / nsplit;
-  const int tile0 = rank * per_cta;
-  const int tile1 = min(tiles, tile0 + per_cta);
-
-  // Query rows of this KV head's group as mma A fragments (rows >= G are 0).
-  uint32_t qa[D / 16][4];
+  // Q^T as mma B fragments: b0 = Q[head nt*8+g][dims ks*16+2t, +1], b1 the
+  // same 8 dims further (heads >= G are 0).
+  uint32_t qb[D / 16][NT][2];
   {
-    const char* qb = a.q + int64_t(b) * a.q_stride_b;
+    const char* qbase = a.q + int64_t(b) * a.q_stride_b;
 #pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks) {
+    for (int nt = 0; nt < NT; ++nt) {
+      const int head = nt * 8 + g;
+      const char* qrow = qbase + int64_t(hk * G + head) * a.q_stride_h;
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int row = g + ((r & 1) ? 8 : 0);
-        const int col = ks * 16 + 2 * t + ((r & 2) ? 8 : 0);
-        uint32_t v = 0;
-        if (row < G) v = *reinterpret_cast<const uint32_t*>(qb + int64_t(hk * G + row) * a.q_stride_h + col * 2);
-        qa[ks][r] = v;
+      for (int ks = 0; ks < D / 16; ++ks) {
+        uint32_t v0 = 0, v1 = 0;
+        if (head < G) {
+          v0 = *reinterpret_cast<const uint32_t*>(qrow + (ks * 16 + 2 * t) * 2);
+          v1 = *reinterpret_cast<const uint32_t*>(qrow + (ks * 16 + 8 + 2 * t) * 2);
+        }
+        qb[ks][nt][0] = v0;
+        qb[ks][nt][1] = v1;
       }
     }
   }
 
-  float o[D / 8][4];
+  // O^T accumulators: o[dm][nt] = O^T[dims dm*16 + g (+8)][heads nt*8 + 2t (+1)]
+  float o[D / 16][NT][4];
 #pragma unroll
-  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float mrow[2] = {kNegInf, kNegInf}, lrow[2] = {0.f, 0.f};
+  for (int i = 0; i < D / 16; ++i)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) o[i][nt][0] = o[i][nt][1] = o[i][nt][2] = o[i][nt][3] = 0.f;
+  // base-2 running max and lane-partial sums of the lane's two head columns per n-tile
+  float mrow[NT][2], lrow[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) mrow[nt][0] = mrow[nt][1] = kNegInf, lrow[nt][0] = lrow[nt][1] = 0.f;
 
-  constexpr int NST = SM::kStages;
-  unsigned char* wbuf = smem + warp * (NST * 2 * SM::kTileBytes);
-  // Each lane copies a fixed 16-byte column (part) of RPL rows of every
-  // tile, for K and V alike: one table lookup per row serves both.
-  constexpr int RPL = CHUNKS / 2;           // rows per lane per tile
-  constexpr int ROW_STEP = 32 / CHUNKS;     // row distance between a lane's rows
-  const int part = lane % CHUNKS;
-  const int row_base = lane / CHUNKS;
-  auto load_tile = [&](int tile, int st) {
-    unsigned char* kdst = wbuf + (st * 2 + 0) * SM::kTileBytes + part * 16;
-    unsigned char* vdst = wbuf + (st * 2 + 1) * SM::kTileBytes + part * 16;
+  unsigned char* wbuf = smem + warp * CF::kWarpStage;
+  const int part = lane % PARTS, row0 = lane / PARTS;
+  const int64_t lane_off = int64_t(hk) * a.head_stride + part * 16;
+  const int32_t* tbl = a.tables + int64_t(b) * a.tables_stride;
+  const int shift = a.bs_shift;
+  // Stage tokens [s0, s0 + 32): lane l reads the table entry of the stage's
+  // l-th logical block (a stage spans at most 32 blocks).
+  auto load_stage = [&](int s0) {
+    const int last = min(tok1, s0 + kStageTok) - 1;
+    const int lb_first = shift >= 0 ? (s0 >> shift) : s0 / a.block_size;
+    const int lb_last = shift >= 0 ? (last >> shift) : last / a.block_size;
+    int my_blk = -1;
+    if (lb_first + lane <= lb_last && lb_first + lane < a.max_blocks) my_blk = __ldg(tbl + lb_first + lane);
+    unsigned char* kdst = wbuf + part * 16;
+    unsigned char* vdst = kdst + CF::kStageBytes;
 #pragma unroll
     for (int i = 0; i < RPL; ++i) {
-      const int r = row_base + i * ROW_STEP;
-      const int pos = tile * kTile + r;
+      const int r = row0 + i * ROW_STEP;
+      const int pos = s0 + r;
+      int lb, off;
+      if (shift >= 0) {
+        lb = pos >> shift;
+        off = pos & (a.block_size - 1);
+      } else {
+        lb = pos / a.block_size;
+        off = pos - lb * a.block_size;
+      }
+      const int blk = __shfl_sync(0xffffffffu, my_blk, (lb - lb_first) & 31);
       const char* kp = a.k;
       const char* vp = a.v;
       int bytes = 0;
-      if (pos < S) {
-        const char* rk = row_addr(a, a.k, b, hk, pos);
-        if (rk != nullptr) {
-          kp = rk + part * 16;
-          vp = a.v + (rk - a.k) + part * 16;
+      if (pos < tok1) {
+        if (blk >= 0 && blk < a.num_blocks) {
+          const int64_t ofs = int64_t(blk) * a.blk_stride + lane_off + int64_t(off) * a.row_stride;
+          kp += ofs;
+          vp += ofs;
           bytes = 16;
+        } else {
+          record_status(a.status, AUGUR_KV_EBOUNDS);  // reads as zeros
         }
       }
-      cp_async16(kdst + r * SM::kRowBytes, kp, bytes);
-      cp_async16(vdst + r * SM::kRowBytes, vp, bytes);
+      cp_async16(kdst + r * CF::kRowBytes, kp, bytes);
+      cp_async16(vdst + r * CF::kRowBytes, vp, bytes);
     }
     cp_async_commit();
   };
 
-  const int my_first = tile0 + warp;
-  const int n_my = my_first < tile1 ? (tile1 - my_first + kAttnWarps - 1) / kAttnWarps : 0;
-#pragma unroll
-  for (int i = 0; i < NST - 1; ++i) {
-    if (i < n_my) load_tile(my_first + i * kAttnWarps, i);
-    else cp_async_commit();
-  }
+  // warp w takes stages w, w + W, w + 2W, ... of the chunk
+  const int n_stages = (tok1 - tok0 + kStageTok - 1) / kStageTok;
+  const int n_my = warp < n_stages ? (n_stages - warp + W - 1) / W : 0;
+  const bool round_twice = DT == AUGUR_KV_F16 || !a.scale_exact;
+  // scores to base 2: one multiply when no second rounding sits between the
+  // division by sqrt(head_dim) and the change of base
+  const float scale1 = round_twice ? (a.scale_exact ? a.inv_sqrt_d : 1.f) : a.inv_sqrt_d * kLog2e;
+  const int mat = lane >> 3, r8 = lane & 7;
+  if (n_my > 0) load_stage(tok0 + warp * kStageTok);
+  // every load of the first stage is issued: the next kernel may start launching
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   for (int it = 0; it < n_my; ++it) {
-    const int nxt = it + NST - 1;
-    if (nxt < n_my) load_tile(my_first + nxt * kAttnWarps, nxt % NST);
-    else cp_async_commit();
-    cp_async_wait<NST - 1>();
+    const int s0 = tok0 + (warp + it * W) * kStageTok;
+    cp_async_wait<0>();
     __syncwarp();
-    const int tile = my_first + it * kAttnWarps;
-    const int stage = it % NST;
-    const unsigned char* Ks = wbuf + (stage * 2 + 0) * SM::kTileBytes;
-    const unsigned char* Vs = wbuf + (stage * 2 + 1) * SM::kTileBytes;
+    const unsigned char* Ks = wbuf;
+    const unsigned char* Vs = wbuf + CF::kStageBytes;
 
-    // scores: 16 query rows x 16 tokens, two n8 tiles
-    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    {
-      const int mat = lane >> 3, r8 = lane & 7;
-      const int tok = (mat >> 1) * 8 + r8;
+    // S^T: two 16-token row tiles x NT 8-head column tiles
+    float s[2][NT][4];
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) s[mt][nt][0] = s[mt][nt][1] = s[mt][nt][2] = s[mt][nt][3] = 0.f;
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      const int tok = mt * 16 + (mat & 1) * 8 + r8;
 #pragma unroll
       for (int ks = 0; ks < D / 16; ++ks) {
-        uint32_t bk[4];
-        ldmatrix_x4(bk, Ks + tok * SM::kRowBytes + (ks * 16 + (mat & 1) * 8) * 2);
-        mma16816<T>(s[0], qa[ks], bk[0], bk[1]);
-        mma16816<T>(s[1], qa[ks], bk[2], bk[3]);
+        uint32_t ka[4];
+        ldmatrix_x4(ka, Ks + tok * CF::kRowBytes + (ks * 16 + (mat >> 1) * 8) * 2);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma16816<T>(s[mt][nt], ka, qb[ks][nt][0], qb[ks][nt][1]);
       }
     }
-    // round as the reference's dtype matmul and scalar division do; mask the tail
+    // round as the reference's dtype matmul and scalar division do, move to
+    // base 2, mask the tail of the last stage (rows are tokens)
+    const bool full = s0 + kStageTok <= tok1;
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
+    for (int mt = 0; mt < 2; ++mt) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int pos = tile * kTile + nt * 8 + 2 * t + (j & 1);
-        const float r = round_to(s[nt][j], DT);
-        float x = round_to(a.scale_exact ? r * a.inv_sqrt_d : r / a.sqrt_d, DT);
-        s[nt][j] = pos < S ? x : kNegInf;
+      for (int hp = 0; hp < 2; ++hp) {
+        const bool dead = !full && s0 + mt * 16 + hp * 8 + g >= tok1;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          float2 r = round2<T>(s[mt][nt][2 * hp], s[mt][nt][2 * hp + 1]);
+          float x0, x1;
+          if (round_twice) {
+            if (!a.scale_exact) {
+              r.x /= a.sqrt_d;
+              r.y /= a.sqrt_d;
+            } else {
+              r.x *= scale1;
+              r.y *= scale1;
+            }
+            r = round2<T>(r.x, r.y);
+            x0 = r.x * kLog2e;
+            x1 = r.y * kLog2e;
+          } else {
+            x0 = r.x * scale1;
+            x1 = r.y * scale1;
+          }
+          s[mt][nt][2 * hp] = dead ? kNegInf : x0;
+          s[mt][nt][2 * hp + 1] = dead ? kNegInf : x1;
+        }
       }
     }
-    float mx[2];
-    mx[0] = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
-    mx[1] = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
+    // column (head) maxima over the stage's 32 tokens: this lane's 4, then the 8 g-lanes
+    float mnew[NT][2];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
-      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
-    }
-    float alpha[2], mnew[2], sum[2] = {0.f, 0.f};
+    for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      mnew[h] = fmaxf(mrow[h], mx[h]);
-      alpha[h] = (mrow[h] == kNegInf) ? 0.f : expf(mrow[h] - mnew[h]);
-    }
-    float p[2][4];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int h = j >> 1;
-        const float e = (s[nt][j] == kNegInf) ? 0.f : expf(s[nt][j] - mnew[h]);
-        p[nt][j] = e;
-        sum[h] += e;
+      for (int j = 0; j < 2; ++j) {
+        float m = fmaxf(fmaxf(s[0][nt][j], s[0][nt][2 + j]), fmaxf(s[1][nt][j], s[1][nt][2 + j]));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+        mnew[nt][j] = fmaxf(mrow[nt][j], m);  // finite: every stage holds a valid token
       }
     }
+    if (it > 0) {
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 1);
-      sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 2);
-      lrow[h] = lrow[h] * alpha[h] + sum[h];
-      mrow[h] = mnew[h];
-    }
+      for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-    for (int i = 0; i < D / 8; ++i) {
-      o[i][0] *= alpha[0];
-      o[i][1] *= alpha[0];
-      o[i][2] *= alpha[1];
-      o[i][3] *= alpha[1];
-    }
-    // P (16 rows x 16 tokens) as the A operand of the P.V product
-    uint32_t pa[4];
-    pa[0] = pack2<T>(p[0][0], p[0][1]);
-    pa[1] = pack2<T>(p[0][2], p[0][3]);
-    pa[2] = pack2<T>(p[1][0], p[1][1]);
-    pa[3] = pack2<T>(p[1][2], p[1][3]);
-    {
-      const int mat = lane >> 3, r8 = lane & 7;
-      const int tok = (mat & 1) * 8 + r8;
+        for (int j = 0; j < 2; ++j) {
+          const float al = ex2(mrow[nt][j] - mnew[nt][j]);
+          lrow[nt][j] *= al;
 #pragma unroll
-      for (int dp = 0; dp < D / 16; ++dp) {
-        uint32_t bv[4];
-        ldmatrix_x4_trans(bv, Vs + tok * SM::kRowBytes + (dp * 16 + (mat >> 1) * 8) * 2);
-        mma16816<T>(o[2 * dp], pa, bv[0], bv[1]);
-        mma16816<T>(o[2 * dp + 1], pa, bv[2], bv[3]);
+          for (int dm = 0; dm < D / 16; ++dm) {
+            o[dm][nt][j] *= al;
+            o[dm][nt][2 + j] *= al;
+          }
+        }
       }
     }
-    __syncwarp();  // every lane is done with this stage before it is refilled
+    // probabilities, rounded to the dtype, as P^T B fragments (movmatrix
+    // turns the [token][head pair] layout of S^T into [head][token pair])
+    uint32_t pb[2][NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      mrow[nt][0] = mnew[nt][0];
+      mrow[nt][1] = mnew[nt][1];
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        const float p0 = ex2(s[mt][nt][0] - mnew[nt][0]), p1 = ex2(s[mt][nt][1] - mnew[nt][1]);
+        const float p2 = ex2(s[mt][nt][2] - mnew[nt][0]), p3 = ex2(s[mt][nt][3] - mnew[nt][1]);
+        lrow[nt][0] += p0 + p2;
+        lrow[nt][1] += p1 + p3;
+        pb[mt][nt][0] = movmatrix_trans(pack2<T>(p0, p1));
+        pb[mt][nt][1] = movmatrix_trans(pack2<T>(p2, p3));
+      }
+    }
+    // O^T += V^T P^T: 16-dim row tiles, 16-token k-steps
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      const int tok = mt * 16 + (mat >> 1) * 8 + r8;
+#pragma unroll
+      for (int dm = 0; dm < D / 16; ++dm) {
+        uint32_t va[4];
+        ldmatrix_x4_trans(va, Vs + tok * CF::kRowBytes + (dm * 16 + (mat & 1) * 8) * 2);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma16816<T>(o[dm][nt], va, pb[mt][nt][0], pb[mt][nt][1]);
+      }
+    }
+    __syncwarp();  // every lane is done with the buffer before it is refilled
+    if (it + 1 < n_my) load_stage(s0 + W * kStageTok);
   }
   cp_async_wait<0>();
-  __syncthreads();  // every warp is done with the pipeline buffers the partials reuse
-
-  // warps -> CTA
 #pragma unroll
-  for (int i = 0; i < D / 8; ++i) {
+  for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int row = g + ((j & 2) ? 8 : 0);
-      part_o[(warp * 16 + row) * D + i * 8 + 2 * t + (j & 1)] = o[i][j];
+    for (int j = 0; j < 2; ++j) {
+      lrow[nt][j] += __shfl_xor_sync(0xffffffffu, lrow[nt][j], 4);
+      lrow[nt][j] += __shfl_xor_sync(0xffffffffu, lrow[nt][j], 8);
+      lrow[nt][j] += __shfl_xor_sync(0xffffffffu, lrow[nt][j], 16);
     }
   }
-  if (t == 0) {
-    part_m[warp * 16 + g] = mrow[0];
-    part_m[warp * 16 + g + 8] = mrow[1];
-    part_l[warp * 16 + g] = lrow[0];
-    part_l[warp * 16 + g + 8] = lrow[1];
+  __syncthreads();  // every warp is done with the stage buffers the partials reuse
+
+  // warps -> CTA: part_o[warp][head][dim] (the stores transpose O^T back)
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int dm = 0; dm < D / 16; ++dm) {
+#pragma unroll
+      for (int f = 0; f < 4; ++f) {
+        const int head = nt * 8 + 2 * t + (f & 1), dim = dm * 16 + g + (f >> 1) * 8;
+        part_o[(warp * 16 + head) * PO + dim] = o[dm][nt][f];
+      }
+    }
+    if (g == 0) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        part_m[warp * 16 + nt * 8 + 2 * t + j] = mrow[nt][j];
+        part_l[warp * 16 + nt * 8 + 2 * t + j] = lrow[nt][j];
+      }
+    }
   }
   __syncthreads();
-  // warps -> CTA: rescale factors once per (warp, row), then the 16 x D sums
   if (int(threadIdx.x) < G) {
     const int row = threadIdx.x;
     float M = kNegInf;
-    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, part_m[w * 16 + row]);
+    for (int w = 0; w < W; ++w) M = fmaxf(M, part_m[w * 16 + row]);
     float L = 0.f;
-    for (int w = 0; w < kAttnWarps; ++w) {
+    for (int w = 0; w < W; ++w) {
       const float mw = part_m[w * 16 + row];
-      const float f = (mw == kNegInf) ? 0.f : expf(mw - M);
+      const float f = mw == kNegInf ? 0.f : ex2(mw - M);
       fac[w * 16 + row] = f;
       L += part_l[w * 16 + row] * f;
     }
@@ -415,50 +649,98 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_mma_kernel(AttnAr
     cta_l[row] = L;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+  const int GD = G * D;
+  char* ob = a.out + int64_t(b) * a.out_stride_b;
+  if (my_nch == 1) {  // the whole sequence is in this CTA
+    for (int i = threadIdx.x; i < GD; i += blockDim.x) {
+      const int row = i / D, d = i - row * D;
+      float O = 0.f;
+#pragma unroll
+      for (int w = 0; w < W; ++w) O += part_o[(w * 16 + row) * PO + d] * fac[w * 16 + row];
+      const float L = cta_l[row];
+      store_elem(ob + int64_t(hk * G + row) * a.out_stride_h + d * 2, DT, L > 0.f ? O / L : 0.f);
+    }
+    return;
+  }
+  // partial of this chunk -> the workspace slot of this item
+  float* wo = a.ws_o + int64_t(item_first) * GD;
+  float* wml = a.ws_ml + int64_t(item_first) * 32;
+  for (int i = threadIdx.x; i < GD; i += blockDim.x) {
     const int row = i / D, d = i - row * D;
     float O = 0.f;
 #pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) O += part_o[(w * 16 + row) * D + d] * fac[w * 16 + row];
-    cta_o[row * D + d] = O;
+    for (int w = 0; w < W; ++w) O += part_o[(w * 16 + row) * PO + d] * fac[w * 16 + row];
+    wo[int64_t(chunk) * GD + i] = O;
   }
-  // CTAs of the cluster, through distributed shared memory: every rank reads
-  // all ranks' (m, l), then combines and writes its own slice of the outputs
-  cluster.sync();
-  if (int(threadIdx.x) < G * nsplit) {
-    const int row = threadIdx.x % G, r = threadIdx.x / G;
-    rm[r * 16 + row] = cluster.map_shared_rank(cta_m, r)[row];
-    rl[r * 16 + row] = cluster.map_shared_rank(cta_l, r)[row];
+  if (int(threadIdx.x) < G) {
+    wml[chunk * 32 + threadIdx.x] = cta_m[threadIdx.x];
+    wml[chunk * 32 + 16 + threadIdx.x] = cta_l[threadIdx.x];
+  }
+  const int64_t unit = int64_t(b) * a.hkv + hk;
+  // One release-acquire increment by thread 0 after the barrier publishes the
+  // whole CTA's partial (barrier then release is cumulative) and, for the
+  // last CTA, makes every other CTA's partial visible to the reads below.
+  __syncthreads();
+  if (threadIdx.x == 0) *last_flag = atom_add_acq_rel_gpu(a.ws_cnt + unit, 1) == my_nch - 1;
+  __syncthreads();
+  if (!*last_flag) return;
+  // last CTA of the (sequence, KV head): combine every chunk's partial. The
+  // row maxima and sums of all chunks and (for up to kCombineRegs chunks)
+  // this thread's partial outputs load together, in one round of requests.
+  constexpr int kPerThread = (NT * 8 * D + CF::kThreads - 1) / CF::kThreads;  // outputs per thread
+  constexpr int kCombineRegs = 32 / kPerThread > 1 ? 32 / kPerThread : 1;     // 32 registers of partials
+  float* cm = reinterpret_cast<float*>(smem);  // [my_nch][16] maxima, then rescale factors
+  float* cl = cm + kMaxChunks * 16;            // [my_nch][16] sums
+  float pv[kPerThread][kCombineRegs];
+  const bool in_regs = my_nch <= kCombineRegs;
+  if (in_regs) {
+#pragma unroll
+    for (int e = 0; e < kPerThread; ++e) {
+      const int i = threadIdx.x + e * CF::kThreads;
+#pragma unroll
+      for (int c = 0; c < kCombineRegs; ++c)
+        pv[e][c] = (i < GD && c < my_nch) ? __ldcg(wo + int64_t(c) * GD + i) : 0.f;
+    }
+  }
+  for (int j = threadIdx.x; j < my_nch * G; j += blockDim.x) {
+    const int c = j / G, row = j - c * G;
+    cm[c * 16 + row] = __ldcg(wml + c * 32 + row);
+    cl[c * 16 + row] = __ldcg(wml + c * 32 + 16 + row);
   }
   __syncthreads();
   if (int(threadIdx.x) < G) {
     const int row = threadIdx.x;
     float M = kNegInf;
-    for (int r = 0; r < nsplit; ++r) M = fmaxf(M, rm[r * 16 + row]);
+    for (int c = 0; c < my_nch; ++c) M = fmaxf(M, cm[c * 16 + row]);
     float L = 0.f;
-    for (int r = 0; r < nsplit; ++r) {
-      const float mr = rm[r * 16 + row];
-      const float f = (mr == kNegInf) ? 0.f : expf(mr - M);
-      rf[r * 16 + row] = f;
-      L += rl[r * 16 + row] * f;
+    for (int c = 0; c < my_nch; ++c) {
+      const float mc = cm[c * 16 + row];
+      const float f = mc == kNegInf ? 0.f : ex2(mc - M);
+      cm[c * 16 + row] = f;
+      L += cl[c * 16 + row] * f;
     }
-    rL[row] = L;
+    cta_l[row] = L;
   }
   __syncthreads();
-  {
-    const int total = G * D;
-    const int chunk = (total + nsplit - 1) / nsplit;
-    const int i0 = rank * chunk, i1 = min(total, i0 + chunk);
-    char* ob = a.out + int64_t(b) * a.out_stride_b;
-    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+#pragma unroll
+  for (int e = 0; e < kPerThread; ++e) {
+    const int i = threadIdx.x + e * CF::kThreads;
+    if (i < GD) {
       const int row = i / D, d = i - row * D;
       float O = 0.f;
-      for (int r = 0; r < nsplit; ++r) O += cluster.map_shared_rank(cta_o, r)[row * D + d] * rf[r * 16 + row];
-      const float L = rL[row];
+      if (in_regs) {
+#pragma unroll
+        for (int c = 0; c < kCombineRegs; ++c)
+          if (c < my_nch) O += pv[e][c] * cm[c * 16 + row];
+      } else {
+#pragma unroll 8
+        for (int c = 0; c < my_nch; ++c) O += __ldcg(wo + int64_t(c) * GD + i) * cm[c * 16 + row];
+      }
+      const float L = cta_l[row];
       store_elem(ob + int64_t(hk * G + row) * a.out_stride_h + d * 2, DT, L > 0.f ? O / L : 0.f);
     }
   }
-  cluster.sync();  // keep every CTA's shared memory alive until all ranks have read it
+  if (threadIdx.x == 0) a.ws_cnt[unit] = 0;  // ready for the next launch
 }
 
 // ---------------------------------------------------------------------------
@@ -538,48 +820,146 @@ using namespace augur_kv_dev;
 
 namespace {
 
-template <typename T, int D>
-int launch_mma(const AttnArgs& a, int nsplit, cudaStream_t st) {
-  using SM = MmaSmem<D>;
-  auto kern = attn_decode_mma_kernel<T, D>;
-  static bool attr_done[kMaxDevices] = {false};
+int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
+
+// Launch shape of the split kernel. The grid is the larger of the resident
+// CTAs (slots) and the (sequence, KV head) units; the kernel picks its chunk
+// size on the device (never below chunk_min) so its work items fit the grid.
+// Partials are indexed by work item (< slots), so the workspace is: one
+// arrival counter per unit, then slots x 32 floats (row maxima and sums),
+// then slots x G x D partial outputs; none when no sequence can split.
+struct SplitPlan {
+  int chunk_min = 0;
+  int64_t grid = 0, cnt_bytes = 0, ml_bytes = 0, ws_bytes = 0;
+};
+
+SplitPlan plan_split(int batch, int hkv, int G, int D, int max_seq, int slots, int unit) {
+  SplitPlan p;
+  int64_t C = unit;
+  while ((int64_t(max_seq) + C - 1) / C > kMaxChunks) C *= 2;
+  p.chunk_min = int(C);
+  const int64_t units = int64_t(batch) * hkv;
+  p.grid = std::max<int64_t>(units, slots);
+  if (units < slots && max_seq > C) {
+    p.cnt_bytes = align256(units * 4);
+    p.ml_bytes = align256(int64_t(slots) * 32 * 4);
+    p.ws_bytes = p.cnt_bytes + p.ml_bytes + int64_t(slots) * G * D * 4;
+  }
+  return p;
+}
+
+bool mma_shape_ok(int dtype, int head_dim, int groups) {
+  return dtype != AUGUR_KV_F32 && (head_dim == 64 || head_dim == 128) && groups <= 16;
+}
+
+// Resident CTAs of one split-kernel instance on the current device (cached).
+template <typename T, int D, int NT>
+int split_slots(int* slots_out) {
+  using CF = SplitCfg<D>;
+  auto kern = attn_decode_split_kernel<T, D, NT>;
+  static int slots[kMaxDevices] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return fail(AUGUR_KV_ECUDA, "paged_decode_attention: cannot query the current device");
-  {
-    std::lock_guard<std::mutex> lock(g_cache_mutex);
-    if (!attr_done[dev]) {
-      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::kBytes) != cudaSuccess)
-        return check_launch("cudaFuncSetAttribute(attn_decode_mma_kernel)");
-      attr_done[dev] = true;
-    }
+  const int sms = sm_count();
+  std::lock_guard<std::recursive_mutex> lock(g_cache_mutex);
+  if (slots[dev] == 0) {
+    int per_sm = 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, CF::kBytes) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, CF::kThreads, CF::kBytes) != cudaSuccess)
+      return check_launch("attn_decode_split_kernel occupancy");
+    slots[dev] = std::max(1, per_sm) * sms;
   }
+  *slots_out = slots[dev];
+  return AUGUR_KV_OK;
+}
+
+template <typename T, int D, int NT>
+int launch_split(AttnArgs a, int max_seq, void* ws, int64_t ws_bytes, cudaStream_t st) {
+  using CF = SplitCfg<D>;
+  int slots = 0;
+  const int rc = split_slots<T, D, NT>(&slots);
+  if (rc != AUGUR_KV_OK) return rc;
+  const SplitPlan p = plan_split(a.batch, a.hkv, a.groups, D, max_seq, slots, CF::kChunkUnit);
+  a.chunk = p.chunk_min;
+  if (p.ws_bytes > 0 && (ws == nullptr || ws_bytes < p.ws_bytes)) {
+    // not enough workspace: one chunk per sequence (chunk sizes stay powers of two)
+    int64_t C = CF::kChunkUnit;
+    while (C < max_seq) C *= 2;
+    a.chunk = int(C);
+  } else if (p.ws_bytes > 0) {
+    char* w = static_cast<char*>(ws);
+    a.ws_cnt = reinterpret_cast<int32_t*>(w);
+    a.ws_ml = reinterpret_cast<float*>(w + p.cnt_bytes);
+    a.ws_o = reinterpret_cast<float*>(w + p.cnt_bytes + p.ml_bytes);
+  }
+  // programmatic dependent launch: the CTAs may become resident while the
+  // previous kernel drains; the kernel waits for it before reading anything
   cudaLaunchConfig_t cfg;
   memset(&cfg, 0, sizeof(cfg));
-  cfg.gridDim = dim3(unsigned(nsplit), unsigned(a.hkv), unsigned(a.batch));
-  cfg.blockDim = dim3(kAttnWarps * 32, 1, 1);
-  cfg.dynamicSmemBytes = SM::kBytes;
+  cfg.gridDim = dim3(unsigned(p.grid), 1, 1);
+  cfg.blockDim = dim3(CF::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = CF::kBytes;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = unsigned(nsplit);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
-  if (e != cudaSuccess) return fail(AUGUR_KV_ECUDA, "attn_decode_mma_kernel: %s", cudaGetErrorString(e));
-  return check_launch("attn_decode_mma_kernel");
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, attn_decode_split_kernel<T, D, NT>, a);
+  if (e != cudaSuccess) return fail(AUGUR_KV_ECUDA, "attn_decode_split_kernel: %s", cudaGetErrorString(e));
+  return check_launch("attn_decode_split_kernel");
+}
+
+template <typename T, int D, int NT>
+int64_t split_workspace(int batch, int hkv, int G, int max_seq) {
+  int slots = 0;
+  if (split_slots<T, D, NT>(&slots) != AUGUR_KV_OK) return -1;
+  return plan_split(batch, hkv, G, D, max_seq, slots, SplitCfg<D>::kChunkUnit).ws_bytes;
+}
+
+template <typename T, int D>
+int launch_split_g(const AttnArgs& a, int max_seq, void* ws, int64_t ws_bytes, cudaStream_t st) {
+  return a.groups <= 8 ? launch_split<T, D, 1>(a, max_seq, ws, ws_bytes, st)
+                       : launch_split<T, D, 2>(a, max_seq, ws, ws_bytes, st);
+}
+
+template <typename T, int D>
+int64_t split_workspace_g(int batch, int hkv, int G, int max_seq) {
+  return G <= 8 ? split_workspace<T, D, 1>(batch, hkv, G, max_seq) : split_workspace<T, D, 2>(batch, hkv, G, max_seq);
 }
 
 }  // namespace
+
+AUGUR_KV_EXPORT int64_t augur_kv_paged_decode_attention_workspace(int32_t batch, int32_t n_q_heads,
+                                                                  int32_t n_kv_heads, int32_t head_dim,
+                                                                  int32_t max_seq_len, int32_t dtype,
+                                                                  int32_t flags) {
+  g_last_error[0] = '\0';
+  if (elem_size(dtype) == 0 || batch < 0 || max_seq_len < 0 || n_q_heads <= 0 || n_kv_heads <= 0 ||
+      n_q_heads % n_kv_heads != 0 || head_dim <= 0) {
+    fail(AUGUR_KV_EINVAL, "paged_decode_attention_workspace: bad sizes");
+    return -1;
+  }
+  const int G = n_q_heads / n_kv_heads;
+  if (batch == 0 || flags == AUGUR_KV_ATTN_GENERIC || !mma_shape_ok(dtype, head_dim, G)) return 0;
+  if (max_seq_len > kMaxSeq) {
+    fail(AUGUR_KV_EINVAL, "paged_decode_attention_workspace: max_seq_len above %d", kMaxSeq);
+    return -1;
+  }
+  if (dtype == AUGUR_KV_BF16)
+    return head_dim == 64 ? split_workspace_g<__nv_bfloat16, 64>(batch, n_kv_heads, G, max_seq_len)
+                          : split_workspace_g<__nv_bfloat16, 128>(batch, n_kv_heads, G, max_seq_len);
+  return head_dim == 64 ? split_workspace_g<__half, 64>(batch, n_kv_heads, G, max_seq_len)
+                        : split_workspace_g<__half, 128>(batch, n_kv_heads, G, max_seq_len);
+}
 
 AUGUR_KV_EXPORT int augur_kv_paged_decode_attention(
     const void* q, const int64_t* q_strides, const void* k_pool, const void* v_pool, const int64_t* pool_strides,
     int64_t num_blocks, int32_t block_size, const int32_t* block_tables, int64_t tables_stride, int64_t max_blocks,
     const int32_t* seq_lens, int32_t max_seq_len, int32_t batch, int32_t n_q_heads, int32_t n_kv_heads,
-    int32_t head_dim, int32_t dtype, void* out, const int64_t* out_strides, int32_t flags, int32_t* status,
-    void* stream) {
+    int32_t head_dim, int32_t dtype, void* out, const int64_t* out_strides, int32_t flags, void* workspace,
+    int64_t workspace_bytes, int32_t* status, void* stream) {
   g_last_error[0] = '\0';
   const int es = elem_size(dtype);
   if (es == 0) return fail(AUGUR_KV_EINVAL, "paged_decode_attention: unknown dtype %d", dtype);
@@ -628,26 +1008,27 @@ AUGUR_KV_EXPORT int augur_kv_paged_decode_attention(
   a.status = status;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
+  a.max_seq = max_seq_len;
+  a.bs_shift = (block_size & (block_size - 1)) == 0 ? __builtin_ctz(unsigned(block_size)) : -1;
+  if (workspace_bytes < 0 || (workspace == nullptr && workspace_bytes != 0) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 15u) != 0)
+    return fail(AUGUR_KV_EINVAL, "paged_decode_attention: workspace must be 16-byte aligned, bytes >= 0");
+
   // The tensor-core path needs a 16-bit dtype, head_dim 64 or 128, at most 16
   // query heads per KV head, and 16-byte aligned rows.
   uintptr_t align = reinterpret_cast<uintptr_t>(k_pool) | reinterpret_cast<uintptr_t>(v_pool) |
                     uintptr_t(a.blk_stride) | uintptr_t(a.head_stride) | uintptr_t(a.row_stride) |
                     reinterpret_cast<uintptr_t>(q) | uintptr_t(a.q_stride_b) | uintptr_t(a.q_stride_h);
-  const bool mma_ok = dtype != AUGUR_KV_F32 && (head_dim == 64 || head_dim == 128) && a.groups <= 16 &&
-                      (align & 15u) == 0 && a.row_stride == int64_t(head_dim) * es;
+  const bool mma_ok = mma_shape_ok(dtype, head_dim, a.groups) && (align & 15u) == 0 &&
+                      a.row_stride == int64_t(head_dim) * es;
   if (flags != AUGUR_KV_ATTN_GENERIC && mma_ok) {
-    // split each sequence over a cluster of CTAs: enough CTAs to cover the
-    // SMs, at least one 16-token tile per warp, at most 8 (portable clusters)
-    const int tiles = (max_seq_len + kTile - 1) / kTile;
-    const int64_t units = int64_t(batch) * n_kv_heads;
-    int nsplit = int((4 * int64_t(sm_count()) + units - 1) / units);  // about 4 CTAs per SM
-    const int by_len = (tiles + kAttnWarps - 1) / kAttnWarps;            // at least one tile per warp
-    if (nsplit > by_len) nsplit = by_len;
-    if (nsplit > 8) nsplit = 8;
-    if (nsplit < 1) nsplit = 1;
+    if (max_seq_len > kMaxSeq)
+      return fail(AUGUR_KV_EINVAL, "paged_decode_attention: max_seq_len above %d", kMaxSeq);
     if (dtype == AUGUR_KV_BF16)
-      return head_dim == 64 ? launch_mma<__nv_bfloat16, 64>(a, nsplit, st) : launch_mma<__nv_bfloat16, 128>(a, nsplit, st);
-    return head_dim == 64 ? launch_mma<__half, 64>(a, nsplit, st) : launch_mma<__half, 128>(a, nsplit, st);
+      return head_dim == 64 ? launch_split_g<__nv_bfloat16, 64>(a, max_seq_len, workspace, workspace_bytes, st)
+                            : launch_split_g<__nv_bfloat16, 128>(a, max_seq_len, workspace, workspace_bytes, st);
+    return head_dim == 64 ? launch_split_g<__half, 64>(a, max_seq_len, workspace, workspace_bytes, st)
+                          : launch_split_g<__half, 128>(a, max_seq_len, workspace, workspace_bytes, st);
   }
 
   // generic path: the whole sequence's scores live in shared memory
@@ -655,13 +1036,12 @@ AUGUR_KV_EXPORT int augur_kv_paged_decode_attention(
   if (smem > 200 * 1024)
     return fail(AUGUR_KV_EINVAL, "paged_decode_attention: generic path limited to %d positions",
                 int(200 * 1024 / sizeof(float)) - head_dim - kGenericThreads);
-  a.max_seq = max_seq_len;
   {
     static int attr_bytes[kMaxDevices] = {0};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
       return fail(AUGUR_KV_ECUDA, "paged_decode_attention: cannot query the current device");
-    std::lock_guard<std::mutex> lock(g_cache_mutex);
+    std::lock_guard<std::recursive_mutex> lock(g_cache_mutex);
     if (smem > 48 * 1024 && size_t(attr_bytes[dev]) < smem) {
       if (cudaFuncSetAttribute(attn_decode_generic_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                int(200 * 1024)) != cudaSuccess)

@@ -36,7 +36,7 @@
 #include "augur_kv.h"
 #include "common.cuh"
 
-#define AUGUR_KV_VERSION ((0 << 16) | 4)
+#define AUGUR_KV_VERSION ((0 << 16) | 5)
 
 namespace augur_kv_dev {
 
@@ -77,13 +77,13 @@ int pow2_shift(int64_t v) {
 
 // Guards the per-device launch-configuration caches below; entry points are
 // otherwise stateless and may be called from several host threads.
-std::mutex g_cache_mutex;
+std::recursive_mutex g_cache_mutex;
 
 int sm_count() {
   static int cached[kMaxDevices] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
-  std::lock_guard<std::mutex> lock(g_cache_mutex);
+  std::lock_guard<std::recursive_mutex> lock(g_cache_mutex);
   if (cached[dev] == 0) {
     int n = 0;
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
@@ -104,7 +104,7 @@ int resident_ctas(const void* kernel, int threads) {
   static int used = 0;
   int dev = 0;
   cudaGetDevice(&dev);
-  std::lock_guard<std::mutex> lock(g_cache_mutex);
+  std::lock_guard<std::recursive_mutex> lock(g_cache_mutex);
   for (int i = 0; i < used; ++i)
     if (cache[i].k == kernel && cache[i].dev == dev) return cache[i].n;
   int n = 0;
@@ -1133,7 +1133,7 @@ AUGUR_KV_EXPORT int augur_kv_copy_runs(const void* src_k, const void* src_v, con
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
       return fail(AUGUR_KV_ECUDA, "copy_runs: cannot query the current device");
     {
-      std::lock_guard<std::mutex> lock(g_cache_mutex);
+      std::lock_guard<std::recursive_mutex> lock(g_cache_mutex);
       if (smem > 48 * 1024 && attr_bytes[dev] < smem) {
         if (cudaFuncSetAttribute(copy_runs_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  smem) != cudaSuccess)
@@ -1185,7 +1185,7 @@ typedef int (*MemGetAddressRangeFn)(unsigned long long*, size_t*, unsigned long 
 int allocation_base(const void* ptr, const char** base) {
   static MemGetAddressRangeFn fn = nullptr;
   {
-    std::lock_guard<std::mutex> lock(g_cache_mutex);
+    std::lock_guard<std::recursive_mutex> lock(g_cache_mutex);
     if (fn == nullptr) {
       void* f = nullptr;
       cudaDriverEntryPointQueryResult q;
@@ -1317,7 +1317,7 @@ int noalloc_runs_ptr(int32_t** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return fail(AUGUR_KV_ECUDA, "copy_runs_noalloc: cannot query the current device");
-  std::lock_guard<std::mutex> lock(g_cache_mutex);
+  std::lock_guard<std::recursive_mutex> lock(g_cache_mutex);
   if (cached[dev] == nullptr) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_runs);

@@ -12,8 +12,9 @@ constexpr int kMaxDevices = 64;
 
 // Text of the last error on this host thread (augur_kv_last_error).
 extern thread_local char g_last_error[512];
-// Guards the per-device launch-configuration caches.
-extern std::mutex g_cache_mutex;
+// Guards the per-device launch-configuration caches (recursive: cached
+// queries such as sm_count may run while a caller holds it).
+extern std::recursive_mutex g_cache_mutex;
 
 // Record an error message and return `code`.
 int fail(int code, const char* fmt, ...);

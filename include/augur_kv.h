@@ -163,6 +163,14 @@ int augur_kv_copy_runs(const void* src_k, const void* src_v,
  * flags: AUGUR_KV_ATTN_AUTO picks the tensor-core kernel for bf16/fp16,
  * head_dim 64 or 128, <= 16 query heads per KV head; AUGUR_KV_ATTN_GENERIC
  * forces the CUDA-core kernel (any dtype; max_seq_len <= ~51,000).
+ * workspace: device memory, 16-byte aligned, whose first bytes (the arrival
+ * counters) are zero before the first launch that uses it; every launch
+ * leaves them zero again. Size it with
+ * augur_kv_paged_decode_attention_workspace; with a smaller one (or NULL,
+ * 0) each sequence is processed by one CTA, unsplit. Launches that may run
+ * concurrently need separate workspaces. max_seq_len is at most 2^30.
+ * A seq_lens entry above max_seq_len records AUGUR_KV_EBOUNDS and only its
+ * first max_seq_len positions are attended.
  */
 #define AUGUR_KV_ATTN_AUTO 0
 #define AUGUR_KV_ATTN_GENERIC 1
@@ -175,7 +183,18 @@ int augur_kv_paged_decode_attention(const void* q, const int64_t* q_strides, /* 
                                     const int32_t* seq_lens, int32_t max_seq_len, int32_t batch,
                                     int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim, int32_t dtype,
                                     void* out, const int64_t* out_strides, /* [2] */
-                                    int32_t flags, int32_t* status, void* stream);
+                                    int32_t flags, void* workspace, int64_t workspace_bytes,
+                                    int32_t* status, void* stream);
+
+/*
+ * augur_kv_paged_decode_attention_workspace — bytes of workspace
+ * augur_kv_paged_decode_attention uses for these sizes on the current device
+ * (0: none), or -1 for invalid sizes. No reference counterpart (the
+ * reference's eager attention allocates its temporaries per call).
+ */
+int64_t augur_kv_paged_decode_attention_workspace(int32_t batch, int32_t n_q_heads, int32_t n_kv_heads,
+                                                  int32_t head_dim, int32_t max_seq_len, int32_t dtype,
+                                                  int32_t flags);
 
 /*
  * Peer memory for the disaggregated mode: a decode GPU's process exports its
