@@ -435,7 +435,77 @@ def bench_decode_attention(device, pool, tables) -> dict:
             "kernel": "attn_decode_split_kernel<bf16,64>", "timed": "CUDA graph of 24 per-layer launches, L2 flushed"}
 
 
-def run_extras(device, handoff_only: bool = False, attention_only: bool = False) -> dict:
+def bench_rope(device, pool, reps: int = 7) -> dict:
+    """RoPE fused with the paged write for a config-2-sized prefill (8,192 tokens, one layer per
+    launch, all 24 layers), against the same math as separate torch ops plus the scatter.
+
+    Algorithmic bytes per token and layer: q read + rotated q written (2 x 14 x 64 x 2 B),
+    K and V read and written (2 x 512 B), two cos/sin table rows (2 x 64 B), position and
+    slot (16 B) = 4,752 B.
+    """
+    from augur_b200 import batched
+    from augur_b200.rope import rope_tables, write_paged_kv_batch_rope
+
+    T, Hq, theta = 8192, 14, 1000000.0
+    g = torch.Generator(device=device).manual_seed(11)
+    rng = np.random.default_rng(11)
+    lens = config2_lengths(0)
+    pos = torch.from_numpy(np.concatenate([np.arange(n) for n in lens]).astype(np.int64)).to(device)
+    nslots = pool.keys.shape[1] * BS
+    slots = torch.from_numpy(rng.permutation(nslots)[:T].astype(np.int64)).to(device)
+    q = torch.randn(L, T, Hq, D, generator=g, device=device).to(torch.bfloat16)
+    k = torch.randn(L, T, H, D, generator=g, device=device).to(torch.bfloat16)
+    v = torch.randn(L, T, H, D, generator=g, device=device).to(torch.bfloat16)
+    cos, sin = rope_tables(D, theta, torch.bfloat16, int(lens.max()), device)
+    maxp = int(lens.max()) - 1
+
+    def fused() -> None:
+        for layer in range(L):
+            write_paged_kv_batch_rope(pool, q[layer], k[layer], v[layer], slots, pos, theta, layer, max_position=maxp)
+
+    def unfused() -> None:  # the reference's elementwise ops (augur/rope.py:38-39), then the scatter
+        c = torch.cat((cos[pos], cos[pos]), dim=-1).unsqueeze(1)
+        s_ = torch.cat((sin[pos], sin[pos]), dim=-1).unsqueeze(1)
+        for layer in range(L):
+            x, y = q[layer], k[layer]
+            rq = torch.cat((-x[..., D // 2:], x[..., : D // 2]), dim=-1)
+            ry = torch.cat((-y[..., D // 2:], y[..., : D // 2]), dim=-1)
+            _ = x * c + rq * s_
+            ke = y * c + ry * s_
+            batched.write_paged_kv_batch(pool, ke, v[layer], slots, layer_idx=layer)
+
+    res = {}
+    for name, fn in (("fused", fused), ("torch_ops_then_scatter", unfused)):
+        fn()
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        cs = torch.cuda.Stream(device)
+        cs.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(cs):
+            fn()
+        torch.cuda.synchronize(device)
+        with torch.cuda.graph(graph, stream=cs):
+            fn()
+        times = []
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            graph.replay()
+            b.record()
+            torch.cuda.synchronize(device)
+            times.append(a.elapsed_time(b))
+        graph.reset()
+        res[name] = statistics.median(times[2:]) * 1e3 / L
+    nbytes = T * 4752
+    peak, _ = load_peaks()
+    gbs = nbytes / (res["fused"] / 1e6) / 1e9
+    return {"us_per_layer_fused": round(res["fused"], 2),
+            "us_per_layer_torch_ops_then_scatter": round(res["torch_ops_then_scatter"], 2),
+            "tokens": T, "GBps_fused": round(gbs, 1), "frac_of_hbm_peak": round(gbs / peak, 4),
+            "timed": "CUDA graph of 24 per-layer launches; q, k, v of all layers (450 MB) exceed L2"}
+
+
+def run_extras(device, handoff_only: bool = False, attention_only: bool = False, rope_only: bool = False) -> dict:
     """Config 3 handoff + decode append and config 4 fork/COW, timed with CUDA events."""
     import augur_b200 as ab
     from augur_b200 import _lib, _ops, batched
@@ -513,8 +583,13 @@ def run_extras(device, handoff_only: bool = False, attention_only: bool = False)
 
     # ---- decode attention reading the pool in place: one decode step of the
     # 32 sequences (each n + 256 tokens long now) across all 24 layers
-    out["decode_attention"] = bench_decode_attention(device, pool, tables)
+    if not rope_only:
+        out["decode_attention"] = bench_decode_attention(device, pool, tables)
     if attention_only:
+        return out
+    # ---- RoPE fused with the paged write, config-2-sized prefill, all layers
+    out["rope_scatter"] = bench_rope(device, pool)
+    if rope_only:
         return out
 
     # ---- config 4: 1000-token prefix (62 full blocks + 8 rows) forked 256 ways, COW, 128-token suffix
@@ -809,6 +884,8 @@ def main() -> None:
     ap.add_argument("--handoff-only", action="store_true", help="profiling case: config-3 handoff only")
     ap.add_argument("--attention-only", action="store_true",
                     help="profiling case: config-3 cache, then decode attention over all layers")
+    ap.add_argument("--rope-only", action="store_true",
+                    help="profiling case: config-3 cache, then RoPE fused with the paged write")
     ap.add_argument("--workload", choices=["scatter", "disagg", "box"], default="scatter",
                     help="scatter: headline (config 2); disagg: NVLink block push between rank pairs; "
                          "box: config 5, 2048 sequences sharded over the ranks (strong scaling)")
@@ -821,6 +898,10 @@ def main() -> None:
     if args.handoff_only:  # profiling case: only the config-3 handoff (about 3 GB on the device)
         torch.cuda.set_device(0)
         emit(run_extras(torch.device("cuda", 0), handoff_only=True))
+        return
+    if args.rope_only:  # profiling case: config-3 pool, then the fused RoPE + write
+        torch.cuda.set_device(0)
+        emit(run_extras(torch.device("cuda", 0), rope_only=True))
         return
     if args.attention_only:  # profiling case: config-3 handoff + appends, then decode attention
         torch.cuda.set_device(0)

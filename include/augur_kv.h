@@ -109,6 +109,47 @@ int augur_kv_scatter(const void* src_k, const void* src_v,
                      void* stream);
 
 /*
+ * augur_kv_rope_scatter — rotary position embedding fused with the cache
+ * write: rotates q (into q_out) and k by the table row of each token's
+ * position, then writes the rotated k and the unchanged v to the cache. This
+ * replaces apply_rope (augur/rope.py:12-40) followed by write_kv
+ * (augur/kv_cache.py:75-112) or write_paged_kv (augur/paged_kv_cache.py:
+ * 167-192), the sequence at augur/attention.py:53-71.
+ *
+ * Source addressing, the slot index and the destination follow
+ * augur_kv_scatter (device index only; one dtype on every tensor). Token t
+ * (row = t / tokens_per_row, col = t % tokens_per_row) has position
+ * positions[row*position_strides[0] + col*position_strides[1]]. rope_cos and
+ * rope_sin are [rope_positions][head_dim/2] tables in the cache dtype, built
+ * like the reference's cos/sin (inv_freq = 1/theta^(2i/head_dim), angle =
+ * position * inv_freq in float32, cos/sin cast to the dtype); element d and
+ * d + head_dim/2 of a rotated row use entry d. q (n_q_heads heads, strides
+ * [4] layer, row, col, head) is rotated into q_out (same shape); n_q_heads = 0
+ * rotates k only. A token whose index is negative still has its q rotated.
+ * Rounding matches the reference's three dtype ops (x*cos, rotate_half(x)*sin,
+ * their sum), so the result is bit-exact given the same table. A position
+ * outside [0, rope_positions) records AUGUR_KV_EBOUNDS and skips that token's
+ * rotated rows.
+ */
+int augur_kv_rope_scatter(const void* src_k, const void* src_v,
+                          const int64_t* src_k_strides, /* [4] layer, row, col, head */
+                          const int64_t* src_v_strides, /* [4] */
+                          int64_t tokens_per_row, int32_t dtype,
+                          void* dst_k, void* dst_v,
+                          const int64_t* dst_strides, /* [4] layer, major, row, head */
+                          int64_t rows_per_major, int64_t num_majors,
+                          const int64_t* index,         /* device */
+                          const int64_t* index_strides, /* [2] row, col */
+                          int64_t index_row_base,
+                          const int64_t* positions,         /* device */
+                          const int64_t* position_strides,  /* [2] row, col */
+                          const void* rope_cos, const void* rope_sin, int64_t rope_positions,
+                          const void* q, const int64_t* q_strides, /* [4] layer, row, col, head */
+                          void* q_out, const int64_t* q_out_strides, int32_t n_q_heads,
+                          int64_t n_tokens, int32_t n_layers, int32_t n_heads, int32_t head_dim,
+                          int32_t* status, void* stream);
+
+/*
  * augur_kv_copy_runs — copy runs of consecutive rows between two caches, all
  * layers, K and V, every head, in one launch. This is the block mover behind:
  *   - read_paged_kv, the logical-order gather (augur/paged_kv_cache.py:195-221)

@@ -295,3 +295,43 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch
     scores = torch.matmul(q, k.transpose(-2, -1)) / math.sqrt(q.shape[-1])
     probs = torch.softmax(scores, dim=-1, dtype=torch.float32).to(q.dtype)
     return torch.matmul(probs, v)
+
+
+def rope_inv_freq(head_dim: int, rope_theta: float) -> torch.Tensor:
+    """augur/rope.py:29-32: 1 / theta^(arange(0, D, 2) / D), float32."""
+    return 1.0 / (rope_theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim))
+
+
+def rope_table(head_dim: int, rope_theta: float, n_positions: int, dtype: torch.dtype):
+    """cos / sin [n_positions, head_dim // 2] in `dtype`, as augur/rope.py:33-36 forms them
+    for positions 0..n_positions-1 (float32 angles, cos/sin in float32, cast)."""
+    freqs = torch.arange(n_positions, dtype=torch.float32).unsqueeze(-1) * rope_inv_freq(head_dim, rope_theta)
+    return freqs.cos().to(dtype), freqs.sin().to(dtype)
+
+
+def apply_rope(q: torch.Tensor, k: torch.Tensor, position_ids: torch.Tensor, rope_theta: float,
+               table: tuple[torch.Tensor, torch.Tensor] | None = None):
+    """Restates augur/rope.py:12-40 on the CPU: x * cos + rotate_half(x) * sin, every op in
+    the input dtype. q [B, Hq, S, D], k [B, Hkv, S, D], position_ids [B, S].
+
+    table=None computes cos/sin from the positions exactly as the reference does;
+    a (cos, sin) table [P, D/2] (rope_table) is indexed by position instead, which
+    is what the kernel consumes.
+    """
+    q, k, position_ids = _cpu(q), _cpu(k), _cpu(position_ids)
+    head_dim = q.shape[-1]
+    if table is None:
+        freqs = position_ids.to(torch.float32).unsqueeze(-1) * rope_inv_freq(head_dim, rope_theta)
+        emb = torch.cat((freqs, freqs), dim=-1)
+        cos = emb.cos().unsqueeze(1).to(q.dtype)
+        sin = emb.sin().unsqueeze(1).to(q.dtype)
+    else:
+        c, s = table[0][position_ids.long()], table[1][position_ids.long()]
+        cos = torch.cat((c, c), dim=-1).unsqueeze(1).to(q.dtype)
+        sin = torch.cat((s, s), dim=-1).unsqueeze(1).to(q.dtype)
+
+    def rotate_half(x):
+        half = x.shape[-1] // 2
+        return torch.cat((-x[..., half:], x[..., :half]), dim=-1)
+
+    return (q * cos) + (rotate_half(q) * sin), (k * cos) + (rotate_half(k) * sin)

@@ -278,6 +278,8 @@ def attention_cases(ref, g):
                                        device=torch.device("cpu"), dtype=dtype),
             block_table=P.SequenceBlockTable.empty(block_size=16),
         )
+        poison(state.cache.keys)  # rows never written stay 0xFF: deterministic fixtures
+        poison(state.cache.values)
         state.cache.allocator.allocate()  # the pool already holds another block
         pos = torch.arange(seq).unsqueeze(0)
         attention(x[:, : seq - 1], w, cfg, pos[:, : seq - 1], paged_cache=state, layer_idx=0)
@@ -293,6 +295,67 @@ def attention_cases(ref, g):
                        "k": kk.clone(), "v": vv.clone(),
                        "out": out.view(1, 1, Hq, D).permute(0, 2, 1, 3).contiguous(),
                        "n_kv_heads": Hkv}
+    return cases
+
+
+def rope_cases(ref, g):
+    """apply_rope (augur/rope.py:12-40) followed by the cache write, as augur/attention.py:53-71 runs it.
+
+    theta 1e6 (Qwen2.5's), 14 query / 2 KV heads, head_dim 64, fp32 / bf16 / fp16:
+    - paged_*: write_paged_kv (block 16, one layer, a 40-block poisoned pool that
+      already holds another block) of a 37-token chunk at positions 100..136, then
+      one decode token at position 600 (the table grows lazily to 38 blocks).
+      Stored: the inputs of each call, the rotated q, the block table and the
+      pool blocks the calls touched (every other block must still be poison).
+    - contig_*: write_kv of 5 tokens into two batch rows at positions 0..4 and 20..24.
+    - far_*: apply_rope alone at positions 0, 1, 4095, 8191, 32767 (large angles).
+    q / k / v are strided views of a token-major projection, as in the reference.
+    """
+    from augur.rope import apply_rope
+
+    P, K = ref.paged_kv_cache, ref.kv_cache
+    theta = 1000000.0
+    cases = {}
+    for name, dtype in (("f32", torch.float32), ("bf16", torch.bfloat16), ("f16", torch.float16)):
+        cfg = ref.config.QwenConfig(vocab_size=16, hidden_size=896, intermediate_size=16, num_hidden_layers=1,
+                                    num_attention_heads=14, num_key_value_heads=2)
+        pool = P.new_paged_kv_cache(cfg, num_blocks=40, block_size=16, device=torch.device("cpu"), dtype=dtype)
+        poison(pool.keys)
+        poison(pool.values)
+        pool.allocator.allocate()  # another sequence's block
+        table = P.SequenceBlockTable.empty(block_size=16)
+        calls, touched = [], set()
+        for pos in (torch.arange(100, 137), torch.tensor([600])):
+            S = pos.numel()
+            q = strided_kv(g, 1, 14, S, 64, dtype)
+            k = strided_kv(g, 1, 2, S, 64, dtype)
+            v = strided_kv(g, 1, 2, S, 64, dtype)
+            qe, ke = apply_rope(q, k, pos[None], theta)
+            P.write_paged_kv(pool, 0, table, pos[None], ke, v)
+            touched.update(int(p) // 16 for p in pos)
+            calls.append({"q": q, "k": k, "v": v, "position_ids": pos[None].clone(), "q_embed": qe.contiguous()})
+        blocks = [table.block_ids[j] for j in sorted(touched)]
+        cases[f"paged_{name}"] = {"calls": calls, "block_ids": list(table.block_ids), "touched_blocks": blocks,
+                                  "keys": pool.keys[:, blocks].clone(), "values": pool.values[:, blocks].clone(),
+                                  "num_blocks": 40, "prior_allocated": 1, "theta": theta}
+        cache = K.new_kv_cache(cfg, batch_size=2, max_seq_len=32, device=torch.device("cpu"), dtype=dtype)
+        poison(cache.keys)
+        poison(cache.values)
+        pos = torch.stack([torch.arange(0, 5), torch.arange(20, 25)])
+        q = strided_kv(g, 2, 14, 5, 64, dtype)
+        k = strided_kv(g, 2, 2, 5, 64, dtype)
+        v = strided_kv(g, 2, 2, 5, 64, dtype)
+        qe, ke = apply_rope(q, k, pos, theta)
+        K.write_kv(cache, 0, pos, ke, v)
+        cases[f"contig_{name}"] = {"q": q, "k": k, "v": v, "position_ids": pos, "q_embed": qe.contiguous(),
+                                   "keys": cache.keys.clone(), "values": cache.values.clone(),
+                                   "seq_len": cache.seq_len, "theta": theta}
+        pos = torch.tensor([[0, 1, 4095, 8191, 32767]])
+        q = strided_kv(g, 1, 14, 5, 64, dtype)
+        k = strided_kv(g, 1, 2, 5, 64, dtype)
+        qe, ke = apply_rope(q, k, pos, theta)
+        cases[f"far_{name}"] = {"q": q, "k": k, "position_ids": pos, "q_embed": qe.contiguous(),
+                                "k_embed": ke.contiguous(), "theta": theta}
     return cases
 
 
@@ -427,6 +490,7 @@ def main() -> None:
         "bookkeeping": bookkeeping_scripts(Ref),
     }
     cases["attention"] = attention_cases(Ref, torch.Generator().manual_seed(4321))
+    cases["rope"] = rope_cases(Ref, torch.Generator().manual_seed(777))
     torch.save(cases, os.path.join(HERE, "reference_cases.pt"))
     if not args.skip_config1:
         torch.save(config1(Ref), os.path.join(HERE, "config1_writes.pt"))

@@ -322,3 +322,44 @@ def test_paged_decode_attention_refuses_cpu_and_bad_shapes():
         paged_decode_attention(torch.zeros(1, 14, 2, 64, dtype=torch.bfloat16), cpu, 0, [t])
     with pytest.raises(ValueError, match="block table capacity"):
         DecodeTables([ab.SequenceBlockTable(block_ids=[0], block_size=16, seq_len=17)], torch.device("cpu"))
+
+
+def test_rope_tables_follow_the_reference_formula(oracle):
+    """The product's cos/sin tables equal the oracle's (pinned to augur/rope.py) bit for bit."""
+    from augur_b200.rope import rope_tables
+
+    for dt in (torch.float32, torch.bfloat16, torch.float16):
+        cos, sin = rope_tables(64, 1000000.0, dt, 5000, torch.device("cpu"))
+        assert cos.shape == (8192, 32) and cos.dtype == dt
+        rc, rs = oracle.rope_table(64, 1000000.0, 8192, dt)
+        assert torch.equal(cos.view(torch.uint8), rc.view(torch.uint8))
+        assert torch.equal(sin.view(torch.uint8), rs.view(torch.uint8))
+    with pytest.raises(ValueError, match="even"):
+        rope_tables(63, 10000.0, torch.float32, 8, torch.device("cpu"))
+
+
+def test_rope_writes_refuse_cpu_and_bad_shapes():
+    from augur_b200.rope import rope_write_kv, rope_write_paged_kv, write_paged_kv_batch_rope
+
+    cfg = ab.QwenConfig()
+    pool = ab.new_paged_kv_cache(cfg, num_blocks=4, block_size=16, device=torch.device("cpu"), dtype=torch.bfloat16)
+    t = ab.SequenceBlockTable.empty(16)
+    q = torch.zeros(1, 14, 3, 64, dtype=torch.bfloat16)
+    kv = torch.zeros(1, 2, 3, 64, dtype=torch.bfloat16)
+    pos = torch.arange(3).unsqueeze(0)
+    with pytest.raises(ValueError, match="needs CUDA tensors"):
+        rope_write_paged_kv(pool, 0, t, pos, q, kv, kv, 1e6)
+    assert t.block_ids == []  # nothing allocated before the refusal
+    with pytest.raises(ValueError, match="batch size 1"):
+        rope_write_paged_kv(pool, 0, t, pos.repeat(2, 1), q.repeat(2, 1, 1, 1), kv.repeat(2, 1, 1, 1),
+                            kv.repeat(2, 1, 1, 1), 1e6)
+    with pytest.raises(ValueError, match="q must be"):
+        rope_write_paged_kv(pool, 0, t, pos, q[:, :, :2], kv, kv, 1e6)
+    cache = ab.new_kv_cache(cfg, batch_size=1, max_seq_len=8, device=torch.device("cpu"), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="needs CUDA tensors"):
+        rope_write_kv(cache, 0, pos, q, kv, kv, 1e6)
+    with pytest.raises(ValueError, match="exceeds cache capacity|needs CUDA"):
+        rope_write_kv(cache, 0, pos + 8, q, kv, kv, 1e6)
+    with pytest.raises(ValueError, match="slot_mapping and positions"):
+        write_paged_kv_batch_rope(pool, q[0].transpose(0, 1), kv[0].transpose(0, 1), kv[0].transpose(0, 1),
+                                  torch.zeros(2, dtype=torch.int64), torch.zeros(3, dtype=torch.int64), 1e6, 0)

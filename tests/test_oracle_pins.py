@@ -279,3 +279,38 @@ def test_golden_decode_attention(oracle, golden, case):
     c = golden["attention"][case]
     got = oracle.decode_attention(c["q"], c["k"], c["v"])
     assert_bits_equal(got, c["out"], "attention output")
+
+
+# --- RoPE fused with the cache write ----------------------------------------
+
+
+@pytest.mark.parametrize("case", ["f32", "bf16", "f16"])
+def test_golden_rope_far_positions(oracle, golden, case):
+    """apply_rope restated, from the reference's formula and from a position-indexed
+    table, equals the reference's apply_rope bit for bit, large angles included."""
+    c = golden["rope"][f"far_{case}"]
+    dt = c["q"].dtype
+    for table in (None, oracle.rope_table(64, c["theta"], 32768, dt)):
+        q, k = oracle.apply_rope(c["q"], c["k"], c["position_ids"], c["theta"], table=table)
+        assert_bits_equal(q, c["q_embed"], "q")
+        assert_bits_equal(k, c["k_embed"], "k")
+
+
+@pytest.mark.parametrize("case", ["f32", "bf16", "f16"])
+def test_golden_rope_then_write_paged_kv(oracle, golden, case):
+    """apply_rope then write_paged_kv, replayed on the oracle from the recorded inputs,
+    reproduces the reference's pool blocks, block table and rotated q."""
+    c = golden["rope"][f"paged_{case}"]
+    dt = c["calls"][0]["q"].dtype
+    pk, pv = _pool((1, c["num_blocks"], 2, 16, 64), dt), _pool((1, c["num_blocks"], 2, 16, 64), dt)
+    alloc = oracle.RefBlockAllocator(c["num_blocks"])
+    for _ in range(c["prior_allocated"]):
+        alloc.allocate()
+    table = oracle.RefBlockTable([], 16)
+    for call in c["calls"]:
+        q, k = oracle.apply_rope(call["q"], call["k"], call["position_ids"], c["theta"])
+        assert_bits_equal(q, call["q_embed"], "q")
+        oracle.write_paged_kv(pk, pv, alloc, 0, table, call["position_ids"][0].tolist(), k, call["v"])
+    assert table.block_ids == c["block_ids"]
+    assert_bits_equal(pk[:, c["touched_blocks"]], c["keys"], "keys")
+    assert_bits_equal(pv[:, c["touched_blocks"]], c["values"], "values")
