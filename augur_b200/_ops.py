@@ -200,14 +200,29 @@ def copy_runs(
     head_dim: int,
     flags: int = _lib.COPY_AUTO,
     stream: torch.cuda.Stream | None = None,
+    allow_pinned_host: bool = False,
 ) -> None:
-    """Launch augur_kv_copy_runs; runs is a device int32 [n_runs, 5] tensor."""
+    """Launch augur_kv_copy_runs; runs is a device int32 [n_runs, 5] tensor.
+
+    allow_pinned_host: src or dst may be pinned host memory (the device reads
+    or writes it in place over the host link, with the vector path's 16-byte
+    accesses); the launch goes to the device of the CUDA-side tensor.
+    """
     global launch_count
-    require_cuda("KV block copy", src_k, src_v, dst_k, dst_v, runs)
+    if allow_pinned_host:
+        host = [t for t in (src_k, src_v, dst_k, dst_v) if t is not None and t.device.type == "cpu"]
+        if any(not t.is_pinned() for t in host):
+            raise ValueError("host-side KV tensors must be in pinned memory (tensor.pin_memory())")
+        require_cuda("KV block copy", runs, *[t for t in (src_k, src_v, dst_k, dst_v)
+                                              if t is not None and t.device.type != "cpu"])
+        if host:
+            flags = (flags & ~(_lib.COPY_BULK | _lib.COPY_AUTO)) | _lib.COPY_VECTOR
+    else:
+        require_cuda("KV block copy", src_k, src_v, dst_k, dst_v, runs)
     if runs.dtype != torch.int32 or runs.dim() != 2 or runs.shape[1] != 5 or not runs.is_contiguous():
         raise ValueError("runs must be a contiguous int32 tensor of shape [n_runs, 5]")
     lib = _lib.load()
-    device = dst_k.device
+    device = runs.device
     st = stream if stream is not None else torch.cuda.current_stream(device)
     with _DeviceGuard(device):
         code = lib.augur_kv_copy_runs(
@@ -237,6 +252,24 @@ def copy_runs(
     if runs.shape[0] > 0 and n_layers > 0:
         launch_count += 1
         keep_until_done(st, runs, src_k, src_v)
+        if allow_pinned_host:
+            keep_host_until_done(st, src_k, src_v, dst_k, dst_v)
+
+
+# Pinned host tensors a launch reads or writes, held until the launch is done:
+# torch's host allocator does not see kernels that use host memory directly.
+_host_keepalive: list[tuple[torch.cuda.Event, tuple]] = []
+
+
+def keep_host_until_done(stream: torch.cuda.Stream, *tensors: Tensor | None) -> None:
+    host = tuple(t for t in tensors if t is not None and t.device.type == "cpu")
+    if not host or torch.cuda.is_current_stream_capturing():
+        return  # a captured graph's owner keeps its buffers alive for the graph's life
+    while _host_keepalive and _host_keepalive[0][0].query():
+        _host_keepalive.pop(0)
+    ev = torch.cuda.Event()
+    ev.record(stream)
+    _host_keepalive.append((ev, host))
 
 
 def host_index_ok(n_tokens: int, src: Tensor, dst: Tensor) -> bool:

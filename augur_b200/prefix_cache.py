@@ -91,12 +91,16 @@ def copy_prefix_into_cache(entry: PrefixCacheEntry, cache: KVCache, batch_idx: i
     if prefix_len > 0:
         device = cache.keys.device
         keys, values = entry.keys, entry.values
-        # An entry kept on another device (e.g. host memory) is transferred
-        # first; the per-row copy and any dtype conversion run in the kernel.
-        if keys.device != device:
-            keys = keys.to(device)
-        if values.device != device:
-            values = values.to(device)
+        # An entry in pinned host memory (offload_prefix_entry) is read in
+        # place by the kernel; one on another device, or in pageable host
+        # memory, is transferred first. The per-row copy and any dtype
+        # conversion run in the kernel.
+        pinned = all(t.device.type == "cpu" and t.is_pinned() for t in (keys, values))
+        if not pinned:
+            if keys.device != device:
+                keys = keys.to(device)
+            if values.device != device:
+                values = values.to(device)
         if keys.stride(-1) != 1:
             keys = keys.contiguous()
         if values.stride(-1) != 1:
@@ -117,7 +121,7 @@ def copy_prefix_into_cache(entry: PrefixCacheEntry, cache: KVCache, batch_idx: i
                 dst_k=dk, dst_v=dv, dst_strides=dst(dk),
                 dst_majors=dk.shape[1], dst_rows_per_major=dk.shape[3],
                 runs=runs, max_rows=max_rows, n_layers=num_layers, n_heads=num_heads,
-                head_dim=head_dim,
+                head_dim=head_dim, allow_pinned_host=pinned,
             )
     cache.seq_len = max(cache.seq_len, entry.seq_len)
 

@@ -505,7 +505,57 @@ def bench_rope(device, pool, reps: int = 7) -> dict:
             "timed": "CUDA graph of 24 per-layer launches; q, k, v of all layers (450 MB) exceed L2"}
 
 
-def run_extras(device, handoff_only: bool = False, attention_only: bool = False, rope_only: bool = False) -> dict:
+def bench_offload(device, pool, tables, n_seqs: int = 16) -> dict:
+    """Offload n_seqs config-3 sequences (all layers, K and V) to pinned host memory and restore
+    them into freshly allocated blocks, against a copy-engine copy of the same byte count.
+
+    Bytes per direction = tokens x 12,288 B. The host link bounds both ways;
+    the copy-engine figure (torch copy_ of one contiguous device slab to
+    pinned memory and back) is its practical ceiling on this box.
+    """
+    from augur_b200.offload import host_buffer, offload_blocks, restore_blocks
+
+    tabs = tables[:n_seqs]
+    ids, rows = [], []
+    for t in tabs:
+        n = -(-t.seq_len // BS)
+        ids += t.block_ids[:n]
+        rows += [min(BS, t.seq_len - j * BS) for j in range(n)]
+    tokens = int(sum(rows))
+    nbytes = tokens * TOKEN_BYTES
+    hk, hv = host_buffer(pool, len(ids))
+    dst = list(range(len(ids)))  # restore target blocks (their contents are scratch here)
+
+    def timed(fn, reps=5):
+        fn()
+        torch.cuda.synchronize(device)
+        times = []
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize(device)
+            times.append(a.elapsed_time(b))
+        return statistics.median(times)
+
+    t_off = timed(lambda: offload_blocks(pool, ids, rows, out=(hk, hv)))
+    host = offload_blocks(pool, ids, rows, out=(hk, hv))
+    t_res = timed(lambda: restore_blocks(pool, host, dst))
+    slab = pool.keys.view(-1)[: nbytes // pool.keys.element_size()]
+    hslab = torch.empty(slab.shape, dtype=slab.dtype, pin_memory=True)
+    t_d2h = timed(lambda: hslab.copy_(slab, non_blocking=True))
+    t_h2d = timed(lambda: slab.copy_(hslab, non_blocking=True))
+    gb = lambda ms: round(nbytes / (ms / 1e3) / 1e9, 2)  # noqa: E731
+    return {"seqs": len(tabs), "tokens": tokens, "MB": round(nbytes / 1e6, 1),
+            "offload_ms": round(t_off, 3), "offload_GBps": gb(t_off),
+            "restore_ms": round(t_res, 3), "restore_GBps": gb(t_res),
+            "copy_engine_d2h_GBps": gb(t_d2h), "copy_engine_h2d_GBps": gb(t_h2d),
+            "timed": "one launch each way, median of 5; pinned host buffers reused"}
+
+
+def run_extras(device, handoff_only: bool = False, attention_only: bool = False, rope_only: bool = False,
+               offload_only: bool = False) -> dict:
     """Config 3 handoff + decode append and config 4 fork/COW, timed with CUDA events."""
     import augur_b200 as ab
     from augur_b200 import _lib, _ops, batched
@@ -583,10 +633,15 @@ def run_extras(device, handoff_only: bool = False, attention_only: bool = False,
 
     # ---- decode attention reading the pool in place: one decode step of the
     # 32 sequences (each n + 256 tokens long now) across all 24 layers
-    if not rope_only:
+    if not (rope_only or offload_only):
         out["decode_attention"] = bench_decode_attention(device, pool, tables)
     if attention_only:
         return out
+    if not rope_only:
+        # ---- offload to pinned host memory and restore (before the RoPE bench reuses the pool)
+        out["host_offload"] = bench_offload(device, pool, tables)
+        if offload_only:
+            return out
     # ---- RoPE fused with the paged write, config-2-sized prefill, all layers
     out["rope_scatter"] = bench_rope(device, pool)
     if rope_only:
@@ -884,6 +939,8 @@ def main() -> None:
     ap.add_argument("--handoff-only", action="store_true", help="profiling case: config-3 handoff only")
     ap.add_argument("--attention-only", action="store_true",
                     help="profiling case: config-3 cache, then decode attention over all layers")
+    ap.add_argument("--offload-only", action="store_true",
+                    help="config-3 cache, then offload to pinned host memory and restore")
     ap.add_argument("--rope-only", action="store_true",
                     help="profiling case: config-3 cache, then RoPE fused with the paged write")
     ap.add_argument("--workload", choices=["scatter", "disagg", "box"], default="scatter",
@@ -898,6 +955,10 @@ def main() -> None:
     if args.handoff_only:  # profiling case: only the config-3 handoff (about 3 GB on the device)
         torch.cuda.set_device(0)
         emit(run_extras(torch.device("cuda", 0), handoff_only=True))
+        return
+    if args.offload_only:  # config-3 pool, then offload to pinned host memory and restore
+        torch.cuda.set_device(0)
+        emit(run_extras(torch.device("cuda", 0), offload_only=True))
         return
     if args.rope_only:  # profiling case: config-3 pool, then the fused RoPE + write
         torch.cuda.set_device(0)

@@ -94,14 +94,21 @@ def test_write_paged_kv_golden(cuda, golden):
 
 
 @pytest.mark.parametrize("case", ["bf16", "f32_to_bf16", "f32"])
-@pytest.mark.parametrize("entry_on_host", [False, True])
-def test_copy_prefix_golden(cuda, golden, case, entry_on_host):
+@pytest.mark.parametrize("entry_on", ["device", "host", "pinned_host"])
+def test_copy_prefix_golden(cuda, golden, case, entry_on):
+    """Entry on the device, in pageable host memory (transferred first) or in pinned host
+    memory (read in place by the kernel)."""
     c = golden["prefix"][case]
     cache = ab.KVCache(keys=_poisoned(c["keys"].shape, c["keys"].dtype, cuda),
                        values=_poisoned(c["keys"].shape, c["keys"].dtype, cuda), seq_len=2)
-    dev = torch.device("cpu") if entry_on_host else cuda
+    dev = cuda if entry_on == "device" else torch.device("cpu")
     entry = ab.PrefixCacheEntry(token_ids=torch.arange(6), keys=c["entry_keys"].to(dev),
                                 values=c["entry_values"].to(dev), logits=torch.empty(0))
+    if entry_on == "pinned_host":
+        from augur_b200.offload import offload_prefix_entry
+
+        entry = offload_prefix_entry(entry)
+        assert entry.keys.is_pinned()
     ab.copy_prefix_into_cache(entry, cache, batch_idx=c["batch_idx"])
     assert cache.seq_len == c["seq_len"]
     assert_bits_equal(cache.keys, c["keys"], "keys")
