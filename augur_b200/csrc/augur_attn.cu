@@ -72,8 +72,8 @@ struct AttnArgs {
   int32_t max_seq;   // max_seq_len: bound on seq_lens (generic kernel: score capacity)
   int32_t bs_shift;  // log2(block_size) when it is a power of two, else -1
   // split kernel
-  int32_t chunk;  // tokens per chunk, a multiple of 128
-  int32_t nch;    // chunk slots per (sequence, KV head) in the workspace
+  int32_t chunk;      // smallest chunk size the plan may pick (a power of two)
+  int32_t max_items;  // work items the plan may create (waves x grid); partial slots in the workspace
   int32_t* ws_cnt;
   float* ws_ml;
   float* ws_o;
@@ -195,27 +195,36 @@ constexpr int kStageTok = 32;       // tokens a warp stages and processes at a t
 constexpr int kMaxChunks = 256;     // chunks per (sequence, KV head)
 constexpr int kMaxSeq = 1 << 30;    // longest sequence a launch accepts
 
-// Launch shape of the split kernel for one head_dim: warps per CTA, one
-// 32-token stage buffer (K and V rows, padded so ldmatrix rows hit distinct
-// banks) per warp; chunks are multiples of warps x 32 tokens.
-template <int D>
+// Launch shape of the split kernel for one head_dim and NS stage buffers per
+// warp: each buffer holds 32 tokens of K and V rows, padded so ldmatrix rows
+// hit distinct banks. The shared memory stays the same for NS = 1 and 2 (half
+// the warps, each with two buffers, so a warp prefetches its next stage).
+// Chunks are multiples of warps x 32 tokens.
+template <int D, int NS>
 struct SplitCfg {
-  static constexpr int kWarps = D == 64 ? 8 : 4;
+  static constexpr int kWarps = (D == 64 ? 8 : 4) / NS;
   static constexpr int kThreads = kWarps * 32;
   static constexpr int kChunkUnit = kWarps * kStageTok;
   static constexpr int kRowBytes = D * 2 + 16;
   static constexpr int kStageBytes = kStageTok * kRowBytes;  // K or V of one stage
   static constexpr int kWarpStage = 2 * kStageBytes;
-  static constexpr int kPipe = kWarps * kWarpStage;
+  static constexpr int kPipe = kWarps * NS * kWarpStage;
   // after the token loop the warps' partial results reuse the stage buffers
   static constexpr int kPO = D + 4;  // floats per partial row: the transposing stores hit distinct banks
   static constexpr int kPartO = kWarps * 16 * kPO * 4;
   static constexpr int kPartML = kWarps * 16 * 4;
   static_assert(kPartO + 2 * kPartML <= kPipe, "partials must fit in the stage buffers");
   static_assert(2 * kMaxChunks * 16 * 4 <= kPipe, "chunk maxima and sums must fit in the stage buffers");
-  static constexpr int kTail = (kWarps * 16 + 16 + 16 + 8) * 4;  // fac, cta_m, cta_l, flag, item
+  static constexpr int kTail = (kWarps * 16 + 16 + 16 + 8) * 4;  // fac, cta_m, cta_l, flag + item
   static constexpr int kBytes = kPipe + kTail;
 };
+
+#ifndef AUGUR_KV_ATTN_STAGES
+#define AUGUR_KV_ATTN_STAGES 1  // stage buffers per warp at head_dim 64
+#endif
+#ifndef AUGUR_KV_ATTN_COMBINE_REGS
+#define AUGUR_KV_ATTN_COMBINE_REGS 16  // registers per thread holding partial outputs in the combine
+#endif
 
 __device__ __forceinline__ float ex2(float x) {  // 2^x; ex2(-inf) = 0
   float y;
@@ -262,10 +271,11 @@ __device__ __forceinline__ int chunks_of(int S, int C) { return max(1, (S + C - 
 
 // Work items are (sequence, KV head, chunk) triples numbered sequence-major,
 // then KV head, then chunk, so the chunks of one (sequence, KV head) are
-// consecutive. Every CTA (each warp on its own, no shared state) derives the
-// same plan from seq_lens: the smallest chunk size C = a.chunk * 2^j for
-// which the items fit in the grid (one wave when the host sized the grid to
-// the resident CTAs), or C >= max_seq_len (one chunk per sequence).
+// consecutive. Every CTA's warp 0 derives the same plan from seq_lens: the
+// smallest chunk size C = a.chunk * 2^j for which the items number at most
+// a.max_items (a few waves of the persistent grid, so the longest sequence is
+// spread over several CTAs), or C >= max_seq_len (one chunk per sequence; also
+// when the (sequence, KV head) units alone exceed a.max_items).
 struct Plan {
   int C, total;
 };
@@ -278,7 +288,7 @@ __device__ Plan make_plan(const AttnArgs& a, int lane) {
   Plan p;
   p.C = a.chunk;
   const int64_t units = int64_t(a.batch) * a.hkv;
-  if (units >= int64_t(gridDim.x) || p.C >= a.max_seq) {  // one chunk per sequence
+  if (units > int64_t(a.max_items) || p.C >= a.max_seq) {  // one chunk per sequence
     p.C = max(p.C, a.max_seq);
     p.total = int(units);
     return p;
@@ -287,7 +297,7 @@ __device__ Plan make_plan(const AttnArgs& a, int lane) {
     int cnt = 0;
     for (int b = lane; b < a.batch; b += 32) cnt += chunks_of(seq_len_at(a, b), p.C);
     p.total = warp_sum(cnt) * a.hkv;
-    if (p.total <= int(gridDim.x) || p.C >= a.max_seq) return p;
+    if (p.total <= a.max_items || p.C >= a.max_seq) return p;
     p.C *= 2;
   }
 }
@@ -296,7 +306,14 @@ struct Item {
   int b, hk, chunk, nch, first;  // first: item number of chunk 0 of (b, hk)
 };
 
-__device__ Item locate(const AttnArgs& a, const Plan& p, int item, int lane) {
+// Position of warp 0's search over seq_lens: the items of sequences < b number base.
+struct Cursor {
+  int b, base;
+};
+
+// Item `item` of the plan. A CTA visits its items in increasing order, so the
+// search resumes from the cursor (sequences before it hold only earlier items).
+__device__ Item locate(const AttnArgs& a, const Plan& p, int item, int lane, Cursor& cur) {
   Item it;
   if (p.C >= a.max_seq) {  // every sequence is one chunk
     it.b = item / a.hkv;
@@ -306,9 +323,8 @@ __device__ Item locate(const AttnArgs& a, const Plan& p, int item, int lane) {
     it.first = item;
     return it;
   }
-  int run = 0;  // items of the sequences before this group of 32
-  for (int b0 = 0;; b0 += 32) {
-    const int b = b0 + lane;
+  for (;;) {
+    const int b = cur.b + lane;
     const int c = b < a.batch ? chunks_of(seq_len_at(a, b), p.C) * a.hkv : 0;
     int incl = c;
 #pragma unroll
@@ -316,19 +332,22 @@ __device__ Item locate(const AttnArgs& a, const Plan& p, int item, int lane) {
       const int y = __shfl_up_sync(0xffffffffu, incl, o);
       if (lane >= o) incl += y;
     }
-    const unsigned hit = __ballot_sync(0xffffffffu, c > 0 && item >= run + incl - c && item < run + incl);
+    const unsigned hit = __ballot_sync(0xffffffffu, c > 0 && item >= cur.base + incl - c && item < cur.base + incl);
     if (hit != 0u) {
       const int src = __ffs(hit) - 1;
-      const int base = run + __shfl_sync(0xffffffffu, incl - c, src);
+      const int base = cur.base + __shfl_sync(0xffffffffu, incl - c, src);
       it.nch = __shfl_sync(0xffffffffu, c, src) / a.hkv;
-      it.b = b0 + src;
+      it.b = cur.b + src;
       const int rel = item - base;
       it.hk = rel / it.nch;
       it.chunk = rel - it.hk * it.nch;
       it.first = base + it.hk * it.nch;
+      cur.b = it.b;
+      cur.base = base;
       return it;
     }
-    run += __shfl_sync(0xffffffffu, incl, 31);
+    cur.base += __shfl_sync(0xffffffffu, incl, 31);
+    cur.b += 32;
   }
 }
 
@@ -345,10 +364,10 @@ __device__ Item locate(const AttnArgs& a, const Plan& p, int item, int lane) {
 // writes its unnormalised partial (o, m, l) to the workspace slot of its item
 // and the last CTA of the (sequence, KV head) to arrive (atomic counter, no
 // waiting) combines them and resets the counter.
-template <typename T, int D, int NT>
-__global__ void __launch_bounds__(SplitCfg<D>::kThreads, (D == 64 && NT == 1) ? 3 : 1)
+template <typename T, int D, int NT, int NS>
+__global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1) ? 3 * NS : 1)
     attn_decode_split_kernel(AttnArgs a) {
-  using CF = SplitCfg<D>;
+  using CF = SplitCfg<D, NS>;
   constexpr int W = CF::kWarps;
   constexpr int DT = MmaType<T>::dtype;
   constexpr int PARTS = D * 2 / 16;         // 16-byte pieces per row
@@ -368,15 +387,21 @@ __global__ void __launch_bounds__(SplitCfg<D>::kThreads, (D == 64 && NT == 1) ? 
   // Launched as a programmatic dependent of the previous kernel on the
   // stream: wait for it to finish (its writes visible) before reading inputs.
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  // warp 0 plans and finds this CTA's item; the others read it from shared memory
+  // Persistent: CTA i takes items i, i + grid, i + 2 grid, ... Warp 0 plans,
+  // then finds each item; the others read it from shared memory.
   int* shared_item = last_flag + 1;  // [6]: C, b, hk, chunk, nch, first (b = -1: no item)
+  Plan plan{0, 0};
+  Cursor cur{0, 0};
+  if (warp == 0) plan = make_plan(a, lane);
+  bool first_item = true;
+  for (int item_id = blockIdx.x;; item_id += gridDim.x) {
+  __syncthreads();  // the previous item is done with shared memory
   if (warp == 0) {
-    const Plan pl = make_plan(a, lane);
     if (lane == 0) shared_item[1] = -1;
-    if (int(blockIdx.x) < pl.total) {
-      const Item itm = locate(a, pl, blockIdx.x, lane);
+    if (item_id < plan.total) {
+      const Item itm = locate(a, plan, item_id, lane, cur);
       if (lane == 0) {
-        shared_item[0] = pl.C;
+        shared_item[0] = plan.C;
         shared_item[1] = itm.b;
         shared_item[2] = itm.hk;
         shared_item[3] = itm.chunk;
@@ -428,20 +453,20 @@ __global__ void __launch_bounds__(SplitCfg<D>::kThreads, (D == 64 && NT == 1) ? 
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) mrow[nt][0] = mrow[nt][1] = kNegInf, lrow[nt][0] = lrow[nt][1] = 0.f;
 
-  unsigned char* wbuf = smem + warp * CF::kWarpStage;
+  unsigned char* wbuf = smem + warp * NS * CF::kWarpStage;
   const int part = lane % PARTS, row0 = lane / PARTS;
   const int64_t lane_off = int64_t(hk) * a.head_stride + part * 16;
   const int32_t* tbl = a.tables + int64_t(b) * a.tables_stride;
   const int shift = a.bs_shift;
-  // Stage tokens [s0, s0 + 32): lane l reads the table entry of the stage's
-  // l-th logical block (a stage spans at most 32 blocks).
-  auto load_stage = [&](int s0) {
+  // Stage tokens [s0, s0 + 32) into buffer buf: lane l reads the table entry
+  // of the stage's l-th logical block (a stage spans at most 32 blocks).
+  auto load_stage = [&](int s0, int buf) {
     const int last = min(tok1, s0 + kStageTok) - 1;
     const int lb_first = shift >= 0 ? (s0 >> shift) : s0 / a.block_size;
     const int lb_last = shift >= 0 ? (last >> shift) : last / a.block_size;
     int my_blk = -1;
     if (lb_first + lane <= lb_last && lb_first + lane < a.max_blocks) my_blk = __ldg(tbl + lb_first + lane);
-    unsigned char* kdst = wbuf + part * 16;
+    unsigned char* kdst = wbuf + buf * CF::kWarpStage + part * 16;
     unsigned char* vdst = kdst + CF::kStageBytes;
 #pragma unroll
     for (int i = 0; i < RPL; ++i) {
@@ -483,15 +508,26 @@ __global__ void __launch_bounds__(SplitCfg<D>::kThreads, (D == 64 && NT == 1) ? 
   // division by sqrt(head_dim) and the change of base
   const float scale1 = round_twice ? (a.scale_exact ? a.inv_sqrt_d : 1.f) : a.inv_sqrt_d * kLog2e;
   const int mat = lane >> 3, r8 = lane & 7;
-  if (n_my > 0) load_stage(tok0 + warp * kStageTok);
-  // every load of the first stage is issued: the next kernel may start launching
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // stage i of this warp starts at token tok0 + (warp + i W) * 32; with two
+  // buffers the next stage loads while this one computes
+#pragma unroll
+  for (int i = 0; i < NS - 1; ++i) {
+    if (i < n_my) load_stage(tok0 + (warp + i * W) * kStageTok, i);
+    else cp_async_commit();
+  }
+  if (first_item) {  // this CTA's first loads are issued: the next kernel may start launching
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    first_item = false;
+  }
   for (int it = 0; it < n_my; ++it) {
     const int s0 = tok0 + (warp + it * W) * kStageTok;
-    cp_async_wait<0>();
+    const int nxt = it + NS - 1;
+    if (nxt < n_my) load_stage(tok0 + (warp + nxt * W) * kStageTok, nxt % NS);
+    else cp_async_commit();
+    cp_async_wait<NS - 1>();
     __syncwarp();
-    const unsigned char* Ks = wbuf;
-    const unsigned char* Vs = wbuf + CF::kStageBytes;
+    const unsigned char* Ks = wbuf + (it % NS) * CF::kWarpStage;
+    const unsigned char* Vs = Ks + CF::kStageBytes;
 
     // S^T: two 16-token row tiles x NT 8-head column tiles
     float s[2][NT][4];
@@ -600,7 +636,6 @@ __global__ void __launch_bounds__(SplitCfg<D>::kThreads, (D == 64 && NT == 1) ? 
       }
     }
     __syncwarp();  // every lane is done with the buffer before it is refilled
-    if (it + 1 < n_my) load_stage(s0 + W * kStageTok);
   }
   cp_async_wait<0>();
 #pragma unroll
@@ -660,7 +695,7 @@ __global__ void __launch_bounds__(SplitCfg<D>::kThreads, (D == 64 && NT == 1) ? 
       const float L = cta_l[row];
       store_elem(ob + int64_t(hk * G + row) * a.out_stride_h + d * 2, DT, L > 0.f ? O / L : 0.f);
     }
-    return;
+    continue;
   }
   // partial of this chunk -> the workspace slot of this item
   float* wo = a.ws_o + int64_t(item_first) * GD;
@@ -683,12 +718,12 @@ __global__ void __launch_bounds__(SplitCfg<D>::kThreads, (D == 64 && NT == 1) ? 
   __syncthreads();
   if (threadIdx.x == 0) *last_flag = atom_add_acq_rel_gpu(a.ws_cnt + unit, 1) == my_nch - 1;
   __syncthreads();
-  if (!*last_flag) return;
+  if (!*last_flag) continue;
   // last CTA of the (sequence, KV head): combine every chunk's partial. The
   // row maxima and sums of all chunks and (for up to kCombineRegs chunks)
   // this thread's partial outputs load together, in one round of requests.
   constexpr int kPerThread = (NT * 8 * D + CF::kThreads - 1) / CF::kThreads;  // outputs per thread
-  constexpr int kCombineRegs = 32 / kPerThread > 1 ? 32 / kPerThread : 1;     // 32 registers of partials
+  constexpr int kCombineRegs = AUGUR_KV_ATTN_COMBINE_REGS / kPerThread > 1 ? AUGUR_KV_ATTN_COMBINE_REGS / kPerThread : 1;
   float* cm = reinterpret_cast<float*>(smem);  // [my_nch][16] maxima, then rescale factors
   float* cl = cm + kMaxChunks * 16;            // [my_nch][16] sums
   float pv[kPerThread][kCombineRegs];
@@ -741,6 +776,7 @@ __global__ void __launch_bounds__(SplitCfg<D>::kThreads, (D == 64 && NT == 1) ? 
     }
   }
   if (threadIdx.x == 0) a.ws_cnt[unit] = 0;  // ready for the next launch
+  }  // items
 }
 
 // ---------------------------------------------------------------------------
@@ -822,14 +858,19 @@ namespace {
 
 int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
 
-// Launch shape of the split kernel. The grid is the larger of the resident
-// CTAs (slots) and the (sequence, KV head) units; the kernel picks its chunk
-// size on the device (never below chunk_min) so its work items fit the grid.
-// Partials are indexed by work item (< slots), so the workspace is: one
-// arrival counter per unit, then slots x 32 floats (row maxima and sums),
-// then slots x G x D partial outputs; none when no sequence can split.
+// Launch shape of the split kernel: a persistent grid of the resident CTAs
+// (slots). The kernel picks its chunk size on the device (never below
+// chunk_min) so its work items number at most kItemWaves x slots. Partials
+// are indexed by work item, so the workspace is: one arrival counter per
+// (sequence, KV head) unit, then max_items x 32 floats (row maxima and sums),
+// then max_items x G x D partial outputs; none when no sequence can split.
+#ifndef AUGUR_KV_ATTN_ITEM_WAVES
+#define AUGUR_KV_ATTN_ITEM_WAVES 4
+#endif
+constexpr int kItemWaves = AUGUR_KV_ATTN_ITEM_WAVES;
+
 struct SplitPlan {
-  int chunk_min = 0;
+  int chunk_min = 0, max_items = 0;
   int64_t grid = 0, cnt_bytes = 0, ml_bytes = 0, ws_bytes = 0;
 };
 
@@ -838,12 +879,13 @@ SplitPlan plan_split(int batch, int hkv, int G, int D, int max_seq, int slots, i
   int64_t C = unit;
   while ((int64_t(max_seq) + C - 1) / C > kMaxChunks) C *= 2;
   p.chunk_min = int(C);
+  p.grid = slots;
+  p.max_items = kItemWaves * slots;
   const int64_t units = int64_t(batch) * hkv;
-  p.grid = std::max<int64_t>(units, slots);
-  if (units < slots && max_seq > C) {
+  if (units <= p.max_items && max_seq > C) {
     p.cnt_bytes = align256(units * 4);
-    p.ml_bytes = align256(int64_t(slots) * 32 * 4);
-    p.ws_bytes = p.cnt_bytes + p.ml_bytes + int64_t(slots) * G * D * 4;
+    p.ml_bytes = align256(int64_t(p.max_items) * 32 * 4);
+    p.ws_bytes = p.cnt_bytes + p.ml_bytes + int64_t(p.max_items) * G * D * 4;
   }
   return p;
 }
@@ -853,10 +895,10 @@ bool mma_shape_ok(int dtype, int head_dim, int groups) {
 }
 
 // Resident CTAs of one split-kernel instance on the current device (cached).
-template <typename T, int D, int NT>
+template <typename T, int D, int NT, int NS>
 int split_slots(int* slots_out) {
-  using CF = SplitCfg<D>;
-  auto kern = attn_decode_split_kernel<T, D, NT>;
+  using CF = SplitCfg<D, NS>;
+  auto kern = attn_decode_split_kernel<T, D, NT, NS>;
   static int slots[kMaxDevices] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
@@ -874,14 +916,15 @@ int split_slots(int* slots_out) {
   return AUGUR_KV_OK;
 }
 
-template <typename T, int D, int NT>
+template <typename T, int D, int NT, int NS>
 int launch_split(AttnArgs a, int max_seq, void* ws, int64_t ws_bytes, cudaStream_t st) {
-  using CF = SplitCfg<D>;
+  using CF = SplitCfg<D, NS>;
   int slots = 0;
-  const int rc = split_slots<T, D, NT>(&slots);
+  const int rc = split_slots<T, D, NT, NS>(&slots);
   if (rc != AUGUR_KV_OK) return rc;
   const SplitPlan p = plan_split(a.batch, a.hkv, a.groups, D, max_seq, slots, CF::kChunkUnit);
   a.chunk = p.chunk_min;
+  a.max_items = p.max_items;
   if (p.ws_bytes > 0 && (ws == nullptr || ws_bytes < p.ws_bytes)) {
     // not enough workspace: one chunk per sequence (chunk sizes stay powers of two)
     int64_t C = CF::kChunkUnit;
@@ -906,27 +949,30 @@ int launch_split(AttnArgs a, int max_seq, void* ws, int64_t ws_bytes, cudaStream
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, attn_decode_split_kernel<T, D, NT>, a);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, attn_decode_split_kernel<T, D, NT, NS>, a);
   if (e != cudaSuccess) return fail(AUGUR_KV_ECUDA, "attn_decode_split_kernel: %s", cudaGetErrorString(e));
   return check_launch("attn_decode_split_kernel");
 }
 
-template <typename T, int D, int NT>
+template <typename T, int D, int NT, int NS>
 int64_t split_workspace(int batch, int hkv, int G, int max_seq) {
   int slots = 0;
-  if (split_slots<T, D, NT>(&slots) != AUGUR_KV_OK) return -1;
-  return plan_split(batch, hkv, G, D, max_seq, slots, SplitCfg<D>::kChunkUnit).ws_bytes;
+  if (split_slots<T, D, NT, NS>(&slots) != AUGUR_KV_OK) return -1;
+  return plan_split(batch, hkv, G, D, max_seq, slots, SplitCfg<D, NS>::kChunkUnit).ws_bytes;
 }
 
 template <typename T, int D>
 int launch_split_g(const AttnArgs& a, int max_seq, void* ws, int64_t ws_bytes, cudaStream_t st) {
-  return a.groups <= 8 ? launch_split<T, D, 1>(a, max_seq, ws, ws_bytes, st)
-                       : launch_split<T, D, 2>(a, max_seq, ws, ws_bytes, st);
+  constexpr int NS = D == 64 ? AUGUR_KV_ATTN_STAGES : 1;
+  return a.groups <= 8 ? launch_split<T, D, 1, NS>(a, max_seq, ws, ws_bytes, st)
+                       : launch_split<T, D, 2, NS>(a, max_seq, ws, ws_bytes, st);
 }
 
 template <typename T, int D>
 int64_t split_workspace_g(int batch, int hkv, int G, int max_seq) {
-  return G <= 8 ? split_workspace<T, D, 1>(batch, hkv, G, max_seq) : split_workspace<T, D, 2>(batch, hkv, G, max_seq);
+  constexpr int NS = D == 64 ? AUGUR_KV_ATTN_STAGES : 1;
+  return G <= 8 ? split_workspace<T, D, 1, NS>(batch, hkv, G, max_seq)
+                : split_workspace<T, D, 2, NS>(batch, hkv, G, max_seq);
 }
 
 }  // namespace

@@ -505,6 +505,36 @@ def bench_rope(device, pool, reps: int = 7) -> dict:
             "timed": "CUDA graph of 24 per-layer launches; q, k, v of all layers (450 MB) exceed L2"}
 
 
+def bench_decode_attention_large(device, n_seqs: int = 256) -> dict:
+    """Decode attention at a serving-sized batch: the first n_seqs config-5 (box) lengths
+    (lognormal, median 1024, 64..8192 tokens), random blocks of a pool sized to them, random
+    K/V; one decode step over all 24 layers in a CUDA graph, L2 flushed before each replay.
+    Same algorithmic bytes as the small case: every cached K/V row once plus q and out.
+    """
+    from augur_b200 import sharding
+    from augur_b200.attention import DecodeTables, paged_decode_attention
+
+    import augur_b200 as ab
+
+    lens = sharding.box_lengths()[:n_seqs]
+    nblk = -(-lens // BS)
+    NB = int(nblk.sum()) + 64
+    g = torch.Generator(device=device).manual_seed(21)
+    keys = torch.randn(L, NB, H, BS, D, generator=g, device=device).to(torch.bfloat16)
+    values = torch.randn(L, NB, H, BS, D, generator=g, device=device).to(torch.bfloat16)
+    pool = ab.PagedKVCache(keys=keys, values=values, block_size=BS, allocator=ab.BlockAllocator(NB))
+    perm = np.random.default_rng(21).permutation(NB)
+    tables, cur = [], 0
+    for n, nb in zip(lens, nblk):
+        tables.append(ab.SequenceBlockTable(block_ids=perm[cur : cur + nb].tolist(), block_size=BS, seq_len=int(n)))
+        cur += nb
+    res = bench_decode_attention(device, pool, tables)
+    res.pop("timed", None)
+    res["timed"] = "CUDA graph of 24 per-layer launches, L2 flushed"
+    del pool, keys, values
+    return res
+
+
 def bench_offload(device, pool, tables, n_seqs: int = 16) -> dict:
     """Offload n_seqs config-3 sequences (all layers, K and V) to pinned host memory and restore
     them, both paths, against a copy-engine copy of the same byte count.
@@ -639,6 +669,7 @@ def run_extras(device, handoff_only: bool = False, attention_only: bool = False,
     # 32 sequences (each n + 256 tokens long now) across all 24 layers
     if not (rope_only or offload_only):
         out["decode_attention"] = bench_decode_attention(device, pool, tables)
+        out["decode_attention_256_seqs"] = bench_decode_attention_large(device)
     if attention_only:
         return out
     if not rope_only:
