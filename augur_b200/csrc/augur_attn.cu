@@ -74,6 +74,7 @@ struct AttnArgs {
   // split kernel
   int32_t chunk;      // smallest chunk size the plan may pick (a power of two)
   int32_t max_items;  // work items the plan may create (waves x grid); partial slots in the workspace
+  int32_t* ws_sched;  // [0]: next item to hand out, [1]: CTAs done (dynamic scheduling; null: static)
   int32_t* ws_cnt;
   float* ws_ml;
   float* ws_o;
@@ -211,11 +212,9 @@ struct SplitCfg {
   static constexpr int kPipe = kWarps * NS * kWarpStage;
   // after the token loop the warps' partial results reuse the stage buffers
   static constexpr int kPO = D + 4;  // floats per partial row: the transposing stores hit distinct banks
-  static constexpr int kPartO = kWarps * 16 * kPO * 4;
-  static constexpr int kPartML = kWarps * 16 * 4;
-  static_assert(kPartO + 2 * kPartML <= kPipe, "partials must fit in the stage buffers");
+  static_assert((16 * kPO + 32) * 4 <= NS * kWarpStage, "a warp's partial must fit in its stage buffers");
   static_assert(2 * kMaxChunks * 16 * 4 <= kPipe, "chunk maxima and sums must fit in the stage buffers");
-  static constexpr int kTail = (kWarps * 16 + 16 + 16 + 8) * 4;  // fac, cta_m, cta_l, flag + item
+  static constexpr int kTail = (kWarps * 16 + 16 + 16 + 16) * 4;  // fac, cta_m, cta_l, flag + 2 items
   static constexpr int kBytes = kPipe + kTail;
 };
 
@@ -284,7 +283,12 @@ __device__ __forceinline__ int seq_len_at(const AttnArgs& a, int b) {
   return min(max(0, __ldg(a.seq_lens + b)), a.max_seq);
 }
 
-__device__ Plan make_plan(const AttnArgs& a, int lane) {
+// Batches up to kResidentSeqs keep each sequence's item count in warp 0's
+// registers (lane l holds sequences l, l + 32, l + 64, l + 96), so finding an
+// item needs no memory access.
+constexpr int kResidentSeqs = 128;
+
+__device__ Plan make_plan(const AttnArgs& a, int lane, int (&rc)[4]) {
   Plan p;
   p.C = a.chunk;
   const int64_t units = int64_t(a.batch) * a.hkv;
@@ -293,13 +297,30 @@ __device__ Plan make_plan(const AttnArgs& a, int lane) {
     p.total = int(units);
     return p;
   }
+  // the first 256 lengths in registers, loaded in one round; the rest (larger
+  // batches) re-read per candidate, four loads in flight at a time
+  constexpr int kRegSeqs = 8;
+  int sl[kRegSeqs];
+#pragma unroll
+  for (int k = 0; k < kRegSeqs; ++k) {
+    const int b = lane + 32 * k;
+    sl[k] = b < a.batch ? seq_len_at(a, b) : -1;
+  }
   for (;;) {
     int cnt = 0;
-    for (int b = lane; b < a.batch; b += 32) cnt += chunks_of(seq_len_at(a, b), p.C);
+#pragma unroll
+    for (int k = 0; k < kRegSeqs; ++k) cnt += sl[k] >= 0 ? chunks_of(sl[k], p.C) : 0;
+#pragma unroll 4
+    for (int b = lane + 32 * kRegSeqs; b < a.batch; b += 32) cnt += chunks_of(seq_len_at(a, b), p.C);
     p.total = warp_sum(cnt) * a.hkv;
-    if (p.total <= a.max_items || p.C >= a.max_seq) return p;
+    if (p.total <= a.max_items || p.C >= a.max_seq) break;
     p.C *= 2;
   }
+  if (a.batch <= kResidentSeqs) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) rc[k] = sl[k] >= 0 ? chunks_of(sl[k], p.C) * a.hkv : 0;
+  }
+  return p;
 }
 
 struct Item {
@@ -313,7 +334,7 @@ struct Cursor {
 
 // Item `item` of the plan. A CTA visits its items in increasing order, so the
 // search resumes from the cursor (sequences before it hold only earlier items).
-__device__ Item locate(const AttnArgs& a, const Plan& p, int item, int lane, Cursor& cur) {
+__device__ Item locate(const AttnArgs& a, const Plan& p, int item, int lane, const int (&rc)[4], Cursor& cur) {
   Item it;
   if (p.C >= a.max_seq) {  // every sequence is one chunk
     it.b = item / a.hkv;
@@ -323,9 +344,18 @@ __device__ Item locate(const AttnArgs& a, const Plan& p, int item, int lane, Cur
     it.first = item;
     return it;
   }
+  // cursor: resident batches scan from group cur.b / 32 of the register counts;
+  // others re-read seq_lens from sequence cur.b on
+  const bool resident = a.batch <= kResidentSeqs;
   for (;;) {
     const int b = cur.b + lane;
-    const int c = b < a.batch ? chunks_of(seq_len_at(a, b), p.C) * a.hkv : 0;
+    int c;
+    if (resident) {
+      const int k = cur.b >> 5;
+      c = k == 0 ? rc[0] : k == 1 ? rc[1] : k == 2 ? rc[2] : rc[3];
+    } else {
+      c = b < a.batch ? chunks_of(seq_len_at(a, b), p.C) * a.hkv : 0;
+    }
     int incl = c;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -342,8 +372,10 @@ __device__ Item locate(const AttnArgs& a, const Plan& p, int item, int lane, Cur
       it.hk = rel / it.nch;
       it.chunk = rel - it.hk * it.nch;
       it.first = base + it.hk * it.nch;
-      cur.b = it.b;
-      cur.base = base;
+      if (!resident) {  // resident: the cursor stays at the start of this group of 32
+        cur.b = it.b;
+        cur.base = base;
+      }
       return it;
     }
     cur.base += __shfl_sync(0xffffffffu, incl, 31);
@@ -375,9 +407,10 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
   constexpr int RPL = kStageTok / ROW_STEP; // rows per lane per stage
   constexpr int PO = CF::kPO;
   extern __shared__ __align__(128) unsigned char smem[];
-  float* part_o = reinterpret_cast<float*>(smem);  // [warp][16 heads][PO], aliases the stage buffers
-  float* part_m = reinterpret_cast<float*>(smem + CF::kPartO);
-  float* part_l = part_m + W * 16;
+  // after the token loop warp w's partial sits in its own stage buffers:
+  // wwpart[w * WSF + head * PO + dim], maxima at + 16 PO, sums at + 16 PO + 16
+  const float* wpart = reinterpret_cast<const float*>(smem);
+  constexpr int WSF = NS * CF::kWarpStage / 4;
   float* fac = reinterpret_cast<float*>(smem + CF::kPipe);  // [warps][16]
   float* cta_m = fac + W * 16;
   float* cta_l = cta_m + 16;
@@ -388,32 +421,60 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
   // stream: wait for it to finish (its writes visible) before reading inputs.
   asm volatile("griddepcontrol.wait;" ::: "memory");
   // Persistent: CTA i takes items i, i + grid, i + 2 grid, ... Warp 0 plans,
-  // then finds each item; the others read it from shared memory.
-  int* shared_item = last_flag + 1;  // [6]: C, b, hk, chunk, nch, first (b = -1: no item)
+  // then finds each item one item ahead (while its own loads for the current
+  // item are in flight) and publishes it in a double-buffered descriptor.
+  int* desc = last_flag + 1;  // [2][6]: C, b, hk, chunk, nch, first (b = -1: no item)
   Plan plan{0, 0};
   Cursor cur{0, 0};
-  if (warp == 0) plan = make_plan(a, lane);
-  bool first_item = true;
-  for (int item_id = blockIdx.x;; item_id += gridDim.x) {
-  __syncthreads();  // the previous item is done with shared memory
-  if (warp == 0) {
-    if (lane == 0) shared_item[1] = -1;
-    if (item_id < plan.total) {
-      const Item itm = locate(a, plan, item_id, lane, cur);
+  int rc[4] = {0, 0, 0, 0};  // warp 0: item counts of sequences lane + 32 k (batches <= 128)
+  auto publish = [&](int slot, int id) {  // warp 0, all lanes
+    int* d = desc + slot * 6;
+    if (id < plan.total) {
+      const Item itm = locate(a, plan, id, lane, rc, cur);
       if (lane == 0) {
-        shared_item[0] = plan.C;
-        shared_item[1] = itm.b;
-        shared_item[2] = itm.hk;
-        shared_item[3] = itm.chunk;
-        shared_item[4] = itm.nch;
-        shared_item[5] = itm.first;
+        d[0] = plan.C;
+        d[1] = itm.b;
+        d[2] = itm.hk;
+        d[3] = itm.chunk;
+        d[4] = itm.nch;
+        d[5] = itm.first;
       }
+    } else if (lane == 0) {
+      d[1] = -1;
     }
+  };
+  // CTA i's first item is i; later ones come from an atomic counter (items
+  // grid, grid + 1, ...) when there is a workspace, the last CTA to finish
+  // resetting it, else CTA i takes i + grid, i + 2 grid, ...
+  int32_t* sched = a.ws_sched;
+  int static_next = blockIdx.x;
+  auto next_id = [&]() -> int {  // warp 0, all lanes
+    int id = static_next;
+    if (sched != nullptr && static_next >= int(gridDim.x)) {
+      if (lane == 0) id = int(gridDim.x) + atomicAdd(sched, 1);
+      id = __shfl_sync(0xffffffffu, id, 0);
+    }
+    static_next += gridDim.x;
+    return id;
+  };
+  if (warp == 0) {
+    plan = make_plan(a, lane, rc);
+    publish(0, next_id());
   }
-  __syncthreads();
-  if (shared_item[1] < 0) return;
-  const int plan_C = shared_item[0], b = shared_item[1], hk = shared_item[2], chunk = shared_item[3];
-  const int my_nch = shared_item[4], item_first = shared_item[5];
+  bool first_item = true;
+  int slot = 0;
+  for (;; slot ^= 1) {
+  __syncthreads();  // descriptor `slot` is published; the previous item is done with shared memory
+  const int* d = desc + slot * 6;
+  if (d[1] < 0) {
+    if (sched != nullptr && threadIdx.x == 0 && atomicAdd(sched + 1, 1) == int(gridDim.x) - 1) {
+      sched[0] = 0;  // every CTA has taken its last id: ready for the next launch
+      sched[1] = 0;
+    }
+    return;
+  }
+  const int plan_C = d[0], b = d[1], hk = d[2], chunk = d[3];
+  const int my_nch = d[4], item_first = d[5];
   const int S = seq_len_at(a, b);
   if (chunk == 0 && threadIdx.x == 0 && __ldg(a.seq_lens + b) > a.max_seq)
     record_status(a.status, AUGUR_KV_EBOUNDS);  // the host sized the launch with max_seq_len
@@ -508,10 +569,10 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
   // division by sqrt(head_dim) and the change of base
   const float scale1 = round_twice ? (a.scale_exact ? a.inv_sqrt_d : 1.f) : a.inv_sqrt_d * kLog2e;
   const int mat = lane >> 3, r8 = lane & 7;
-  // stage i of this warp starts at token tok0 + (warp + i W) * 32; with two
-  // buffers the next stage loads while this one computes
+  // stage i of this warp starts at token tok0 + (warp + i W) * 32; the first
+  // NS stages load up front, and each buffer refills as soon as it is computed
 #pragma unroll
-  for (int i = 0; i < NS - 1; ++i) {
+  for (int i = 0; i < NS; ++i) {
     if (i < n_my) load_stage(tok0 + (warp + i * W) * kStageTok, i);
     else cp_async_commit();
   }
@@ -519,11 +580,9 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     first_item = false;
   }
+  if (warp == 0) publish(slot ^ 1, next_id());  // overlaps this warp's loads
   for (int it = 0; it < n_my; ++it) {
     const int s0 = tok0 + (warp + it * W) * kStageTok;
-    const int nxt = it + NS - 1;
-    if (nxt < n_my) load_stage(tok0 + (warp + nxt * W) * kStageTok, nxt % NS);
-    else cp_async_commit();
     cp_async_wait<NS - 1>();
     __syncwarp();
     const unsigned char* Ks = wbuf + (it % NS) * CF::kWarpStage;
@@ -636,6 +695,9 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
       }
     }
     __syncwarp();  // every lane is done with the buffer before it is refilled
+    const int nxt = it + NS;
+    if (nxt < n_my) load_stage(tok0 + (warp + nxt * W) * kStageTok, nxt % NS);
+    else cp_async_commit();
   }
   cp_async_wait<0>();
 #pragma unroll
@@ -647,24 +709,26 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
       lrow[nt][j] += __shfl_xor_sync(0xffffffffu, lrow[nt][j], 16);
     }
   }
-  __syncthreads();  // every warp is done with the stage buffers the partials reuse
-
-  // warps -> CTA: part_o[warp][head][dim] (the stores transpose O^T back)
+  // warp -> its own stage buffer, which no other warp touches: [16 heads][PO]
+  // partial outputs (the stores transpose O^T back), then 16 maxima, 16 sums
+  {
+    float* wp = reinterpret_cast<float*>(wbuf);
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
+    for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-    for (int dm = 0; dm < D / 16; ++dm) {
+      for (int dm = 0; dm < D / 16; ++dm) {
 #pragma unroll
-      for (int f = 0; f < 4; ++f) {
-        const int head = nt * 8 + 2 * t + (f & 1), dim = dm * 16 + g + (f >> 1) * 8;
-        part_o[(warp * 16 + head) * PO + dim] = o[dm][nt][f];
+        for (int f = 0; f < 4; ++f) {
+          const int head = nt * 8 + 2 * t + (f & 1), dim = dm * 16 + g + (f >> 1) * 8;
+          wp[head * PO + dim] = o[dm][nt][f];
+        }
       }
-    }
-    if (g == 0) {
+      if (g == 0) {
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        part_m[warp * 16 + nt * 8 + 2 * t + j] = mrow[nt][j];
-        part_l[warp * 16 + nt * 8 + 2 * t + j] = lrow[nt][j];
+        for (int j = 0; j < 2; ++j) {
+          wp[16 * PO + nt * 8 + 2 * t + j] = mrow[nt][j];
+          wp[16 * PO + 16 + nt * 8 + 2 * t + j] = lrow[nt][j];
+        }
       }
     }
   }
@@ -672,13 +736,13 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
   if (int(threadIdx.x) < G) {
     const int row = threadIdx.x;
     float M = kNegInf;
-    for (int w = 0; w < W; ++w) M = fmaxf(M, part_m[w * 16 + row]);
+    for (int w = 0; w < W; ++w) M = fmaxf(M, wpart[w * WSF + 16 * PO + row]);
     float L = 0.f;
     for (int w = 0; w < W; ++w) {
-      const float mw = part_m[w * 16 + row];
+      const float mw = wpart[w * WSF + 16 * PO + row];
       const float f = mw == kNegInf ? 0.f : ex2(mw - M);
       fac[w * 16 + row] = f;
-      L += part_l[w * 16 + row] * f;
+      L += wpart[w * WSF + 16 * PO + 16 + row] * f;
     }
     cta_m[row] = M;
     cta_l[row] = L;
@@ -691,7 +755,7 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
       const int row = i / D, d = i - row * D;
       float O = 0.f;
 #pragma unroll
-      for (int w = 0; w < W; ++w) O += part_o[(w * 16 + row) * PO + d] * fac[w * 16 + row];
+      for (int w = 0; w < W; ++w) O += wpart[w * WSF + row * PO + d] * fac[w * 16 + row];
       const float L = cta_l[row];
       store_elem(ob + int64_t(hk * G + row) * a.out_stride_h + d * 2, DT, L > 0.f ? O / L : 0.f);
     }
@@ -704,7 +768,7 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
     const int row = i / D, d = i - row * D;
     float O = 0.f;
 #pragma unroll
-    for (int w = 0; w < W; ++w) O += part_o[(w * 16 + row) * PO + d] * fac[w * 16 + row];
+    for (int w = 0; w < W; ++w) O += wpart[w * WSF + row * PO + d] * fac[w * 16 + row];
     wo[int64_t(chunk) * GD + i] = O;
   }
   if (int(threadIdx.x) < G) {
@@ -882,10 +946,14 @@ SplitPlan plan_split(int batch, int hkv, int G, int D, int max_seq, int slots, i
   p.grid = slots;
   p.max_items = kItemWaves * slots;
   const int64_t units = int64_t(batch) * hkv;
+  // scheduler counters, then per-unit arrival counters when a sequence can split
+  p.cnt_bytes = 256;
   if (units <= p.max_items && max_seq > C) {
-    p.cnt_bytes = align256(units * 4);
+    p.cnt_bytes += align256(units * 4);
     p.ml_bytes = align256(int64_t(p.max_items) * 32 * 4);
     p.ws_bytes = p.cnt_bytes + p.ml_bytes + int64_t(p.max_items) * G * D * 4;
+  } else {
+    p.ws_bytes = p.cnt_bytes;
   }
   return p;
 }
@@ -925,14 +993,17 @@ int launch_split(AttnArgs a, int max_seq, void* ws, int64_t ws_bytes, cudaStream
   const SplitPlan p = plan_split(a.batch, a.hkv, a.groups, D, max_seq, slots, CF::kChunkUnit);
   a.chunk = p.chunk_min;
   a.max_items = p.max_items;
-  if (p.ws_bytes > 0 && (ws == nullptr || ws_bytes < p.ws_bytes)) {
-    // not enough workspace: one chunk per sequence (chunk sizes stay powers of two)
+  if (ws == nullptr || ws_bytes < p.ws_bytes) {
+    // not enough workspace: one chunk per sequence (chunk sizes stay powers of
+    // two), items taken statically; with the scheduler counters alone, dynamically
     int64_t C = CF::kChunkUnit;
     while (C < max_seq) C *= 2;
     a.chunk = int(C);
-  } else if (p.ws_bytes > 0) {
+    if (ws != nullptr && ws_bytes >= 256) a.ws_sched = static_cast<int32_t*>(ws);
+  } else {
     char* w = static_cast<char*>(ws);
-    a.ws_cnt = reinterpret_cast<int32_t*>(w);
+    a.ws_sched = reinterpret_cast<int32_t*>(w);
+    a.ws_cnt = reinterpret_cast<int32_t*>(w + 256);
     a.ws_ml = reinterpret_cast<float*>(w + p.cnt_bytes);
     a.ws_o = reinterpret_cast<float*>(w + p.cnt_bytes + p.ml_bytes);
   }

@@ -974,6 +974,8 @@ def main() -> None:
     ap.add_argument("--handoff-only", action="store_true", help="profiling case: config-3 handoff only")
     ap.add_argument("--attention-only", action="store_true",
                     help="profiling case: config-3 cache, then decode attention over all layers")
+    ap.add_argument("--attention-large-only", action="store_true",
+                    help="profiling case: decode attention over 128 box-length sequences (about 2.2 GB)")
     ap.add_argument("--offload-only", action="store_true",
                     help="config-3 cache, then offload to pinned host memory and restore")
     ap.add_argument("--rope-only", action="store_true",
@@ -990,6 +992,10 @@ def main() -> None:
     if args.handoff_only:  # profiling case: only the config-3 handoff (about 3 GB on the device)
         torch.cuda.set_device(0)
         emit(run_extras(torch.device("cuda", 0), handoff_only=True))
+        return
+    if args.attention_large_only:  # profiling case: decode attention over 128 box-length sequences
+        torch.cuda.set_device(0)
+        emit({"decode_attention_128_seqs": bench_decode_attention_large(torch.device("cuda", 0), n_seqs=128)})
         return
     if args.offload_only:  # config-3 pool, then offload to pinned host memory and restore
         torch.cuda.set_device(0)
