@@ -70,9 +70,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "augur_kv_paged_decode_attention": (
         ctypes.c_int,
         [_P, _I64P, _P, _P, _I64P, _I64, _I32, _P, _I64, _I64, _P, _I32, _I32, _I32, _I32, _I32, _I32,
-         _P, _I64P, _I32, _P, _I64, _P, _P],
+         _P, _I64P, _I32, _P, _I64, _P, _I64, _P, _P],
     ),
-    "augur_kv_paged_decode_attention_workspace": (_I64, [_I32, _I32, _I32, _I32, _I32, _I32, _I32]),
+    "augur_kv_paged_decode_attention_workspace": (
+        ctypes.c_int, [_I32, _I32, _I32, _I32, _I32, _I32, _I32, _I64P, _I64P]),
     "augur_kv_rope_scatter": (
         ctypes.c_int,
         [_P, _P, _I64P, _I64P, _I64, _I32, _P, _P, _I64P, _I64, _I64, _P, _I64P, _I64, _P, _I64P, _P, _P, _I64,

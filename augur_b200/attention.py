@@ -14,6 +14,7 @@ order.
 
 from __future__ import annotations
 
+import ctypes
 from collections.abc import Sequence
 
 import numpy as np
@@ -24,27 +25,36 @@ from . import _lib, _ops
 from .paged_kv_cache import PagedKVCache, SequenceBlockTable
 
 
-# Zero-initialised workspaces of the split kernel, one per (device, stream):
-# launches on one stream run in order, so they can share one.
-_workspaces: dict[tuple[int, int], Tensor] = {}
+# Counters (zeroed once; every launch leaves them zero) and scratch of the split
+# kernel, one pair per (device, stream): launches on one stream run in order,
+# so they can share them whatever their sizes.
+_workspaces: dict[tuple[int, int], tuple[Tensor, Tensor]] = {}
 
 
-def _workspace(lib, device: torch.device, st: torch.cuda.Stream, sizes: tuple) -> tuple[int, int, Tensor | None]:
-    """(pointer, bytes, tensor) of a workspace large enough for these sizes."""
-    need = int(lib.augur_kv_paged_decode_attention_workspace(*sizes))
-    if need < 0:
-        _lib.check(_lib.EINVAL, "augur_kv_paged_decode_attention_workspace")
-    if need == 0:
-        return 0, 0, None
+def workspace_bytes(lib, sizes: tuple) -> tuple[int, int]:
+    """(counters, scratch) bytes augur_kv_paged_decode_attention needs for these sizes."""
+    cnt, scr = ctypes.c_int64(0), ctypes.c_int64(0)
+    _lib.check(lib.augur_kv_paged_decode_attention_workspace(*sizes, ctypes.byref(cnt), ctypes.byref(scr)),
+               "augur_kv_paged_decode_attention_workspace")
+    return cnt.value, scr.value
+
+
+def _workspace(lib, device: torch.device, st: torch.cuda.Stream, sizes: tuple) -> tuple[Tensor | None, Tensor | None]:
+    """Counters and scratch tensors large enough for these sizes (None when not needed)."""
+    need_c, need_s = workspace_bytes(lib, sizes)
+    if need_c == 0 and need_s == 0:
+        return None, None
     key = (device.index, st.cuda_stream)
-    ws = _workspaces.get(key)
-    if ws is None or ws.numel() < need:
-        with torch.cuda.stream(st):
-            ws = torch.zeros(need, dtype=torch.uint8, device=device)
-        if not torch.cuda.is_current_stream_capturing():
-            # memory allocated during a graph capture belongs to that graph
-            _workspaces[key] = ws
-    return ws.data_ptr(), ws.numel(), ws
+    cnt, scr = _workspaces.get(key, (None, None))
+    capturing = torch.cuda.is_current_stream_capturing()
+    with torch.cuda.stream(st):
+        if cnt is None or cnt.numel() * 4 < need_c:
+            cnt = torch.zeros(max(1, -(-need_c // 4)), dtype=torch.int32, device=device)
+        if need_s and (scr is None or scr.numel() < need_s):
+            scr = torch.empty(need_s, dtype=torch.uint8, device=device)
+    if not capturing:  # memory allocated during a graph capture belongs to that graph
+        _workspaces[key] = (cnt, scr)
+    return cnt, scr
 
 
 class DecodeTables:
@@ -130,17 +140,19 @@ def paged_decode_attention(
     flags = _lib.ATTN_GENERIC if generic else _lib.ATTN_AUTO
     dcode = _ops.dtype_code(q3)
     with _ops._DeviceGuard(device):
-        ws_ptr, ws_bytes, ws = _workspace(lib, device, st, (B, Hq, Hkv, D, dt.max_seq_len, dcode, flags))
+        cnt, scr = _workspace(lib, device, st, (B, Hq, Hkv, D, dt.max_seq_len, dcode, flags))
         code = lib.augur_kv_paged_decode_attention(
             q3.data_ptr(), _lib.i64_array((q3.stride(0), q3.stride(1))),
             kc.data_ptr(), vc.data_ptr(), _lib.i64_array((kc.stride(0), kc.stride(1), kc.stride(2))),
             NB, bs, dt.blocks.data_ptr(), dt.blocks.stride(0), dt.blocks.shape[1],
             dt.lens.data_ptr(), dt.max_seq_len, B, Hq, Hkv, D, dcode,
             out3.data_ptr(), _lib.i64_array((out3.stride(0), out3.stride(1))), flags,
-            ws_ptr, ws_bytes, _ops.status_word(device).data_ptr(), st.cuda_stream)
+            cnt.data_ptr() if cnt is not None else None, cnt.numel() * 4 if cnt is not None else 0,
+            scr.data_ptr() if scr is not None else None, scr.numel() if scr is not None else 0,
+            _ops.status_word(device).data_ptr(), st.cuda_stream)
     _lib.check(code, "augur_kv_paged_decode_attention")
     _ops.launch_count += 1
-    _ops.keep_until_done(st, q3, dt.blocks, dt.lens, *([ws] if ws is not None else []))
+    _ops.keep_until_done(st, q3, dt.blocks, dt.lens, cnt, scr)
     if out is not None:
         return out
     return out3.unsqueeze(2) if squeeze else out3

@@ -15,7 +15,7 @@
 //    warp stages 32 tokens of K and V in shared memory with cp.async and
 //    runs both products transposed on mma.sync m16n8k16 (tokens, not the
 //    few query heads of a group, fill the 16 rows) around an online softmax.
-//    Chunks of one sequence combine through a caller-provided workspace: the
+//    Chunks of one sequence combine through caller-provided counters and scratch: the
 //    last CTA to arrive (an atomic counter; no CTA ever waits) merges the
 //    partials and writes the output.
 //  * attn_decode_generic_kernel (any dtype / shape): one CTA per (sequence,
@@ -73,8 +73,8 @@ struct AttnArgs {
   int32_t bs_shift;  // log2(block_size) when it is a power of two, else -1
   // split kernel
   int32_t chunk;      // smallest chunk size the plan may pick (a power of two)
-  int32_t max_items;  // work items the plan may create (waves x grid); partial slots in the workspace
-  int32_t* ws_sched;  // [0]: next item to hand out, [1]: CTAs done (dynamic scheduling; null: static)
+  int32_t max_items;  // work items the plan may create (waves x grid); partial slots in the scratch
+  int32_t* ws_sched;  // counters [0]: next item to hand out, [1]: CTAs done (null: static items)
   int32_t* ws_cnt;
   float* ws_ml;
   float* ws_o;
@@ -393,7 +393,7 @@ __device__ Item locate(const AttnArgs& a, const Plan& p, int item, int lane, con
 // with P^T moved into the B-operand layout by movmatrix. NT = 1 serves up to
 // 8 query heads per KV head, NT = 2 up to 16. Warps combine in shared memory.
 // A sequence of one chunk writes its output directly; otherwise each CTA
-// writes its unnormalised partial (o, m, l) to the workspace slot of its item
+// writes its unnormalised partial (o, m, l) to the scratch slot of its item
 // and the last CTA of the (sequence, KV head) to arrive (atomic counter, no
 // waiting) combines them and resets the counter.
 template <typename T, int D, int NT, int NS>
@@ -444,7 +444,7 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
     }
   };
   // CTA i's first item is i; later ones come from an atomic counter (items
-  // grid, grid + 1, ...) when there is a workspace, the last CTA to finish
+  // grid, grid + 1, ...) when there are counters, the last CTA to finish
   // resetting it, else CTA i takes i + grid, i + 2 grid, ...
   int32_t* sched = a.ws_sched;
   int static_next = blockIdx.x;
@@ -761,7 +761,7 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
     }
     continue;
   }
-  // partial of this chunk -> the workspace slot of this item
+  // partial of this chunk -> the scratch slot of this item
   float* wo = a.ws_o + int64_t(item_first) * GD;
   float* wml = a.ws_ml + int64_t(item_first) * 32;
   for (int i = threadIdx.x; i < GD; i += blockDim.x) {
@@ -924,18 +924,22 @@ int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
 
 // Launch shape of the split kernel: a persistent grid of the resident CTAs
 // (slots). The kernel picks its chunk size on the device (never below
-// chunk_min) so its work items number at most kItemWaves x slots. Partials
-// are indexed by work item, so the workspace is: one arrival counter per
-// (sequence, KV head) unit, then max_items x 32 floats (row maxima and sums),
-// then max_items x G x D partial outputs; none when no sequence can split.
+// chunk_min) so its work items number at most kItemWaves x slots.
+// Counters (zero before the first launch, left zero by every launch, never
+// used for data, so launches of any size may share them): two scheduler words
+// padded to 256 bytes, then one arrival counter per (sequence, KV head) unit
+// when a sequence can split. Scratch (no initial contents), indexed by work
+// item: max_items x 32 floats (row maxima and sums), then max_items x G x D
+// partial outputs; none when no sequence can split.
 #ifndef AUGUR_KV_ATTN_ITEM_WAVES
 #define AUGUR_KV_ATTN_ITEM_WAVES 4
 #endif
 constexpr int kItemWaves = AUGUR_KV_ATTN_ITEM_WAVES;
+constexpr int64_t kSchedBytes = 256;
 
 struct SplitPlan {
   int chunk_min = 0, max_items = 0;
-  int64_t grid = 0, cnt_bytes = 0, ml_bytes = 0, ws_bytes = 0;
+  int64_t grid = 0, cnt_bytes = 0, ml_bytes = 0, scratch_bytes = 0;
 };
 
 SplitPlan plan_split(int batch, int hkv, int G, int D, int max_seq, int slots, int unit) {
@@ -946,14 +950,11 @@ SplitPlan plan_split(int batch, int hkv, int G, int D, int max_seq, int slots, i
   p.grid = slots;
   p.max_items = kItemWaves * slots;
   const int64_t units = int64_t(batch) * hkv;
-  // scheduler counters, then per-unit arrival counters when a sequence can split
-  p.cnt_bytes = 256;
+  p.cnt_bytes = kSchedBytes;
   if (units <= p.max_items && max_seq > C) {
-    p.cnt_bytes += align256(units * 4);
+    p.cnt_bytes += units * 4;
     p.ml_bytes = align256(int64_t(p.max_items) * 32 * 4);
-    p.ws_bytes = p.cnt_bytes + p.ml_bytes + int64_t(p.max_items) * G * D * 4;
-  } else {
-    p.ws_bytes = p.cnt_bytes;
+    p.scratch_bytes = p.ml_bytes + int64_t(p.max_items) * G * D * 4;
   }
   return p;
 }
@@ -985,7 +986,8 @@ int split_slots(int* slots_out) {
 }
 
 template <typename T, int D, int NT, int NS>
-int launch_split(AttnArgs a, int max_seq, void* ws, int64_t ws_bytes, cudaStream_t st) {
+int launch_split(AttnArgs a, int max_seq, int32_t* cnt, int64_t cnt_bytes, void* scratch, int64_t scratch_bytes,
+                 cudaStream_t st) {
   using CF = SplitCfg<D, NS>;
   int slots = 0;
   const int rc = split_slots<T, D, NT, NS>(&slots);
@@ -993,19 +995,17 @@ int launch_split(AttnArgs a, int max_seq, void* ws, int64_t ws_bytes, cudaStream
   const SplitPlan p = plan_split(a.batch, a.hkv, a.groups, D, max_seq, slots, CF::kChunkUnit);
   a.chunk = p.chunk_min;
   a.max_items = p.max_items;
-  if (ws == nullptr || ws_bytes < p.ws_bytes) {
-    // not enough workspace: one chunk per sequence (chunk sizes stay powers of
-    // two), items taken statically; with the scheduler counters alone, dynamically
+  if (cnt != nullptr && cnt_bytes >= kSchedBytes) a.ws_sched = cnt;  // dynamic item scheduling
+  if (p.scratch_bytes > 0 && cnt != nullptr && cnt_bytes >= p.cnt_bytes && scratch != nullptr &&
+      scratch_bytes >= p.scratch_bytes) {
+    a.ws_cnt = cnt + kSchedBytes / 4;
+    a.ws_ml = static_cast<float*>(scratch);
+    a.ws_o = reinterpret_cast<float*>(static_cast<char*>(scratch) + p.ml_bytes);
+  } else {
+    // no room to combine chunks: one chunk per sequence (chunk sizes stay powers of two)
     int64_t C = CF::kChunkUnit;
     while (C < max_seq) C *= 2;
     a.chunk = int(C);
-    if (ws != nullptr && ws_bytes >= 256) a.ws_sched = static_cast<int32_t*>(ws);
-  } else {
-    char* w = static_cast<char*>(ws);
-    a.ws_sched = reinterpret_cast<int32_t*>(w);
-    a.ws_cnt = reinterpret_cast<int32_t*>(w + 256);
-    a.ws_ml = reinterpret_cast<float*>(w + p.cnt_bytes);
-    a.ws_o = reinterpret_cast<float*>(w + p.cnt_bytes + p.ml_bytes);
   }
   // programmatic dependent launch: the CTAs may become resident while the
   // previous kernel drains; the kernel waits for it before reading anything
@@ -1026,57 +1026,65 @@ int launch_split(AttnArgs a, int max_seq, void* ws, int64_t ws_bytes, cudaStream
 }
 
 template <typename T, int D, int NT, int NS>
-int64_t split_workspace(int batch, int hkv, int G, int max_seq) {
+int split_workspace(int batch, int hkv, int G, int max_seq, int64_t* cnt_bytes, int64_t* scratch_bytes) {
   int slots = 0;
-  if (split_slots<T, D, NT, NS>(&slots) != AUGUR_KV_OK) return -1;
-  return plan_split(batch, hkv, G, D, max_seq, slots, SplitCfg<D, NS>::kChunkUnit).ws_bytes;
+  const int rc = split_slots<T, D, NT, NS>(&slots);
+  if (rc != AUGUR_KV_OK) return rc;
+  const SplitPlan p = plan_split(batch, hkv, G, D, max_seq, slots, SplitCfg<D, NS>::kChunkUnit);
+  *cnt_bytes = p.cnt_bytes;
+  *scratch_bytes = p.scratch_bytes;
+  return AUGUR_KV_OK;
 }
 
 template <typename T, int D>
-int launch_split_g(const AttnArgs& a, int max_seq, void* ws, int64_t ws_bytes, cudaStream_t st) {
+int launch_split_g(const AttnArgs& a, int max_seq, int32_t* cnt, int64_t cnt_bytes, void* scratch,
+                   int64_t scratch_bytes, cudaStream_t st) {
   constexpr int NS = D == 64 ? AUGUR_KV_ATTN_STAGES : 1;
-  return a.groups <= 8 ? launch_split<T, D, 1, NS>(a, max_seq, ws, ws_bytes, st)
-                       : launch_split<T, D, 2, NS>(a, max_seq, ws, ws_bytes, st);
+  return a.groups <= 8 ? launch_split<T, D, 1, NS>(a, max_seq, cnt, cnt_bytes, scratch, scratch_bytes, st)
+                       : launch_split<T, D, 2, NS>(a, max_seq, cnt, cnt_bytes, scratch, scratch_bytes, st);
 }
 
 template <typename T, int D>
-int64_t split_workspace_g(int batch, int hkv, int G, int max_seq) {
+int split_workspace_g(int batch, int hkv, int G, int max_seq, int64_t* cnt_bytes, int64_t* scratch_bytes) {
   constexpr int NS = D == 64 ? AUGUR_KV_ATTN_STAGES : 1;
-  return G <= 8 ? split_workspace<T, D, 1, NS>(batch, hkv, G, max_seq)
-                : split_workspace<T, D, 2, NS>(batch, hkv, G, max_seq);
+  return G <= 8 ? split_workspace<T, D, 1, NS>(batch, hkv, G, max_seq, cnt_bytes, scratch_bytes)
+                : split_workspace<T, D, 2, NS>(batch, hkv, G, max_seq, cnt_bytes, scratch_bytes);
 }
 
 }  // namespace
 
-AUGUR_KV_EXPORT int64_t augur_kv_paged_decode_attention_workspace(int32_t batch, int32_t n_q_heads,
-                                                                  int32_t n_kv_heads, int32_t head_dim,
-                                                                  int32_t max_seq_len, int32_t dtype,
-                                                                  int32_t flags) {
+AUGUR_KV_EXPORT int augur_kv_paged_decode_attention_workspace(int32_t batch, int32_t n_q_heads, int32_t n_kv_heads,
+                                                              int32_t head_dim, int32_t max_seq_len, int32_t dtype,
+                                                              int32_t flags, int64_t* counters_bytes,
+                                                              int64_t* scratch_bytes) {
   g_last_error[0] = '\0';
+  if (counters_bytes == nullptr || scratch_bytes == nullptr)
+    return fail(AUGUR_KV_EINVAL, "paged_decode_attention_workspace: null pointer argument");
+  *counters_bytes = 0;
+  *scratch_bytes = 0;
   if (elem_size(dtype) == 0 || batch < 0 || max_seq_len < 0 || n_q_heads <= 0 || n_kv_heads <= 0 ||
-      n_q_heads % n_kv_heads != 0 || head_dim <= 0) {
-    fail(AUGUR_KV_EINVAL, "paged_decode_attention_workspace: bad sizes");
-    return -1;
-  }
+      n_q_heads % n_kv_heads != 0 || head_dim <= 0)
+    return fail(AUGUR_KV_EINVAL, "paged_decode_attention_workspace: bad sizes");
   const int G = n_q_heads / n_kv_heads;
-  if (batch == 0 || flags == AUGUR_KV_ATTN_GENERIC || !mma_shape_ok(dtype, head_dim, G)) return 0;
-  if (max_seq_len > kMaxSeq) {
-    fail(AUGUR_KV_EINVAL, "paged_decode_attention_workspace: max_seq_len above %d", kMaxSeq);
-    return -1;
-  }
+  if (batch == 0 || flags == AUGUR_KV_ATTN_GENERIC || !mma_shape_ok(dtype, head_dim, G)) return AUGUR_KV_OK;
+  if (max_seq_len > kMaxSeq)
+    return fail(AUGUR_KV_EINVAL, "paged_decode_attention_workspace: max_seq_len above %d", kMaxSeq);
   if (dtype == AUGUR_KV_BF16)
-    return head_dim == 64 ? split_workspace_g<__nv_bfloat16, 64>(batch, n_kv_heads, G, max_seq_len)
-                          : split_workspace_g<__nv_bfloat16, 128>(batch, n_kv_heads, G, max_seq_len);
-  return head_dim == 64 ? split_workspace_g<__half, 64>(batch, n_kv_heads, G, max_seq_len)
-                        : split_workspace_g<__half, 128>(batch, n_kv_heads, G, max_seq_len);
+    return head_dim == 64
+               ? split_workspace_g<__nv_bfloat16, 64>(batch, n_kv_heads, G, max_seq_len, counters_bytes, scratch_bytes)
+               : split_workspace_g<__nv_bfloat16, 128>(batch, n_kv_heads, G, max_seq_len, counters_bytes,
+                                                       scratch_bytes);
+  return head_dim == 64 ? split_workspace_g<__half, 64>(batch, n_kv_heads, G, max_seq_len, counters_bytes, scratch_bytes)
+                        : split_workspace_g<__half, 128>(batch, n_kv_heads, G, max_seq_len, counters_bytes,
+                                                         scratch_bytes);
 }
 
 AUGUR_KV_EXPORT int augur_kv_paged_decode_attention(
     const void* q, const int64_t* q_strides, const void* k_pool, const void* v_pool, const int64_t* pool_strides,
     int64_t num_blocks, int32_t block_size, const int32_t* block_tables, int64_t tables_stride, int64_t max_blocks,
     const int32_t* seq_lens, int32_t max_seq_len, int32_t batch, int32_t n_q_heads, int32_t n_kv_heads,
-    int32_t head_dim, int32_t dtype, void* out, const int64_t* out_strides, int32_t flags, void* workspace,
-    int64_t workspace_bytes, int32_t* status, void* stream) {
+    int32_t head_dim, int32_t dtype, void* out, const int64_t* out_strides, int32_t flags, int32_t* counters,
+    int64_t counters_bytes, void* scratch, int64_t scratch_bytes, int32_t* status, void* stream) {
   g_last_error[0] = '\0';
   const int es = elem_size(dtype);
   if (es == 0) return fail(AUGUR_KV_EINVAL, "paged_decode_attention: unknown dtype %d", dtype);
@@ -1127,9 +1135,9 @@ AUGUR_KV_EXPORT int augur_kv_paged_decode_attention(
 
   a.max_seq = max_seq_len;
   a.bs_shift = (block_size & (block_size - 1)) == 0 ? __builtin_ctz(unsigned(block_size)) : -1;
-  if (workspace_bytes < 0 || (workspace == nullptr && workspace_bytes != 0) ||
-      (reinterpret_cast<uintptr_t>(workspace) & 15u) != 0)
-    return fail(AUGUR_KV_EINVAL, "paged_decode_attention: workspace must be 16-byte aligned, bytes >= 0");
+  if (counters_bytes < 0 || scratch_bytes < 0 || (reinterpret_cast<uintptr_t>(counters) & 3u) != 0 ||
+      (reinterpret_cast<uintptr_t>(scratch) & 15u) != 0)
+    return fail(AUGUR_KV_EINVAL, "paged_decode_attention: counters 4-byte and scratch 16-byte aligned, sizes >= 0");
 
   // The tensor-core path needs a 16-bit dtype, head_dim 64 or 128, at most 16
   // query heads per KV head, and 16-byte aligned rows.
@@ -1142,10 +1150,10 @@ AUGUR_KV_EXPORT int augur_kv_paged_decode_attention(
     if (max_seq_len > kMaxSeq)
       return fail(AUGUR_KV_EINVAL, "paged_decode_attention: max_seq_len above %d", kMaxSeq);
     if (dtype == AUGUR_KV_BF16)
-      return head_dim == 64 ? launch_split_g<__nv_bfloat16, 64>(a, max_seq_len, workspace, workspace_bytes, st)
-                            : launch_split_g<__nv_bfloat16, 128>(a, max_seq_len, workspace, workspace_bytes, st);
-    return head_dim == 64 ? launch_split_g<__half, 64>(a, max_seq_len, workspace, workspace_bytes, st)
-                          : launch_split_g<__half, 128>(a, max_seq_len, workspace, workspace_bytes, st);
+      return head_dim == 64 ? launch_split_g<__nv_bfloat16, 64>(a, max_seq_len, counters, counters_bytes, scratch, scratch_bytes, st)
+                            : launch_split_g<__nv_bfloat16, 128>(a, max_seq_len, counters, counters_bytes, scratch, scratch_bytes, st);
+    return head_dim == 64 ? launch_split_g<__half, 64>(a, max_seq_len, counters, counters_bytes, scratch, scratch_bytes, st)
+                          : launch_split_g<__half, 128>(a, max_seq_len, counters, counters_bytes, scratch, scratch_bytes, st);
   }
 
   // generic path: the whole sequence's scores live in shared memory

@@ -204,14 +204,16 @@ int augur_kv_copy_runs(const void* src_k, const void* src_v,
  * flags: AUGUR_KV_ATTN_AUTO picks the tensor-core kernel for bf16/fp16,
  * head_dim 64 or 128, <= 16 query heads per KV head; AUGUR_KV_ATTN_GENERIC
  * forces the CUDA-core kernel (any dtype; max_seq_len <= ~51,000).
- * workspace: device memory, 16-byte aligned, whose first bytes (the arrival
- * counters) are zero before the first launch that uses it; every launch
- * leaves them zero again. Size it with
- * augur_kv_paged_decode_attention_workspace; with a smaller one (or NULL,
- * 0) each sequence is processed by one CTA, unsplit. Launches that may run
- * concurrently need separate workspaces. max_seq_len is at most 2^30.
+ * counters / scratch: device memory for the split kernel, sized by
+ * augur_kv_paged_decode_attention_workspace. counters (int32, 4-byte
+ * aligned) must be zero before its first launch; every launch leaves it zero
+ * and never stores data in it, so one counters buffer may serve launches of
+ * any size one after another. scratch (16-byte aligned) needs no initial
+ * contents. Launches that may run concurrently need their own counters and
+ * scratch. With counters but too small a scratch (or none) every sequence is
+ * processed unsplit; without counters, work items are also assigned statically.
  * A seq_lens entry above max_seq_len records AUGUR_KV_EBOUNDS and only its
- * first max_seq_len positions are attended.
+ * first max_seq_len positions are attended. max_seq_len is at most 2^30.
  */
 #define AUGUR_KV_ATTN_AUTO 0
 #define AUGUR_KV_ATTN_GENERIC 1
@@ -224,18 +226,18 @@ int augur_kv_paged_decode_attention(const void* q, const int64_t* q_strides, /* 
                                     const int32_t* seq_lens, int32_t max_seq_len, int32_t batch,
                                     int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim, int32_t dtype,
                                     void* out, const int64_t* out_strides, /* [2] */
-                                    int32_t flags, void* workspace, int64_t workspace_bytes,
-                                    int32_t* status, void* stream);
+                                    int32_t flags, int32_t* counters, int64_t counters_bytes,
+                                    void* scratch, int64_t scratch_bytes, int32_t* status, void* stream);
 
 /*
- * augur_kv_paged_decode_attention_workspace — bytes of workspace
- * augur_kv_paged_decode_attention uses for these sizes on the current device
- * (0: none), or -1 for invalid sizes. No reference counterpart (the
- * reference's eager attention allocates its temporaries per call).
+ * augur_kv_paged_decode_attention_workspace — bytes of counters and scratch
+ * that augur_kv_paged_decode_attention uses for these sizes on the current
+ * device (0 and 0: none). No reference counterpart (the reference's eager
+ * attention allocates its temporaries per call).
  */
-int64_t augur_kv_paged_decode_attention_workspace(int32_t batch, int32_t n_q_heads, int32_t n_kv_heads,
-                                                  int32_t head_dim, int32_t max_seq_len, int32_t dtype,
-                                                  int32_t flags);
+int augur_kv_paged_decode_attention_workspace(int32_t batch, int32_t n_q_heads, int32_t n_kv_heads,
+                                              int32_t head_dim, int32_t max_seq_len, int32_t dtype,
+                                              int32_t flags, int64_t* counters_bytes, int64_t* scratch_bytes);
 
 /*
  * Peer memory for the disaggregated mode: a decode GPU's process exports its

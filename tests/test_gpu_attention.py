@@ -129,8 +129,8 @@ def test_bad_block_id_is_reported(cuda):
 
 
 
-def _raw_call(cuda, q, pool, dt, out, workspace, ws_bytes, max_seq=None):
-    """The C-ABI entry point with an explicit workspace."""
+def _raw_call(cuda, q, pool, dt, out, counters, scratch, max_seq=None):
+    """The C-ABI entry point with explicit counters and scratch (tensors or None)."""
     lib = _lib.load()
     kc, vc = pool.keys[0], pool.values[0]
     B, Hq, D = q.shape
@@ -140,7 +140,9 @@ def _raw_call(cuda, q, pool, dt, out, workspace, ws_bytes, max_seq=None):
         dt.blocks.data_ptr(), dt.blocks.stride(0), dt.blocks.shape[1], dt.lens.data_ptr(),
         dt.max_seq_len if max_seq is None else max_seq, B, Hq, kc.shape[1], D, _ops.dtype_code(q),
         out.data_ptr(), _lib.i64_array((out.stride(0), out.stride(1))), _lib.ATTN_AUTO,
-        workspace, ws_bytes, _ops.status_word(cuda).data_ptr(), torch.cuda.current_stream(cuda).cuda_stream)
+        None if counters is None else counters.data_ptr(), 0 if counters is None else counters.numel() * 4,
+        None if scratch is None else scratch.data_ptr(), 0 if scratch is None else scratch.numel(),
+        _ops.status_word(cuda).data_ptr(), torch.cuda.current_stream(cuda).cuda_stream)
     _lib.check(code, "augur_kv_paged_decode_attention")
 
 
@@ -161,41 +163,100 @@ def _long_batch(cuda, seed, lens, bs=16):
 
 
 def test_workspace_sizes_and_counters(cuda, oracle):
-    """No workspace and a too-small one (each sequence unsplit) and the full size (split into
-    chunks) give the oracle's result within tolerance; every launch leaves the counters zero."""
+    """No counters (static items, unsplit), counters without scratch (dynamic items, unsplit)
+    and the full workspace (split into chunks) give the oracle's result within tolerance;
+    every launch leaves the counters zero."""
+    from augur_b200.attention import workspace_bytes
+
     lens = [4000, 17, 2500, 129]
     kp, vp, tables, q, pool = _long_batch(cuda, 21, lens)
     dt = DecodeTables(tables, cuda)
     qd = q.to(cuda)
     lib = _lib.load()
-    full = lib.augur_kv_paged_decode_attention_workspace(len(lens), 14, 2, 64, max(lens), _lib.BF16, _lib.ATTN_AUTO)
-    assert full > 0
+    need_c, need_s = workspace_bytes(lib, (len(lens), 14, 2, 64, max(lens), _lib.BF16, _lib.ATTN_AUTO))
+    assert need_c > 256 and need_s > 0
     want = []
     for b, (t, n) in enumerate(zip(tables, lens)):
         k, v = oracle.read_paged_kv(kp, vp, 0, oracle.RefBlockTable(t.block_ids, 16, n))
         want.append(oracle.decode_attention(q[b : b + 1].unsqueeze(2), k, v)[0, :, 0, :])
-    for nbytes in (0, full // 3, full):
-        ws = torch.zeros(max(nbytes, 16), dtype=torch.uint8, device=cuda)
+    for c_bytes, s_bytes in ((0, 0), (256, 0), (need_c, need_s // 2), (need_c, need_s)):
+        cnt = torch.zeros(max(1, c_bytes // 4), dtype=torch.int32, device=cuda) if c_bytes else None
+        scr = torch.empty(s_bytes, dtype=torch.uint8, device=cuda) if s_bytes else None
         out = torch.full_like(qd, float("nan"))
         for _ in range(2):  # the second launch relies on the first having reset the counters
-            _raw_call(cuda, qd, pool, dt, out, ws.data_ptr() if nbytes else None, nbytes)
+            _raw_call(cuda, qd, pool, dt, out, cnt, scr)
         torch.cuda.synchronize(cuda)
         assert _ops.read_status(cuda) == _lib.OK
-        assert int(ws[:512].count_nonzero()) == 0, "scheduler / arrival counters not reset"
+        if cnt is not None:
+            assert int(cnt.count_nonzero()) == 0, "counters not left zero"
         for b in range(len(lens)):
-            _close(out[b], want[b], torch.bfloat16, f"workspace {nbytes} seq {b}")
+            _close(out[b], want[b], torch.bfloat16, f"counters {c_bytes} scratch {s_bytes} seq {b}")
+
+
+def test_counters_shared_across_sizes(cuda, oracle):
+    """One counters buffer and one scratch buffer serve launches of different sizes in turn
+    (head_dim 128 then 64, few then many sequences): counters never hold data."""
+    from augur_b200.attention import workspace_bytes
+
+    lib = _lib.load()
+    cnt = torch.zeros(1 << 16, dtype=torch.int32, device=cuda)
+    scr = torch.empty(64 << 20, dtype=torch.uint8, device=cuda)
+    g = torch.Generator().manual_seed(44)
+    for Hq, Hkv, D, nseq in ((16, 2, 128, 3), (14, 2, 64, 300), (8, 1, 64, 40)):
+        lens = [int(x) for x in np.random.default_rng(nseq).integers(1, 900, size=nseq)]
+        nblk = [-(-n // 16) for n in lens]
+        NB = sum(nblk) + 1
+        kp = torch.randn(1, NB, Hkv, 16, D, generator=g).to(torch.bfloat16)
+        vp = torch.randn(1, NB, Hkv, 16, D, generator=g).to(torch.bfloat16)
+        tabs, cur = [], 0
+        for n, nb in zip(lens, nblk):
+            tabs.append(ab.SequenceBlockTable(block_ids=list(range(cur, cur + nb)), block_size=16, seq_len=n))
+            cur += nb
+        pool = ab.PagedKVCache(keys=kp.to(cuda), values=vp.to(cuda), block_size=16, allocator=ab.BlockAllocator(NB))
+        q = torch.randn(nseq, Hq, D, generator=g).to(torch.bfloat16)
+        need_c, need_s = workspace_bytes(lib, (nseq, Hq, Hkv, D, max(lens), _lib.BF16, _lib.ATTN_AUTO))
+        assert need_c <= cnt.numel() * 4 and need_s <= scr.numel()
+        out = torch.empty(nseq, Hq, D, dtype=torch.bfloat16, device=cuda)
+        _raw_call(cuda, q.to(cuda), pool, DecodeTables(tabs, cuda), out, cnt, scr)
+        torch.cuda.synchronize(cuda)
+        assert int(cnt.count_nonzero()) == 0
+        for b in range(0, nseq, max(1, nseq // 20)):
+            k, v = oracle.read_paged_kv(kp, vp, 0, oracle.RefBlockTable(tabs[b].block_ids, 16, lens[b]))
+            want = oracle.decode_attention(q[b : b + 1].unsqueeze(2), k, v)[0, :, 0, :]
+            _close(out[b], want, torch.bfloat16, f"D {D} seq {b}")
 
 
 def test_seq_len_above_max_is_reported(cuda):
+    from augur_b200.attention import workspace_bytes
+
     lens = [300, 40]
     kp, vp, tables, q, pool = _long_batch(cuda, 22, lens)
     dt = DecodeTables(tables, cuda)
     out = torch.empty_like(q.to(cuda))
     lib = _lib.load()
-    nbytes = lib.augur_kv_paged_decode_attention_workspace(2, 14, 2, 64, 200, _lib.BF16, _lib.ATTN_AUTO)
-    ws = torch.zeros(max(nbytes, 16), dtype=torch.uint8, device=cuda)
-    _raw_call(cuda, q.to(cuda), pool, dt, out, ws.data_ptr(), nbytes, max_seq=200)
+    need_c, need_s = workspace_bytes(lib, (2, 14, 2, 64, 200, _lib.BF16, _lib.ATTN_AUTO))
+    cnt = torch.zeros(need_c // 4, dtype=torch.int32, device=cuda)
+    scr = torch.empty(max(16, need_s), dtype=torch.uint8, device=cuda)
+    _raw_call(cuda, q.to(cuda), pool, dt, out, cnt, scr, max_seq=200)
     torch.cuda.synchronize(cuda)
     assert _ops.read_status(cuda) == _lib.EBOUNDS
     assert torch.isfinite(out.float()).all()
-    assert int(ws[:256].count_nonzero()) == 0
+    assert int(cnt.count_nonzero()) == 0
+
+
+def test_large_batch_scheduling_paths(cuda, oracle):
+    """300 sequences: beyond the register-held lengths (256) and item counts (128), so the
+    plan re-reads lengths and the item search walks seq_lens; several chunk sizes and
+    dynamic item scheduling are exercised against the oracle."""
+    rng = np.random.default_rng(30)
+    lens = [int(x) for x in rng.integers(0, 700, size=300)]
+    lens[7] = 4000  # one long sequence split over many chunks
+    _case(cuda, oracle, torch.bfloat16, len(lens), 14, 2, 64, 16, lens, 30, False)
+
+
+def test_back_to_back_launches_share_the_workspace(cuda, oracle):
+    """Three launches on one stream reuse the cached workspace: the scheduler and arrival
+    counters each launch leaves at zero must serve the next."""
+    for seed in (41, 42, 43):
+        lens = [int(x) for x in np.random.default_rng(seed).integers(100, 3000, size=20)]
+        _case(cuda, oracle, torch.float16, len(lens), 14, 2, 64, 16, lens, seed, False)
