@@ -105,10 +105,14 @@ def keep_until_done(stream: torch.cuda.Stream, *tensors: Tensor | None) -> None:
     Torch's caching allocator orders reuse on the stream a tensor was
     allocated on; for launches on another stream the tensor is recorded there.
     """
+    current = None
     for t in tensors:
         if t is not None and t.device.type == "cuda":
-            if stream != torch.cuda.current_stream(t.device):
-                t.record_stream(stream)
+            if current is None:
+                current = torch.cuda.current_stream(t.device)
+                if stream == current:
+                    return  # the launch is on the stream the tensors' reuse is ordered on
+            t.record_stream(stream)
 
 
 def scatter(

@@ -31,12 +31,20 @@ from .paged_kv_cache import PagedKVCache, SequenceBlockTable
 _workspaces: dict[tuple[int, int], tuple[Tensor, Tensor]] = {}
 
 
+_workspace_sizes: dict[tuple, tuple[int, int]] = {}
+
+
 def workspace_bytes(lib, sizes: tuple) -> tuple[int, int]:
-    """(counters, scratch) bytes augur_kv_paged_decode_attention needs for these sizes."""
-    cnt, scr = ctypes.c_int64(0), ctypes.c_int64(0)
-    _lib.check(lib.augur_kv_paged_decode_attention_workspace(*sizes, ctypes.byref(cnt), ctypes.byref(scr)),
-               "augur_kv_paged_decode_attention_workspace")
-    return cnt.value, scr.value
+    """(counters, scratch) bytes augur_kv_paged_decode_attention needs for these sizes on the
+    current device (cached per device and sizes)."""
+    key = (torch.cuda.current_device(),) + tuple(sizes)
+    got = _workspace_sizes.get(key)
+    if got is None:
+        cnt, scr = ctypes.c_int64(0), ctypes.c_int64(0)
+        _lib.check(lib.augur_kv_paged_decode_attention_workspace(*sizes, ctypes.byref(cnt), ctypes.byref(scr)),
+                   "augur_kv_paged_decode_attention_workspace")
+        got = _workspace_sizes[key] = (cnt.value, scr.value)
+    return got
 
 
 def _workspace(lib, device: torch.device, st: torch.cuda.Stream, sizes: tuple) -> tuple[Tensor | None, Tensor | None]:
@@ -46,14 +54,16 @@ def _workspace(lib, device: torch.device, st: torch.cuda.Stream, sizes: tuple) -
         return None, None
     key = (device.index, st.cuda_stream)
     cnt, scr = _workspaces.get(key, (None, None))
-    capturing = torch.cuda.is_current_stream_capturing()
-    with torch.cuda.stream(st):
-        if cnt is None or cnt.numel() * 4 < need_c:
-            cnt = torch.zeros(max(1, -(-need_c // 4)), dtype=torch.int32, device=device)
-        if need_s and (scr is None or scr.numel() < need_s):
-            scr = torch.empty(need_s, dtype=torch.uint8, device=device)
-    if not capturing:  # memory allocated during a graph capture belongs to that graph
-        _workspaces[key] = (cnt, scr)
+    grow_c = cnt is None or cnt.numel() * 4 < need_c
+    grow_s = need_s > 0 and (scr is None or scr.numel() < need_s)
+    if grow_c or grow_s:
+        with torch.cuda.stream(st):
+            if grow_c:
+                cnt = torch.zeros(max(1, -(-need_c // 4)), dtype=torch.int32, device=device)
+            if grow_s:
+                scr = torch.empty(need_s, dtype=torch.uint8, device=device)
+        if not torch.cuda.is_current_stream_capturing():  # a graph owns what its capture allocates
+            _workspaces[key] = (cnt, scr)
     return cnt, scr
 
 

@@ -505,6 +505,64 @@ def bench_rope(device, pool, reps: int = 7) -> dict:
             "timed": "CUDA graph of 24 per-layer launches; q, k, v of all layers (450 MB) exceed L2"}
 
 
+def bench_decode_step(device, pool, tables) -> dict:
+    """The KV side of one decode step for the config-3 batch (32 sequences) across 24 layers:
+    per layer the fused RoPE append and the decode attention (paged_decode_layer), on copies
+    of the block tables. Device time from a CUDA graph of the 48 launches (L2 flushed
+    before each replay); the step including its host work (DecodeStep: table growth, slot
+    mapping, uploads) timed eagerly.
+    """
+    import augur_b200 as ab
+    from augur_b200.decode import DecodeStep, paged_decode_layer
+
+    Hq, theta = 14, 1000000.0
+    tabs = [ab.SequenceBlockTable(block_ids=list(t.block_ids), block_size=t.block_size, seq_len=t.seq_len)
+            for t in tables]
+    B = len(tabs)
+    g = torch.Generator(device=device).manual_seed(17)
+    q = torch.randn(L, B, Hq, 1, D, generator=g, device=device).to(torch.bfloat16)
+    k = torch.randn(L, B, H, 1, D, generator=g, device=device).to(torch.bfloat16)
+    v = torch.randn(L, B, H, 1, D, generator=g, device=device).to(torch.bfloat16)
+    step = DecodeStep(pool, tabs)
+
+    def layers(st) -> None:
+        for layer in range(L):
+            paged_decode_layer(st, pool, layer, q[layer], k[layer], v[layer], theta)
+
+    graph = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream(device)
+    cs.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(cs):
+        layers(step)
+    torch.cuda.synchronize(device)
+    with torch.cuda.graph(graph, stream=cs):
+        layers(step)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    times = []
+    for _ in range(7):
+        flush.fill_(1)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        graph.replay()
+        b.record()
+        torch.cuda.synchronize(device)
+        times.append(a.elapsed_time(b))
+    graph.reset()
+    dev_ms = statistics.median(times[2:])
+    host = []
+    for _ in range(5):  # real steps: every table grows by one token per step
+        torch.cuda.synchronize(device)
+        t0 = time.perf_counter()
+        layers(DecodeStep(pool, tabs))
+        torch.cuda.synchronize(device)
+        host.append(time.perf_counter() - t0)
+    tokens = int(sum(t.seq_len for t in tabs))
+    return {"seqs": B, "cached_tokens_after": tokens, "launches_per_step": 2 * L,
+            "us_per_step_device": round(dev_ms * 1e3, 1), "us_per_layer_device": round(dev_ms * 1e3 / L, 2),
+            "us_per_step_with_host": round(statistics.median(host) * 1e6, 1),
+            "timed": "per layer: fused RoPE append + decode attention; device: CUDA graph, L2 flushed"}
+
+
 def bench_decode_attention_large(device, n_seqs: int = 256) -> dict:
     """Decode attention at a serving-sized batch: the first n_seqs config-5 (box) lengths
     (lognormal, median 1024, 64..8192 tokens), random blocks of a pool sized to them, random
@@ -670,6 +728,7 @@ def run_extras(device, handoff_only: bool = False, attention_only: bool = False,
     if not (rope_only or offload_only):
         out["decode_attention"] = bench_decode_attention(device, pool, tables)
         out["decode_attention_256_seqs"] = bench_decode_attention_large(device)
+        out["decode_step"] = bench_decode_step(device, pool, tables)
     if attention_only:
         return out
     if not rope_only:

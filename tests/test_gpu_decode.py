@@ -1,0 +1,73 @@
+"""Batched paged decode layer vs the reference's per-sequence paged branch.
+
+For each sequence the oracle runs what augur/attention.py:53-86 runs with a
+paged cache for its new token: apply_rope, write_paged_kv, read_paged_kv, the
+GQA repeat and the attention. The pool must match bit for bit; the attention
+output within the bf16 tolerance of the decode-attention tests.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import augur_b200 as ab
+from augur_b200 import _lib, _ops, batched
+from augur_b200.decode import DecodeStep, paged_decode_layer
+from tests.conftest import assert_bits_equal, poison_
+
+pytestmark = pytest.mark.gpu
+
+THETA = 1000000.0
+
+
+def test_decode_layers_match_the_reference_branch(cuda, oracle):
+    L, H, Hq, D, bs, NB = 2, 2, 14, 64, 16, 64
+    prior = [0, 1, 15, 16, 300]
+    g = torch.Generator().manual_seed(12)
+    pool = ab.PagedKVCache(keys=poison_(torch.empty(L, NB, H, bs, D, dtype=torch.bfloat16, device=cuda)),
+                           values=poison_(torch.empty(L, NB, H, bs, D, dtype=torch.bfloat16, device=cuda)),
+                           block_size=bs, allocator=ab.BlockAllocator(NB))
+    rk = poison_(torch.empty(L, NB, H, bs, D, dtype=torch.bfloat16))
+    rv = poison_(torch.empty(L, NB, H, bs, D, dtype=torch.bfloat16))
+    # the prompts, written through the batched scatter on the device and by the oracle
+    tables = [ab.SequenceBlockTable.empty(bs) for _ in prior]
+    sm = batched.prefill_slot_mapping(tables, prior, pool.allocator)
+    T = sum(prior)
+    pk = torch.randn(L, T, H, D, generator=g).to(torch.bfloat16)
+    pv = torch.randn(L, T, H, D, generator=g).to(torch.bfloat16)
+    flat = np.concatenate([sm[b, :n] for b, n in enumerate(prior)])
+    batched.write_paged_kv_batch(pool, pk.to(cuda), pv.to(cuda), torch.from_numpy(flat).to(cuda))
+    oracle.scatter_slots(pk, pv, flat, rk, rv, bs)
+    ref_tables = [oracle.RefBlockTable(list(t.block_ids), bs, t.seq_len) for t in tables]
+    ref_alloc = oracle.RefBlockAllocator(NB)
+    for _ in range(NB - len(pool.allocator._free_blocks)):
+        ref_alloc.allocate()  # the same blocks are taken on both sides
+
+    step = DecodeStep(pool, tables)
+    for layer in range(L):
+        q = torch.randn(len(prior), Hq, 1, D, generator=g).to(torch.bfloat16)
+        k = torch.randn(len(prior), H, 1, D, generator=g).to(torch.bfloat16)
+        v = torch.randn(len(prior), H, 1, D, generator=g).to(torch.bfloat16)
+        out = paged_decode_layer(step, pool, layer, q.to(cuda), k.to(cuda), v.to(cuda), THETA)
+        assert out.shape == (len(prior), Hq, 1, D)
+        for b, n in enumerate(prior):
+            pos = torch.tensor([[n]])
+            qe, ke = oracle.apply_rope(q[b : b + 1], k[b : b + 1], pos, THETA)
+            rt = ref_tables[b]
+            if layer == 0:
+                oracle.write_paged_kv(rk, rv, ref_alloc, layer, rt, [n], ke, v[b : b + 1])
+            else:
+                blk, off = rt.block_ids[n // bs], n % bs
+                rk[layer, blk, :, off] = ke[0, :, 0]
+                rv[layer, blk, :, off] = v[b, :, 0]
+            kk, vv = oracle.read_paged_kv(rk, rv, layer, oracle.RefBlockTable(rt.block_ids, bs, n + 1))
+            want = oracle.decode_attention(qe, kk, vv)[0, :, 0, :]
+            torch.testing.assert_close(out[b, :, 0].float().cpu(), want.float(), rtol=1e-2, atol=1e-2,
+                                       msg=f"layer {layer} seq {b}")
+    assert [t.block_ids for t in tables] == [rt.block_ids for rt in ref_tables]
+    assert [t.seq_len for t in tables] == [n + 1 for n in prior]
+    assert_bits_equal(pool.keys, rk, "pool keys")
+    assert_bits_equal(pool.values, rv, "pool values")
+    assert _ops.read_status(cuda) == _lib.OK
