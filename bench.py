@@ -103,7 +103,16 @@ def scatter_bytes(n_tokens: int, layers: int = L) -> int:
 
 
 class ClockSampler:
-    """Poll SM clock and throttle reasons through NVML while the timed region runs."""
+    """SM clock and throttle reasons sampled around the timed region.
+
+    An `nvidia-smi -lms` child process samples every 20 ms with timestamps,
+    outside this interpreter, so a busy launch loop holding the GIL cannot
+    starve it. Only samples inside the window between mark_start() and
+    mark_end() count; for a region shorter than the sampling period, the ones
+    nearest to it count. Start the sampler before warm-up so the child is
+    running when the timed region begins. Without nvidia-smi, a thread polls
+    NVML instead.
+    """
 
     REASONS = {
         "sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
@@ -111,54 +120,112 @@ class ClockSampler:
     }
 
     def __init__(self, device_index: int, period_s: float = 0.002) -> None:
-        self.samples: list[int] = []
-        self.reasons: set[str] = set()
+        self.samples: list[tuple[float, int, int]] = []  # (time, SM MHz, reason mask)
         self.max_mhz = None
         self._stop = threading.Event()
         self._period = period_s
+        self._proc = None
+        self._nv = None
+        self._window = None
+        self._t0 = None
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        self._idx = int(vis.split(",")[device_index]) if vis else device_index
         try:
             import pynvml
 
             pynvml.nvmlInit()
-            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-            idx = int(vis.split(",")[device_index]) if vis else device_index
-            self._h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(self._idx)
             self._nv = pynvml
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
-        except Exception:  # NVML missing: report no clocks rather than fail the bench
-            self._nv = None
+        except Exception:  # NVML missing: nvidia-smi alone, or no clocks
+            pass
         self._t = threading.Thread(target=self._run, daemon=True)
 
     def _sample(self) -> None:
         nv = self._nv
-        self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
-        mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
-        for name, bit in self.REASONS.items():
-            if mask & bit:
-                self.reasons.add(name)
+        self.samples.append((time.time(), nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM),
+                             nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)))
 
     def _run(self) -> None:
         while not self._stop.is_set():
             self._sample()
             time.sleep(self._period)
 
-    def __enter__(self):
-        if self._nv is not None:
+    def start(self) -> "ClockSampler":
+        import shutil
+        import subprocess
+
+        smi = shutil.which("nvidia-smi")
+        if smi is not None:
+            self._proc = subprocess.Popen(
+                [smi, "-i", str(self._idx),
+                 "--query-gpu=timestamp,clocks.sm,clocks.max.sm,clocks_event_reasons.active",
+                 "--format=csv,noheader,nounits", "-lms", "20"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            import atexit
+
+            atexit.register(self._reap)  # an error before stop() must not leave the child running
+        elif self._nv is not None:
             self._t.start()
         return self
 
-    def __exit__(self, *exc) -> None:
-        if self._nv is not None:
+    def _reap(self) -> None:
+        if self._proc is not None and self._proc.poll() is None:
+            self._proc.terminate()
+
+    def mark_start(self) -> None:
+        self._t0 = time.time()
+
+    def mark_end(self) -> None:
+        self._window = (self._t0 if self._t0 is not None else time.time(), time.time())
+
+    def stop(self) -> None:
+        import datetime
+
+        if self._proc is not None:
+            self._proc.terminate()  # the child this sampler started, by its own handle
+            out, _ = self._proc.communicate(timeout=30)
+            for line in out.splitlines():
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) != 4:
+                    continue
+                try:
+                    ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                    self.samples.append((ts, int(parts[1]), int(parts[3], 16)))
+                    self.max_mhz = self.max_mhz or int(parts[2])
+                except ValueError:
+                    continue
+        elif self._nv is not None:
             self._stop.set()
             self._t.join()
-            if not self.samples:
-                self._sample()
+        if not self.samples and self._nv is not None:
+            self._sample()
+
+    def __enter__(self):
+        self.start()
+        self.mark_start()
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.mark_end()
+        self.stop()
+
+    def _in_window(self) -> list[tuple[float, int, int]]:
+        if self._window is None or not self.samples:
+            return self.samples
+        t0, t1 = self._window
+        inside = [x for x in self.samples if t0 - 0.005 <= x[0] <= t1 + 0.005]
+        if inside:
+            return inside
+        return sorted(self.samples, key=lambda x: min(abs(x[0] - t0), abs(x[0] - t1)))[:3]
 
     def summary(self) -> dict:
-        if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml unavailable"]}
-        return {"sm_mhz": int(statistics.median(self.samples)), "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+        sel = self._in_window()
+        if not sel:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["clock sampling unavailable"]}
+        reasons = sorted({name for _, _, m in sel for name, bit in self.REASONS.items() if m & bit})
+        return {"sm_mhz": int(statistics.median(x[1] for x in sel)), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(sel)}
 
 
 def load_peaks() -> tuple[float, str]:
@@ -275,6 +342,7 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
         for i in range(n_sets):
             step(i)
     launches_per_replay = _ops.launch_count - launches_before
+    clocks = ClockSampler(local).start()  # running before the timed region begins
     for _ in range(2):
         graph.replay()
     torch.cuda.synchronize(device)
@@ -292,14 +360,16 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
 
     barrier(world, device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        start.record()
-        for _ in range(replays):
-            graph.replay()
-        if rem_graph is not None:
-            rem_graph.replay()
-        end.record()
-        torch.cuda.synchronize(device)
+    clocks.mark_start()
+    start.record()
+    for _ in range(replays):
+        graph.replay()
+    if rem_graph is not None:
+        rem_graph.replay()
+    end.record()
+    torch.cuda.synchronize(device)
+    clocks.mark_end()
+    clocks.stop()
     ms = start.elapsed_time(end)
     barrier(world, device)
     ms_max = max_over_ranks(ms, world, device)
@@ -1023,7 +1093,9 @@ def main() -> None:
 
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default: 20000 for the scatter headline, 2000 for the reference arm, "
+                         "20 for box, 50 for disagg)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -1046,6 +1118,8 @@ def main() -> None:
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.steps is None:  # each default keeps its timed region well under a minute
+        args.steps = 2000 if args.impl == "reference" else {"scatter": 20000, "box": 20, "disagg": 50}[args.workload]
     if args.small:
         args.skip_cpu = args.skip_extras = True
     if args.handoff_only:  # profiling case: only the config-3 handoff (about 3 GB on the device)
