@@ -22,7 +22,9 @@ pytestmark = pytest.mark.gpu
 THETA = 1000000.0
 
 
-def test_decode_layers_match_the_reference_branch(cuda, oracle):
+@pytest.mark.parametrize("path", ["prepared", "general"])
+def test_decode_layers_match_the_reference_branch(cuda, oracle, path):
+    """path: the step's prepared launches, or the general wrappers (an explicit stream)."""
     L, H, Hq, D, bs, NB = 2, 2, 14, 64, 16, 64
     prior = [0, 1, 15, 16, 300]
     g = torch.Generator().manual_seed(12)
@@ -50,7 +52,8 @@ def test_decode_layers_match_the_reference_branch(cuda, oracle):
         q = torch.randn(len(prior), Hq, 1, D, generator=g).to(torch.bfloat16)
         k = torch.randn(len(prior), H, 1, D, generator=g).to(torch.bfloat16)
         v = torch.randn(len(prior), H, 1, D, generator=g).to(torch.bfloat16)
-        out = paged_decode_layer(step, pool, layer, q.to(cuda), k.to(cuda), v.to(cuda), THETA)
+        stream = torch.cuda.current_stream(cuda) if path == "general" else None
+        out = paged_decode_layer(step, pool, layer, q.to(cuda), k.to(cuda), v.to(cuda), THETA, stream=stream)
         assert out.shape == (len(prior), Hq, 1, D)
         for b, n in enumerate(prior):
             pos = torch.tensor([[n]])
