@@ -8,16 +8,17 @@
 // of the batch for one layer, reading each K/V row of the pool once:
 //
 //  * attn_decode_split_kernel (bf16 / fp16, head_dim 64 or 128, <= 16 query
-//    heads per KV head): sequences are cut into chunks of equal size (a
-//    multiple of warps x 32 tokens) that each CTA derives on the device from
-//    seq_lens so the work items, (sequence, KV head, chunk) triples numbered
-//    in order, fill the grid of resident CTAs once; one item per CTA. Each
-//    warp stages 32 tokens of K and V in shared memory with cp.async and
-//    runs both products transposed on mma.sync m16n8k16 (tokens, not the
-//    few query heads of a group, fill the 16 rows) around an online softmax.
-//    Chunks of one sequence combine through caller-provided counters and scratch: the
-//    last CTA to arrive (an atomic counter; no CTA ever waits) merges the
-//    partials and writes the output.
+//    heads per KV head): a persistent grid of the resident CTAs. Sequences
+//    are cut into chunks of equal size (a power-of-two multiple of warps x 32
+//    tokens) that each CTA derives on the device from seq_lens so the work
+//    items, (sequence, KV head, chunk) triples numbered in order, number at
+//    most four waves of the grid; CTA i takes item i, then items from an
+//    atomic counter. Each warp stages 32 tokens of K and V in shared memory
+//    with cp.async and runs both products transposed on mma.sync m16n8k16
+//    (tokens, not the few query heads of a group, fill the 16 rows) around
+//    an online softmax. Chunks of one sequence combine through
+//    caller-provided counters and scratch: the last CTA to arrive (an atomic
+//    counter; no CTA ever waits) merges the partials and writes the output.
 //  * attn_decode_generic_kernel (any dtype / shape): one CTA per (sequence,
 //    query head), scores of the whole sequence in shared memory, then the
 //    reference's order of operations: max, exp, sum, normalise, P.V.
@@ -383,8 +384,9 @@ __device__ Item locate(const AttnArgs& a, const Plan& p, int item, int lane, con
   }
 }
 
-// One work item per CTA: a chunk of C tokens of one (sequence, KV head).
-// Each warp takes every kWarps-th 32-token stage of the chunk and stages its
+// Each work item is a chunk of C tokens of one (sequence, KV head), and a CTA
+// processes its items one after another. Each warp takes every kWarps-th
+// 32-token stage of the chunk (NS stage buffers per warp) and stages its
 // K and V rows in shared memory with cp.async (one block-table entry per lane
 // per stage, shared by shuffle). Both products run transposed on mma.sync
 // m16n8k16 so the stage's tokens, not the few query heads of the group, fill
