@@ -79,9 +79,50 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _P, _I64P, _I64P, _I64, _I32, _P, _P, _I64P, _I64, _I64, _P, _I64P, _I64, _P, _I64P, _P, _P, _I64,
          _P, _I64P, _P, _I64P, _I32, _I64, _I32, _I32, _I32, _P, _P],
     ),
+    "augur_kv_decode_layer": (ctypes.c_int, [_P, _I32, _P, _P, _P, _P, _P]),
     "augur_kv_signal": (ctypes.c_int, [_P, _I32, _P]),
     "augur_kv_wait": (ctypes.c_int, [_P, _I32, _I64, _P, _P]),
 }
+
+
+
+class DecodeArgs(ctypes.Structure):
+    """augur_kv_decode_args: what every layer of a decode step shares (field for field)."""
+
+    _fields_ = [
+        ("k_pool", ctypes.c_void_p),
+        ("v_pool", ctypes.c_void_p),
+        ("pool_strides", ctypes.c_int64 * 4),
+        ("num_blocks", ctypes.c_int64),
+        ("block_size", ctypes.c_int32),
+        ("n_layers", ctypes.c_int32),
+        ("n_q_heads", ctypes.c_int32),
+        ("n_kv_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("batch", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
+        ("slots", ctypes.c_void_p),
+        ("positions", ctypes.c_void_p),
+        ("rope_cos", ctypes.c_void_p),
+        ("rope_sin", ctypes.c_void_p),
+        ("rope_positions", ctypes.c_int64),
+        ("q_strides", ctypes.c_int64 * 2),
+        ("kv_strides", ctypes.c_int64 * 2),
+        ("q_rot", ctypes.c_void_p),
+        ("block_tables", ctypes.c_void_p),
+        ("tables_stride", ctypes.c_int64),
+        ("max_blocks", ctypes.c_int64),
+        ("seq_lens", ctypes.c_void_p),
+        ("max_seq_len", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+        ("counters", ctypes.c_void_p),
+        ("counters_bytes", ctypes.c_int64),
+        ("scratch", ctypes.c_void_p),
+        ("scratch_bytes", ctypes.c_int64),
+        ("status", ctypes.c_void_p),
+    ]
+
 
 NOALLOC_MAX_RUNS = 65536
 INLINE_INDEX_MAX = 32

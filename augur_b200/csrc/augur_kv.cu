@@ -36,7 +36,7 @@
 #include "augur_kv.h"
 #include "common.cuh"
 
-#define AUGUR_KV_VERSION ((0 << 16) | 5)
+#define AUGUR_KV_VERSION ((0 << 16) | 6)
 
 namespace augur_kv_dev {
 

@@ -15,12 +15,14 @@ The host work of a step (growing each table by one position, the slot
 mapping, the device tables) is done once per step in DecodeStep and shared
 by all layers. So is everything the two launches need apart from the layer's
 own tensors: the checks, the RoPE table, the attention counters and scratch,
-and the argument arrays. A layer is then two foreign calls. The projections
-and everything after the attention core stay the model's.
+gathered in one argument block (augur_kv_decode_args). A layer is then one
+foreign call, augur_kv_decode_layer, which issues both launches. The
+projections and everything after the attention core stay the model's.
 """
 
 from __future__ import annotations
 
+import ctypes
 from collections.abc import Sequence
 
 import numpy as np
@@ -28,7 +30,7 @@ import torch
 from torch import Tensor
 
 from . import _lib, _ops
-from .attention import DecodeTables, _workspace, paged_decode_attention
+from .attention import DecodeTables, _workspace, paged_decode_attention, workspace_bytes
 from .batched import decode_slot_mapping
 from .paged_kv_cache import PagedKVCache, SequenceBlockTable
 from .rope import rope_tables, write_paged_kv_batch_rope
@@ -50,9 +52,9 @@ class DecodeStep:
         self.tables = DecodeTables(tables, device)
         self._fast: tuple | None = None  # launch arguments shared by the layers, built on first use
 
-    def _prepare(self, cache: PagedKVCache, q: Tensor, key: Tensor, rope_theta: float) -> tuple:
-        """Checks and launch arguments that every layer of this step shares, or None when the
-        inputs need the general path."""
+    def _prepare(self, cache: PagedKVCache, q: Tensor, key: Tensor, rope_theta: float) -> tuple | None:
+        """The argument block every layer of this step shares (augur_kv_decode_args), or None
+        when the inputs need the general path."""
         L, NB, Hkv, bs, D = cache.keys.shape
         B, Hq = q.shape[0], q.shape[1]
         dev, dt = cache.keys.device, cache.keys.dtype
@@ -62,57 +64,178 @@ class DecodeStep:
         if not ok:
             return None
         lib = _lib.load()
-        es = cache.keys.element_size()
         cos, sin = rope_tables(D, rope_theta, dt, self.max_position + 1, dev)
         st = torch.cuda.current_stream(dev)
         dcode = _ops.dtype_code(q)
         cnt, scr = _workspace(lib, dev, st, (B, Hq, Hkv, D, self.tables.max_seq_len, dcode, _lib.ATTN_AUTO))
         q_rot = torch.empty(B, Hq, D, dtype=dt, device=dev)  # reused by every layer, stream-ordered
+        status = _ops.status_word(dev)
         kc = cache.keys
-        pool_str = _lib.i64_array((kc.stride(1), kc.stride(2), kc.stride(3)))
-        dst_str = _lib.i64_array((0, kc.stride(1), kc.stride(3), kc.stride(2)))
-        return (lib, st, dcode, cos, sin, cnt, scr, q_rot, pool_str, dst_str, kc.stride(0) * es,
-                _ops.status_word(dev), (q.stride(), key.stride()), rope_theta)
+        a = _lib.DecodeArgs()
+        a.k_pool, a.v_pool = kc.data_ptr(), cache.values.data_ptr()
+        a.pool_strides[:] = kc.stride()[:4]  # layer, block, kv head, row
+        a.num_blocks, a.block_size, a.n_layers = NB, bs, L
+        a.n_q_heads, a.n_kv_heads, a.head_dim, a.dtype, a.batch, a.flags = Hq, Hkv, D, dcode, B, _lib.ATTN_AUTO
+        a.slots, a.positions = self.slots.data_ptr(), self.positions.data_ptr()
+        a.rope_cos, a.rope_sin, a.rope_positions = cos.data_ptr(), sin.data_ptr(), cos.shape[0]
+        a.q_strides[:] = q.stride()[:2]
+        a.kv_strides[:] = key.stride()[:2]
+        a.q_rot = q_rot.data_ptr()
+        blocks = self.tables.blocks
+        a.block_tables, a.tables_stride, a.max_blocks = blocks.data_ptr(), blocks.stride(0), blocks.shape[1]
+        a.seq_lens, a.max_seq_len = self.tables.lens.data_ptr(), self.tables.max_seq_len
+        a.counters, a.counters_bytes = (cnt.data_ptr(), cnt.numel() * 4) if cnt is not None else (None, 0)
+        a.scratch, a.scratch_bytes = (scr.data_ptr(), scr.numel()) if scr is not None else (None, 0)
+        a.status = status.data_ptr()
+        key_sig = (q.shape, q.stride(), key.shape, key.stride())
+        # the tensors the argument block points into stay referenced with it
+        return (lib, st, ctypes.addressof(a), key_sig, a, cos, sin, q_rot, cnt, scr, status, rope_theta)
 
     def layer(self, cache: PagedKVCache, layer_idx: int, q: Tensor, key: Tensor, value: Tensor,
               rope_theta: float) -> Tensor | None:
-        """The two launches of paged_decode_layer with the step's prepared arguments, on the
-        current stream; None when the inputs need the general path."""
-        if self._fast is None or self._fast[-1] != rope_theta:
-            self._fast = self._prepare(cache, q, key, rope_theta)
+        """paged_decode_layer's two launches as one augur_kv_decode_layer call with the step's
+        prepared arguments, on the current stream; None when the inputs need the general path."""
         f = self._fast
-        if (f is None or (q.stride(), key.stride()) != f[12] or value.shape != key.shape
-                or value.stride() != key.stride() or value.dtype != key.dtype):
+        if f is None or f[-1] != rope_theta:
+            f = self._fast = self._prepare(cache, q, key, rope_theta)
+            if f is None:
+                return None
+        if ((q.shape, q.stride(), key.shape, key.stride()) != f[3] or value.shape != key.shape
+                or value.stride() != key.stride() or value.dtype != key.dtype or q.dtype != key.dtype):
             return None
-        (lib, st, dcode, cos, sin, cnt, scr, q_rot, pool_str, dst_str, layer_bytes, status, _, _) = f
+        lib, st = f[0], f[1]
         dev = cache.keys.device
-        if (dev.index != torch.cuda.current_device() or st != torch.cuda.current_stream(dev)
-                or not 0 <= layer_idx < cache.keys.shape[0]):
+        if not 0 <= layer_idx < f[4].n_layers or _current_raw_stream(dev) != st.cuda_stream:
             return None
-        L, NB, Hkv, bs, D = cache.keys.shape
-        B, Hq = q.shape[0], q.shape[1]
-        koff, sh = layer_idx * layer_bytes, st.cuda_stream
-        k_layer, v_layer = cache.keys.data_ptr() + koff, cache.values.data_ptr() + koff
-        qs, ks = q.stride(), key.stride()
-        out = torch.empty(B, Hq, 1, D, dtype=q.dtype, device=q.device)
-        code = lib.augur_kv_rope_scatter(
-            key.data_ptr(), value.data_ptr(), _lib.i64_array((0, 0, ks[0], ks[1])),
-            _lib.i64_array((0, 0, ks[0], ks[1])), B, dcode, k_layer, v_layer, dst_str, bs, NB,
-            self.slots.data_ptr(), _lib.i64_array((0, 1)), 0, self.positions.data_ptr(), _lib.i64_array((0, 1)),
-            cos.data_ptr(), sin.data_ptr(), cos.shape[0], q.data_ptr(), _lib.i64_array((0, 0, qs[0], qs[1])),
-            q_rot.data_ptr(), _lib.i64_array((0, 0, Hq * D, D)), Hq, B, 1, Hkv, D, status.data_ptr(), sh)
-        _lib.check(code, "augur_kv_rope_scatter")
-        code = lib.augur_kv_paged_decode_attention(
-            q_rot.data_ptr(), _lib.i64_array((Hq * D, D)), k_layer, v_layer, pool_str, NB, bs,
-            self.tables.blocks.data_ptr(), self.tables.blocks.stride(0), self.tables.blocks.shape[1],
-            self.tables.lens.data_ptr(), self.tables.max_seq_len, B, Hq, Hkv, D, dcode,
-            out.data_ptr(), _lib.i64_array((Hq * D, D)), _lib.ATTN_AUTO,
-            cnt.data_ptr() if cnt is not None else None, cnt.numel() * 4 if cnt is not None else 0,
-            scr.data_ptr() if scr is not None else None, scr.numel() if scr is not None else 0,
-            status.data_ptr(), sh)
-        _lib.check(code, "augur_kv_paged_decode_attention")
+        out = torch.empty(q.shape, dtype=q.dtype, device=dev)
+        code = lib.augur_kv_decode_layer(f[2], layer_idx, q.data_ptr(), key.data_ptr(), value.data_ptr(),
+                                         out.data_ptr(), st.cuda_stream)
+        _lib.check(code, "augur_kv_decode_layer")
         _ops.launch_count += 2
         return out
+
+
+class DecodeGraphStep:
+    """A decode step whose device state lives in fixed buffers, for CUDA-graph replay.
+
+    DecodeStep uploads each step's slots, positions and block tables into new
+    tensors, which a captured graph cannot follow. Here they live in buffers
+    sized once for `batch` sequences of up to `max_blocks` blocks, and so does
+    everything else the launches read (the RoPE table for every position the
+    tables can hold, a private attention workspace, the rotated-q buffer): the
+    argument block never changes. update() grows each table by one position
+    and refreshes the buffers, one host-to-device copy each on the current
+    stream; layer() issues augur_kv_decode_layer. A graph captured over
+    layer() calls (the model's own ops between them) therefore replays
+    correctly after every later update(). Rows past len(tables) are padding:
+    slot -1 (nothing written), length 0 (a zero output).
+    """
+
+    def __init__(self, cache: PagedKVCache, batch: int, max_blocks: int, n_q_heads: int,
+                 rope_theta: float) -> None:
+        _ops.require_cuda("DecodeGraphStep", cache.keys, cache.values)
+        L, NB, Hkv, bs, D = cache.keys.shape
+        if batch <= 0 or max_blocks <= 0 or n_q_heads <= 0 or n_q_heads % Hkv != 0:
+            raise ValueError("batch and max_blocks must be positive, n_q_heads a multiple of the KV heads")
+        if cache.keys.stride() != cache.values.stride():
+            raise ValueError("keys and values must share one layout")
+        dev, dt = cache.keys.device, cache.keys.dtype
+        self.cache, self.batch, self.max_blocks, self.rope_theta = cache, batch, max_blocks, rope_theta
+        self.capacity = max_blocks * bs  # longest sequence the buffers describe
+        lib = _lib.load()
+        self._lib = lib
+        with _ops._DeviceGuard(dev):
+            self._h64 = torch.empty(2, batch, dtype=torch.int64).pin_memory()  # slots, positions
+            self._h32 = torch.empty(batch * (max_blocks + 1), dtype=torch.int32).pin_memory()  # lens, tables
+            self._d64 = torch.empty(2, batch, dtype=torch.int64, device=dev)
+            self._d32 = torch.empty(batch * (max_blocks + 1), dtype=torch.int32, device=dev)
+            self._cos, self._sin = rope_tables(D, rope_theta, dt, self.capacity, dev)
+            dcode = _ops.dtype_code(cache.keys)
+            need_c, need_s = workspace_bytes(lib, (batch, n_q_heads, Hkv, D, self.capacity, dcode, _lib.ATTN_AUTO))
+            self._cnt = torch.zeros(max(1, -(-need_c // 4)), dtype=torch.int32, device=dev)
+            self._scr = torch.empty(max(16, need_s), dtype=torch.uint8, device=dev)
+            self._q_rot = torch.empty(batch, n_q_heads, D, dtype=dt, device=dev)
+            self._status = _ops.status_word(dev)
+        self._copied: torch.cuda.Event | None = None
+        a = self._args = _lib.DecodeArgs()
+        kc = cache.keys
+        a.k_pool, a.v_pool = kc.data_ptr(), cache.values.data_ptr()
+        a.pool_strides[:] = kc.stride()[:4]
+        a.num_blocks, a.block_size, a.n_layers = NB, bs, L
+        a.n_q_heads, a.n_kv_heads, a.head_dim, a.dtype, a.batch, a.flags = n_q_heads, Hkv, D, dcode, batch, _lib.ATTN_AUTO
+        a.slots, a.positions = self._d64[0].data_ptr(), self._d64[1].data_ptr()
+        a.rope_cos, a.rope_sin, a.rope_positions = self._cos.data_ptr(), self._sin.data_ptr(), self._cos.shape[0]
+        a.q_strides[:] = (n_q_heads * D, D)  # dense [batch, n_q_heads, 1, head_dim]
+        a.kv_strides[:] = (Hkv * D, D)
+        a.q_rot = self._q_rot.data_ptr()
+        a.block_tables, a.tables_stride, a.max_blocks = self._d32[batch:].data_ptr(), max_blocks, max_blocks
+        a.seq_lens, a.max_seq_len = self._d32.data_ptr(), self.capacity
+        a.counters, a.counters_bytes = self._cnt.data_ptr(), self._cnt.numel() * 4
+        a.scratch, a.scratch_bytes = self._scr.data_ptr(), self._scr.numel()
+        a.status = self._status.data_ptr()
+        self._addr = ctypes.addressof(a)
+        self._shapes = ((batch, n_q_heads, 1, D), (batch, Hkv, 1, D))
+
+    def update(self, tables: Sequence[SequenceBlockTable]) -> None:
+        """Grow each table by one position (allocating a block when it crosses a boundary)
+        and copy the step's slots, positions, lengths and block tables to the device."""
+        n, bs = len(tables), self.cache.block_size
+        if n > self.batch:
+            raise ValueError(f"{n} tables for a step of at most {self.batch} sequences")
+        for t in tables:
+            if t.block_size != bs:
+                raise ValueError("block table block_size must equal the cache block size")
+            if t.seq_len >= self.capacity:
+                raise ValueError(f"a sequence would grow past the step's capacity of {self.capacity} positions")
+        if self._copied is not None:
+            self._copied.synchronize()  # the previous step's copies have left the staging buffers
+        positions = [t.seq_len for t in tables]
+        slots = decode_slot_mapping(tables, self.cache.allocator)
+        h64 = self._h64.numpy()
+        h64[0, :n], h64[0, n:] = slots, -1
+        h64[1, :n], h64[1, n:] = positions, 0
+        h32 = self._h32.numpy()
+        lens, blocks = h32[: self.batch], h32[self.batch :].reshape(self.batch, self.max_blocks)
+        lens[:n], lens[n:] = [t.seq_len for t in tables], 0
+        blocks.fill(-1)
+        for b, t in enumerate(tables):
+            ids = t.block_ids[: self.max_blocks]  # positions below capacity live in these
+            blocks[b, : len(ids)] = ids
+        dev = self.cache.keys.device
+        with _ops._DeviceGuard(dev):
+            self._d64.copy_(self._h64, non_blocking=True)
+            self._d32.copy_(self._h32, non_blocking=True)
+            self._copied = torch.cuda.Event()
+            self._copied.record(torch.cuda.current_stream(dev))
+
+    def layer(self, layer_idx: int, q: Tensor, key: Tensor, value: Tensor) -> Tensor:
+        """One layer of the step on the current stream (graph-capturable): q ``[batch,
+        n_q_heads, 1, head_dim]``, key / value ``[batch, kv_heads, 1, head_dim]``, contiguous,
+        before RoPE. Returns the attention output ``[batch, n_q_heads, 1, head_dim]``."""
+        dev = self.cache.keys.device
+        dt = self.cache.keys.dtype
+        for t, shape in ((q, self._shapes[0]), (key, self._shapes[1]), (value, self._shapes[1])):
+            if tuple(t.shape) != shape or not t.is_contiguous() or t.dtype != dt or t.get_device() != dev.index:
+                raise ValueError(f"decode inputs must be contiguous {dt} tensors of shape {shape} on {dev}")
+        if not 0 <= layer_idx < self._args.n_layers:
+            raise ValueError("layer_idx is outside the cache layer range")
+        with _ops._DeviceGuard(dev):
+            out = torch.empty(q.shape, dtype=dt, device=dev)
+            code = self._lib.augur_kv_decode_layer(self._addr, layer_idx, q.data_ptr(), key.data_ptr(),
+                                                   value.data_ptr(), out.data_ptr(),
+                                                   torch.cuda.current_stream(dev).cuda_stream)
+        _lib.check(code, "augur_kv_decode_layer")
+        _ops.launch_count += 2
+        return out
+
+
+def _current_raw_stream(dev: torch.device) -> int:
+    """Handle of the current stream on dev (0 when dev is not the current device, which sends
+    the caller to the general path)."""
+    if dev.index != torch.cuda.current_device():
+        return 0
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    return raw(dev.index) if raw is not None else torch.cuda.current_stream(dev).cuda_stream
 
 
 def paged_decode_layer(

@@ -600,7 +600,7 @@ def bench_decode_step(device, pool, tables) -> dict:
     mapping, uploads) timed eagerly.
     """
     import augur_b200 as ab
-    from augur_b200.decode import DecodeStep, paged_decode_layer
+    from augur_b200.decode import DecodeGraphStep, DecodeStep, paged_decode_layer
 
     Hq, theta = 14, 1000000.0
     tabs = [ab.SequenceBlockTable(block_ids=list(t.block_ids), block_size=t.block_size, seq_len=t.seq_len)
@@ -643,11 +643,35 @@ def bench_decode_step(device, pool, tables) -> dict:
         layers(DecodeStep(pool, tabs))
         torch.cuda.synchronize(device)
         host.append(time.perf_counter() - t0)
+    # the same steps replayed from one captured graph (DecodeGraphStep): per step the host
+    # grows the tables and refreshes the step's buffers, then the 48 launches replay
+    max_blocks = max(len(t.block_ids) for t in tabs) + 4
+    gstep = DecodeGraphStep(pool, B, max_blocks, Hq, theta)
+    gs = torch.cuda.Stream(device)
+    gs.wait_stream(torch.cuda.current_stream(device))
+    ggraph = torch.cuda.CUDAGraph()
+    replay = []
+    with torch.cuda.stream(gs):
+        gstep.update(tabs)
+        with torch.cuda.graph(ggraph, stream=gs):
+            for layer in range(L):
+                gstep.layer(layer, q[layer], k[layer], v[layer])
+        ggraph.replay()
+        for _ in range(5):
+            torch.cuda.synchronize(device)
+            t0 = time.perf_counter()
+            gstep.update(tabs)
+            ggraph.replay()
+            torch.cuda.synchronize(device)
+            replay.append(time.perf_counter() - t0)
+    ggraph.reset()
     tokens = int(sum(t.seq_len for t in tabs))
     return {"seqs": B, "cached_tokens_after": tokens, "launches_per_step": 2 * L,
             "us_per_step_device": round(dev_ms * 1e3, 1), "us_per_layer_device": round(dev_ms * 1e3 / L, 2),
             "us_per_step_with_host": round(statistics.median(host) * 1e6, 1),
-            "timed": "per layer: fused RoPE append + decode attention; device: CUDA graph, L2 flushed"}
+            "us_per_step_graph_with_host": round(statistics.median(replay) * 1e6, 1),
+            "timed": "per layer: fused RoPE append + decode attention; device: CUDA graph, L2 flushed; "
+                     "with host: eager DecodeStep, and DecodeGraphStep update + graph replay"}
 
 
 def bench_decode_attention_large(device, n_seqs: int = 256) -> dict:

@@ -240,6 +240,55 @@ int augur_kv_paged_decode_attention_workspace(int32_t batch, int32_t n_q_heads, 
                                               int32_t flags, int64_t* counters_bytes, int64_t* scratch_bytes);
 
 /*
+ * augur_kv_decode_layer — one layer of a batch's decode step, as one call:
+ * the fused RoPE write of every sequence's new token (augur_kv_rope_scatter)
+ * then decode attention over each whole cached sequence
+ * (augur_kv_paged_decode_attention), both on `stream`. For a decode step of
+ * the whole batch this replaces augur's paged branch of attention
+ * (augur/attention.py:53-86 with paged_cache: apply_rope, write_paged_kv,
+ * read_paged_kv, the GQA repeat and the attention core), which the reference
+ * runs for a batch of one (augur/paged_kv_cache.py:179-180,
+ * augur/generation.py:35-40).
+ *
+ * args holds what every layer of the step shares and is filled once per step:
+ * the pools, the step's slots and positions, the RoPE table, the block tables
+ * and lengths (including the new token), the attention workspace and the
+ * strides of q, key and value. Per layer: its index, the new token's q
+ * (element (b, h, d) at q + b*q_strides[0] + h*q_strides[1] + d), key and
+ * value (likewise with kv_strides) and out, a dense [batch][n_q_heads]
+ * [head_dim] output. The rotated q goes to args->q_rot (dense, same shape).
+ * Returns the first failing call's code; AUGUR_KV_EINVAL for a null args or a
+ * layer outside [0, n_layers).
+ */
+typedef struct augur_kv_decode_args {
+  void* k_pool;                /* layer 0 of the K pool */
+  void* v_pool;                /* layer 0 of the V pool (same strides) */
+  int64_t pool_strides[4];     /* layer, block, kv_head, row (elements; head_dim contiguous) */
+  int64_t num_blocks;
+  int32_t block_size, n_layers, n_q_heads, n_kv_heads, head_dim, dtype, batch, flags;
+  const int64_t* slots;        /* device [batch]: block * block_size + offset of each new token */
+  const int64_t* positions;    /* device [batch]: position of each new token */
+  const void* rope_cos;        /* device [rope_positions][head_dim / 2], cache dtype */
+  const void* rope_sin;
+  int64_t rope_positions;
+  int64_t q_strides[2];        /* batch, head (elements) */
+  int64_t kv_strides[2];       /* batch, head (elements) of key and value */
+  void* q_rot;                 /* device [batch][n_q_heads][head_dim] */
+  const int32_t* block_tables; /* device [batch][tables_stride] */
+  int64_t tables_stride, max_blocks;
+  const int32_t* seq_lens;     /* device [batch] */
+  int32_t max_seq_len, reserved;
+  int32_t* counters;           /* augur_kv_paged_decode_attention workspace */
+  int64_t counters_bytes;
+  void* scratch;
+  int64_t scratch_bytes;
+  int32_t* status;             /* device int32 or NULL */
+} augur_kv_decode_args;
+
+int augur_kv_decode_layer(const augur_kv_decode_args* args, int32_t layer, const void* q, const void* key,
+                          const void* value, void* out, void* stream);
+
+/*
  * Peer memory for the disaggregated mode: a decode GPU's process exports its
  * block pool, a prefill GPU's process opens it and pushes finished blocks into
  * it with augur_kv_copy_runs (vector path: plain 16-byte stores over NVLink).

@@ -109,3 +109,42 @@ def test_missing_library_fails_loudly(monkeypatch):
     monkeypatch.setattr(_lib, "LIB_PATH", "/nonexistent/libaugur_kv.so")
     with pytest.raises(_lib.KVLibraryError, match="no CPU or torch fallback"):
         _lib.load()
+
+
+def test_decode_args_layout_matches_header(tmp_path):
+    """The ctypes mirror of augur_kv_decode_args has the C struct's size and field offsets
+    (compiled here with the host compiler from the header itself)."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no host C compiler")
+    fields = [name for name, _ in _lib.DecodeArgs._fields_]
+    lines = ['#include <stddef.h>', '#include <stdio.h>', '#include "augur_kv.h"', "int main(void) {",
+             '  printf("size %zu\\n", sizeof(augur_kv_decode_args));']
+    lines += [f'  printf("{f} %zu\\n", offsetof(augur_kv_decode_args, {f}));' for f in fields]
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-I", os.path.dirname(HEADER), str(src), "-o", str(exe)], check=True)
+    got = dict(line.split() for line in subprocess.run([str(exe)], check=True, capture_output=True,
+                                                          text=True).stdout.splitlines())
+    assert int(got["size"]) == ctypes.sizeof(_lib.DecodeArgs)
+    for f in fields:
+        assert int(got[f]) == getattr(_lib.DecodeArgs, f).offset, f
+
+
+def test_decode_layer_rejects_bad_arguments_without_touching_the_device():
+    lib = _lib.load()
+    assert lib.augur_kv_decode_layer(None, 0, None, None, None, None, None) == _lib.EINVAL
+    assert b"null args" in lib.augur_kv_last_error()
+    args = _lib.DecodeArgs()
+    args.n_layers = 24
+    args.dtype = _lib.BF16
+    for layer in (-1, 24):
+        assert lib.augur_kv_decode_layer(ctypes.byref(args), layer, None, None, None, None, None) == _lib.EINVAL
+        assert b"outside [0, 24)" in lib.augur_kv_last_error()
+    assert lib.augur_kv_decode_layer(ctypes.byref(args), 0, None, None, None, None, None) == _lib.EINVAL
+    assert b"null pool" in lib.augur_kv_last_error()

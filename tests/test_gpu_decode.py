@@ -74,3 +74,93 @@ def test_decode_layers_match_the_reference_branch(cuda, oracle, path):
     assert_bits_equal(pool.keys, rk, "pool keys")
     assert_bits_equal(pool.values, rv, "pool values")
     assert _ops.read_status(cuda) == _lib.OK
+
+
+def test_graph_step_replays_match_eager_steps(cuda):
+    """A CUDA graph captured once over DecodeGraphStep.layer calls, replayed after each
+    update(), gives the eager DecodeStep results: the same pool bits, the same block tables,
+    attention outputs within the bf16 tolerance (the launch plan sees the step's capacity
+    instead of its longest sequence); padding rows write nothing and return zeros."""
+    from augur_b200.decode import DecodeGraphStep
+
+    L, H, Hq, D, bs, NB = 2, 2, 14, 64, 16, 96
+    prior = [0, 1, 15, 16, 300]
+    cap_seqs, max_blocks = 6, 24
+    g = torch.Generator().manual_seed(31)
+
+    def fresh():
+        pool = ab.PagedKVCache(keys=poison_(torch.empty(L, NB, H, bs, D, dtype=torch.bfloat16, device=cuda)),
+                               values=poison_(torch.empty(L, NB, H, bs, D, dtype=torch.bfloat16, device=cuda)),
+                               block_size=bs, allocator=ab.BlockAllocator(NB))
+        tables = [ab.SequenceBlockTable.empty(bs) for _ in prior]
+        return pool, tables
+
+    pool_e, tabs_e = fresh()
+    pool_g, tabs_g = fresh()
+    T = sum(prior)
+    pk = torch.randn(L, T, H, D, generator=g).to(torch.bfloat16).to(cuda)
+    pv = torch.randn(L, T, H, D, generator=g).to(torch.bfloat16).to(cuda)
+    for pool, tabs in ((pool_e, tabs_e), (pool_g, tabs_g)):
+        sm = batched.prefill_slot_mapping(tabs, prior, pool.allocator)
+        flat = np.concatenate([sm[b, :n] for b, n in enumerate(prior)])
+        batched.write_paged_kv_batch(pool, pk, pv, torch.from_numpy(flat).to(cuda))
+    B = len(prior)
+    steps = 3
+    qs = torch.randn(steps, L, B, Hq, 1, D, generator=g).to(torch.bfloat16).to(cuda)
+    ks = torch.randn(steps, L, B, H, 1, D, generator=g).to(torch.bfloat16).to(cuda)
+    vs = torch.randn(steps, L, B, H, 1, D, generator=g).to(torch.bfloat16).to(cuda)
+
+    # static inputs of the graph: rows past B are padding
+    q_in = torch.zeros(L, cap_seqs, Hq, 1, D, dtype=torch.bfloat16, device=cuda)
+    k_in = torch.zeros(L, cap_seqs, H, 1, D, dtype=torch.bfloat16, device=cuda)
+    v_in = torch.zeros(L, cap_seqs, H, 1, D, dtype=torch.bfloat16, device=cuda)
+    gs = DecodeGraphStep(pool_g, cap_seqs, max_blocks, Hq, THETA)
+    graph = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream(cuda)
+    cs.wait_stream(torch.cuda.current_stream(cuda))
+    outs_g = None
+    for s in range(steps):
+        # eager reference step
+        step = DecodeStep(pool_e, tabs_e)
+        outs_e = [paged_decode_layer(step, pool_e, layer, qs[s, layer], ks[s, layer], vs[s, layer], THETA)
+                  for layer in range(L)]
+        # graph step
+        with torch.cuda.stream(cs):
+            q_in[:, :B].copy_(qs[s])
+            k_in[:, :B].copy_(ks[s])
+            v_in[:, :B].copy_(vs[s])
+            gs.update(tabs_g)
+            if s == 0:
+                with torch.cuda.graph(graph, stream=cs):
+                    outs_g = [gs.layer(layer, q_in[layer], k_in[layer], v_in[layer]) for layer in range(L)]
+            graph.replay()
+        torch.cuda.synchronize(cuda)
+        for layer in range(L):
+            torch.testing.assert_close(outs_g[layer][:B].float(), outs_e[layer].float(), rtol=1e-2, atol=1e-2,
+                                       msg=f"step {s} layer {layer}")
+            assert int(outs_g[layer][B:].abs().sum()) == 0, "padding rows must return zeros"
+    graph.reset()
+    assert [t.block_ids for t in tabs_g] == [t.block_ids for t in tabs_e]
+    assert [t.seq_len for t in tabs_g] == [n + steps for n in prior]
+    assert_bits_equal(pool_g.keys, pool_e.keys.cpu(), "pool keys")
+    assert_bits_equal(pool_g.values, pool_e.values.cpu(), "pool values")
+    assert _ops.read_status(cuda) == _lib.OK
+
+
+def test_graph_step_rejects_what_it_cannot_describe(cuda):
+    from augur_b200.decode import DecodeGraphStep
+
+    pool = ab.PagedKVCache(keys=torch.zeros(1, 8, 2, 16, 64, dtype=torch.bfloat16, device=cuda),
+                           values=torch.zeros(1, 8, 2, 16, 64, dtype=torch.bfloat16, device=cuda),
+                           block_size=16, allocator=ab.BlockAllocator(8))
+    gs = DecodeGraphStep(pool, 2, 2, 14, THETA)
+    with pytest.raises(ValueError, match="at most 2 sequences"):
+        gs.update([ab.SequenceBlockTable.empty(16) for _ in range(3)])
+    full = ab.SequenceBlockTable.empty(16)
+    full.seq_len = 32
+    with pytest.raises(ValueError, match="capacity of 32 positions"):
+        gs.update([full])
+    with pytest.raises(ValueError, match="contiguous"):
+        gs.layer(0, torch.zeros(2, 14, 1, 64, dtype=torch.float16, device=cuda),
+                 torch.zeros(2, 2, 1, 64, dtype=torch.bfloat16, device=cuda),
+                 torch.zeros(2, 2, 1, 64, dtype=torch.bfloat16, device=cuda))
