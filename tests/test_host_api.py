@@ -363,3 +363,13 @@ def test_rope_writes_refuse_cpu_and_bad_shapes():
     with pytest.raises(ValueError, match="slot_mapping and positions"):
         write_paged_kv_batch_rope(pool, q[0].transpose(0, 1), kv[0].transpose(0, 1), kv[0].transpose(0, 1),
                                   torch.zeros(2, dtype=torch.int64), torch.zeros(3, dtype=torch.int64), 1e6, 0)
+
+
+def test_decode_graph_step_refuses_a_cpu_cache():
+    from augur_b200.decode import DecodeGraphStep
+
+    cpu = ab.PagedKVCache(keys=torch.zeros(1, 4, 2, 16, 64, dtype=torch.bfloat16),
+                          values=torch.zeros(1, 4, 2, 16, 64, dtype=torch.bfloat16),
+                          block_size=16, allocator=ab.BlockAllocator(4))
+    with pytest.raises(ValueError, match="needs CUDA tensors"):
+        DecodeGraphStep(cpu, batch=2, max_blocks=2, n_q_heads=14, rope_theta=1e6)
