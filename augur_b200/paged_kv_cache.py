@@ -132,6 +132,16 @@ class PagedPrefixCache:
             block_ids.append(block_id)
         return PagedPrefixCacheMatch(block_ids=block_ids, matched_tokens=len(block_ids) * block_size)
 
+    def lookup(self, parent_hash: int | None, block_tokens: list[int]) -> tuple[int, int] | None:
+        """(hash, block id) of a registered block, or None (an addition to augur's API)."""
+        return self._blocks.get((parent_hash, tuple(block_tokens)))
+
+    def remove_block(self, parent_hash: int | None, block_tokens: list[int]) -> int | None:
+        """Unregister a block and return its id, or None (an addition to augur's API).
+        Blocks chained after it can no longer be matched."""
+        entry = self._blocks.pop((parent_hash, tuple(block_tokens)), None)
+        return None if entry is None else entry[1]
+
     def _hash_block(self, parent_hash: int | None, block_tokens: tuple[int, ...]) -> int:
         return hash((parent_hash, block_tokens))
 
