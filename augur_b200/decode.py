@@ -52,15 +52,22 @@ class DecodeStep:
         self.tables = DecodeTables(tables, device)
         self._fast: tuple | None = None  # launch arguments shared by the layers, built on first use
 
-    def _prepare(self, cache: PagedKVCache, q: Tensor, key: Tensor, rope_theta: float) -> tuple | None:
-        """The argument block every layer of this step shares (augur_kv_decode_args), or None
-        when the inputs need the general path."""
+    def _prepare(self, cache: PagedKVCache, q: Tensor, key: Tensor, value: Tensor,
+                 rope_theta: float) -> tuple | None:
+        """The argument block every layer of this step shares (augur_kv_decode_args) and the
+        input signature it was built for, or None when the inputs need the general path."""
+        if q.dim() != 4 or key.dim() != 4 or value.dim() != 4:
+            return None
         L, NB, Hkv, bs, D = cache.keys.shape
         B, Hq = q.shape[0], q.shape[1]
         dev, dt = cache.keys.device, cache.keys.dtype
-        ok = (B > 0 and self.tables.block_size == bs and Hq % Hkv == 0 and q.dtype == dt and key.dtype == dt
-              and q.device == dev and key.device == dev and cache.keys.stride() == cache.values.stride()
-              and q.shape[3] == D and key.shape[1] == Hkv and key.shape[3] == D)
+        ok = (B == self.batch and B > 0 and self.tables.block_size == bs and Hq % Hkv == 0
+              and tuple(q.shape) == (B, Hq, 1, D) and tuple(key.shape) == (B, Hkv, 1, D)
+              and value.shape == key.shape and value.stride() == key.stride()
+              and q.stride(-1) == 1 and key.stride(-1) == 1
+              and q.dtype == dt and key.dtype == dt and value.dtype == dt
+              and q.device == dev and key.device == dev and value.device == dev
+              and cache.keys.stride() == cache.values.stride())
         if not ok:
             return None
         lib = _lib.load()
@@ -87,21 +94,22 @@ class DecodeStep:
         a.counters, a.counters_bytes = (cnt.data_ptr(), cnt.numel() * 4) if cnt is not None else (None, 0)
         a.scratch, a.scratch_bytes = (scr.data_ptr(), scr.numel()) if scr is not None else (None, 0)
         a.status = status.data_ptr()
-        key_sig = (q.shape, q.stride(), key.shape, key.stride())
+        sig = _signature(q, key, value)
         # the tensors the argument block points into stay referenced with it
-        return (lib, st, ctypes.addressof(a), key_sig, a, cos, sin, q_rot, cnt, scr, status, rope_theta)
+        return (lib, st, ctypes.addressof(a), sig, a, cache, cos, sin, q_rot, cnt, scr, status, rope_theta)
 
     def layer(self, cache: PagedKVCache, layer_idx: int, q: Tensor, key: Tensor, value: Tensor,
               rope_theta: float) -> Tensor | None:
         """paged_decode_layer's two launches as one augur_kv_decode_layer call with the step's
-        prepared arguments, on the current stream; None when the inputs need the general path."""
+        prepared arguments, on the current stream; None when the inputs need the general path
+        (anything other than the shapes, strides, dtypes, devices, cache and stream the
+        arguments were prepared for, or a layer outside the cache)."""
         f = self._fast
-        if f is None or f[-1] != rope_theta:
-            f = self._fast = self._prepare(cache, q, key, rope_theta)
+        if f is None or f[-1] != rope_theta or f[5] is not cache:
+            f = self._fast = self._prepare(cache, q, key, value, rope_theta)
             if f is None:
                 return None
-        if ((q.shape, q.stride(), key.shape, key.stride()) != f[3] or value.shape != key.shape
-                or value.stride() != key.stride() or value.dtype != key.dtype or q.dtype != key.dtype):
+        if _signature(q, key, value) != f[3]:
             return None
         lib, st = f[0], f[1]
         dev = cache.keys.device
@@ -113,6 +121,12 @@ class DecodeStep:
         _lib.check(code, "augur_kv_decode_layer")
         _ops.launch_count += 2
         return out
+
+
+def _signature(q: Tensor, key: Tensor, value: Tensor) -> tuple:
+    """What the prepared arguments of a step assume about a layer's inputs."""
+    return (q.shape, q.stride(), q.dtype, q.get_device(), key.shape, key.stride(), key.dtype, key.get_device(),
+            value.shape, value.stride(), value.dtype, value.get_device())
 
 
 class DecodeGraphStep:
@@ -256,17 +270,14 @@ def paged_decode_layer(
     yet concatenated, before the o-projection). The rotated k and v are in the
     cache afterwards, bit-exact with apply_rope + write_paged_kv.
     """
+    if stream is None:  # the step's prepared launch when the inputs are the ones it was prepared for
+        out = step.layer(cache, layer_idx, q, key, value, rope_theta)
+        if out is not None:
+            return out
     B = step.batch
     for name, t in (("q", q), ("key", key), ("value", value)):
         if t.dim() != 4 or t.shape[0] != B or t.shape[2] != 1:
             raise ValueError(f"{name} must be [batch, heads, 1, head_dim] with one token per sequence")
-        if t.device.type != "cuda" or t.stride(-1) != 1:
-            break
-    else:
-        if stream is None:
-            out = step.layer(cache, layer_idx, q, key, value, rope_theta)
-            if out is not None:
-                return out
     q_rot = write_paged_kv_batch_rope(cache, q[:, :, 0], key[:, :, 0], value[:, :, 0], step.slots, step.positions,
                                       rope_theta, layer_idx, max_position=step.max_position, stream=stream)
     return paged_decode_attention(q_rot, cache, layer_idx, step.tables, stream=stream).unsqueeze(2)

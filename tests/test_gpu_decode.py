@@ -22,9 +22,11 @@ pytestmark = pytest.mark.gpu
 THETA = 1000000.0
 
 
-@pytest.mark.parametrize("path", ["prepared", "general"])
+@pytest.mark.parametrize("path", ["prepared", "general", "mixed"])
 def test_decode_layers_match_the_reference_branch(cuda, oracle, path):
-    """path: the step's prepared launches, or the general wrappers (an explicit stream)."""
+    """path: the step's prepared launches, the general wrappers (an explicit stream), or
+    both in one step (a later layer's q is a strided view, which the prepared arguments
+    do not describe, so that layer takes the general path)."""
     L, H, Hq, D, bs, NB = 2, 2, 14, 64, 16, 64
     prior = [0, 1, 15, 16, 300]
     g = torch.Generator().manual_seed(12)
@@ -53,7 +55,13 @@ def test_decode_layers_match_the_reference_branch(cuda, oracle, path):
         k = torch.randn(len(prior), H, 1, D, generator=g).to(torch.bfloat16)
         v = torch.randn(len(prior), H, 1, D, generator=g).to(torch.bfloat16)
         stream = torch.cuda.current_stream(cuda) if path == "general" else None
-        out = paged_decode_layer(step, pool, layer, q.to(cuda), k.to(cuda), v.to(cuda), THETA, stream=stream)
+        qd = q.to(cuda)
+        if path == "mixed" and layer == 1:
+            wide = torch.empty(len(prior), Hq, 2, D, dtype=torch.bfloat16, device=cuda)
+            wide[:, :, :1] = qd
+            qd = wide[:, :, :1]
+            assert qd.stride() != q.stride()
+        out = paged_decode_layer(step, pool, layer, qd, k.to(cuda), v.to(cuda), THETA, stream=stream)
         assert out.shape == (len(prior), Hq, 1, D)
         for b, n in enumerate(prior):
             pos = torch.tensor([[n]])
