@@ -80,6 +80,20 @@ struct AttnArgs {
   float* ws_ml;
   float* ws_o;
   int32_t* status;
+  // RoPE write of a decode step's new tokens fused into the attention launch
+  // (augur_kv_decode_layer): q is before RoPE, and position seq_len - 1 of
+  // each sequence is its new token, whose k and v come from new_k / new_v
+  // (element (b, h, d) at + b*new_stride_b + h*new_stride_h + d*2); the
+  // rotated k and the v are written to that position's pool row here.
+  int32_t fuse;
+  const char* new_k;
+  const char* new_v;
+  int64_t new_stride_b, new_stride_h;  // bytes
+  const char* rope_cos;  // [rope_n][head_dim / 2] in the cache dtype
+  const char* rope_sin;
+  int64_t rope_n;
+  char* k_w;  // the pools, writable (fused launches only)
+  char* v_w;
 };
 
 constexpr float kNegInf = -INFINITY;
@@ -193,6 +207,29 @@ __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// RoPE of two packed element pairs (x1 from the first half of a row, x2 the
+// same dims of the second half) with packed cos / sin c, s, in the cache
+// dtype: x1' = x1 c - x2 s, x2' = x2 c + x1 s, each product and the sum
+// rounded to the dtype as the reference's three tensor ops round them (the
+// same packed mul.rn / sub.rn / add.rn sequence as rope_scatter_kernel, so
+// the fused and separate RoPE writes give the same bits).
+template <typename T>
+__device__ __forceinline__ void rope_pair(uint32_t& x1, uint32_t& x2, uint32_t c, uint32_t s);
+#define AUGUR_ATTN_ROPE_PAIR(TYPE, SUFFIX)                                                         \
+  template <>                                                                                      \
+  __device__ __forceinline__ void rope_pair<TYPE>(uint32_t & x1, uint32_t & x2, uint32_t c, uint32_t s) { \
+    uint32_t ac, bs, bc, as;                                                                        \
+    asm("mul.rn." SUFFIX " %0, %1, %2;" : "=r"(ac) : "r"(x1), "r"(c));                              \
+    asm("mul.rn." SUFFIX " %0, %1, %2;" : "=r"(bs) : "r"(x2), "r"(s));                              \
+    asm("mul.rn." SUFFIX " %0, %1, %2;" : "=r"(bc) : "r"(x2), "r"(c));                              \
+    asm("mul.rn." SUFFIX " %0, %1, %2;" : "=r"(as) : "r"(x1), "r"(s));                              \
+    asm("sub.rn." SUFFIX " %0, %1, %2;" : "=r"(x1) : "r"(ac), "r"(bs));                             \
+    asm("add.rn." SUFFIX " %0, %1, %2;" : "=r"(x2) : "r"(bc), "r"(as));                             \
+  }
+AUGUR_ATTN_ROPE_PAIR(__nv_bfloat16, "bf16x2")
+AUGUR_ATTN_ROPE_PAIR(__half, "f16x2")
+#undef AUGUR_ATTN_ROPE_PAIR
+
 constexpr int kStageTok = 32;       // tokens a warp stages and processes at a time
 constexpr int kMaxChunks = 256;     // chunks per (sequence, KV head)
 constexpr int kMaxSeq = 1 << 30;    // longest sequence a launch accepts
@@ -215,7 +252,11 @@ struct SplitCfg {
   static constexpr int kPO = D + 4;  // floats per partial row: the transposing stores hit distinct banks
   static_assert((16 * kPO + 32) * 4 <= NS * kWarpStage, "a warp's partial must fit in its stage buffers");
   static_assert(2 * kMaxChunks * 16 * 4 <= kPipe, "chunk maxima and sums must fit in the stage buffers");
-  static constexpr int kTail = (kWarps * 16 + 16 + 16 + 16) * 4;  // fac, cta_m, cta_l, flag + 2 items
+  // fac, cta_m, cta_l, flag, 2 item descriptors; then, for fused launches,
+  // the new token's cos and sin rows and its pool offset
+  static constexpr int kTailNew = 768;
+  static_assert((kWarps * 16 + 16 + 16 + 16) * 4 + 2 * 6 * 4 <= kTailNew, "tail layout");
+  static constexpr int kTail = kTailNew + D * 2 + 16;
   static constexpr int kBytes = kPipe + kTail;
 };
 
@@ -398,7 +439,7 @@ __device__ Item locate(const AttnArgs& a, const Plan& p, int item, int lane, con
 // writes its unnormalised partial (o, m, l) to the scratch slot of its item
 // and the last CTA of the (sequence, KV head) to arrive (atomic counter, no
 // waiting) combines them and resets the counter.
-template <typename T, int D, int NT, int NS>
+template <typename T, int D, int NT, int NS, bool FUSE>
 __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1) ? 3 * NS : 1)
     attn_decode_split_kernel(AttnArgs a) {
   using CF = SplitCfg<D, NS>;
@@ -417,6 +458,10 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
   float* cta_m = fac + W * 16;
   float* cta_l = cta_m + 16;
   int* last_flag = reinterpret_cast<int*>(cta_l + 16);
+  // fused launches: the new token's cos and sin rows, then its pool offset
+  unsigned char* new_cs = smem + CF::kPipe + CF::kTailNew;
+  unsigned char* new_sn = new_cs + D;
+  int64_t* new_ofs = reinterpret_cast<int64_t*>(new_sn + D);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   // Launched as a programmatic dependent of the previous kernel on the
@@ -518,6 +563,7 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
 
   unsigned char* wbuf = smem + warp * NS * CF::kWarpStage;
   const int part = lane % PARTS, row0 = lane / PARTS;
+  const int new_pos = FUSE ? S - 1 : -1;  // fused launches: the step's new token
   const int64_t lane_off = int64_t(hk) * a.head_stride + part * 16;
   const int32_t* tbl = a.tables + int64_t(b) * a.tables_stride;
   const int shift = a.bs_shift;
@@ -548,13 +594,31 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
       const char* vp = a.v;
       int bytes = 0;
       if (pos < tok1) {
-        if (blk >= 0 && blk < a.num_blocks) {
+        const bool blk_ok = blk >= 0 && blk < a.num_blocks;
+        if (blk_ok) {
           const int64_t ofs = int64_t(blk) * a.blk_stride + lane_off + int64_t(off) * a.row_stride;
           kp += ofs;
           vp += ofs;
           bytes = 16;
         } else {
           record_status(a.status, AUGUR_KV_EBOUNDS);  // reads as zeros
+        }
+        if (FUSE && pos == new_pos) {  // the new token: its k and v from the inputs, its cos / sin rows to the tail
+          const int64_t src = int64_t(b) * a.new_stride_b + int64_t(hk) * a.new_stride_h + part * 16;
+          kp = a.new_k + src;
+          vp = a.new_v + src;
+          bytes = 16;
+          if (part == 0)
+            *new_ofs = blk_ok ? int64_t(blk) * a.blk_stride + int64_t(hk) * a.head_stride +
+                                    int64_t(off) * a.row_stride
+                              : int64_t(-1);
+          if (part < PARTS / 2) {
+            const bool in_table = pos < a.rope_n;
+            const int64_t row = in_table ? int64_t(pos) * D : 0;  // D/2 elements of 2 bytes
+            cp_async16(new_cs + part * 16, a.rope_cos + row + part * 16, in_table ? 16 : 0);
+            cp_async16(new_sn + part * 16, a.rope_sin + row + part * 16, in_table ? 16 : 0);
+            if (!in_table && part == 0) record_status(a.status, AUGUR_KV_EBOUNDS);
+          }
         }
       }
       cp_async16(kdst + r * CF::kRowBytes, kp, bytes);
@@ -583,12 +647,60 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
     first_item = false;
   }
   if (warp == 0) publish(slot ^ 1, next_id());  // overlaps this warp's loads
+  if (FUSE && n_my > 0 && S > 0) {
+    // fused launches: q arrives before RoPE. Dims d and d + D/2 of a head sit
+    // in the same lane (k-steps ks and ks + D/32), so each lane rotates its
+    // own fragments with the new token's cos / sin row.
+    const int pos = S - 1;
+    if (pos < a.rope_n) {
+      const char* cs = a.rope_cos + int64_t(pos) * D;
+      const char* sn = a.rope_sin + int64_t(pos) * D;
+#pragma unroll
+      for (int ks = 0; ks < D / 32; ++ks) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int dim = ks * 16 + j * 8 + 2 * t;
+          const uint32_t cv = *reinterpret_cast<const uint32_t*>(cs + dim * 2);
+          const uint32_t sv = *reinterpret_cast<const uint32_t*>(sn + dim * 2);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) rope_pair<T>(qb[ks][nt][j], qb[ks + D / 32][nt][j], cv, sv);
+        }
+      }
+    }
+  }
   for (int it = 0; it < n_my; ++it) {
     const int s0 = tok0 + (warp + it * W) * kStageTok;
     cp_async_wait<NS - 1>();
     __syncwarp();
     const unsigned char* Ks = wbuf + (it % NS) * CF::kWarpStage;
     const unsigned char* Vs = Ks + CF::kStageBytes;
+    if (FUSE && new_pos >= s0 && new_pos < s0 + kStageTok) {
+      // fused launches: the new token's row holds its k and v as given; rotate
+      // k in place (lane l: pieces l and l + PARTS/2, the two halves of the
+      // row) and write the rotated k and the v to the token's pool row
+      unsigned char* kr = const_cast<unsigned char*>(Ks) + (new_pos - s0) * CF::kRowBytes;
+      unsigned char* vr = const_cast<unsigned char*>(Vs) + (new_pos - s0) * CF::kRowBytes;
+      const int64_t dofs = *new_ofs;
+      if (lane < PARTS / 2) {
+        uint4 x1 = *reinterpret_cast<const uint4*>(kr + lane * 16);
+        uint4 x2 = *reinterpret_cast<const uint4*>(kr + (lane + PARTS / 2) * 16);
+        const uint4 cv = *reinterpret_cast<const uint4*>(new_cs + lane * 16);
+        const uint4 sv = *reinterpret_cast<const uint4*>(new_sn + lane * 16);
+        rope_pair<T>(x1.x, x2.x, cv.x, sv.x);
+        rope_pair<T>(x1.y, x2.y, cv.y, sv.y);
+        rope_pair<T>(x1.z, x2.z, cv.z, sv.z);
+        rope_pair<T>(x1.w, x2.w, cv.w, sv.w);
+        *reinterpret_cast<uint4*>(kr + lane * 16) = x1;
+        *reinterpret_cast<uint4*>(kr + (lane + PARTS / 2) * 16) = x2;
+        if (dofs >= 0) {
+          *reinterpret_cast<uint4*>(a.k_w + dofs + lane * 16) = x1;
+          *reinterpret_cast<uint4*>(a.k_w + dofs + (lane + PARTS / 2) * 16) = x2;
+        }
+      }
+      if (lane < PARTS && dofs >= 0)
+        *reinterpret_cast<uint4*>(a.v_w + dofs + lane * 16) = *reinterpret_cast<const uint4*>(vr + lane * 16);
+      __syncwarp();
+    }
 
     // S^T: two 16-token row tiles x NT 8-head column tiles
     float s[2][NT][4];
@@ -969,7 +1081,8 @@ bool mma_shape_ok(int dtype, int head_dim, int groups) {
 template <typename T, int D, int NT, int NS>
 int split_slots(int* slots_out) {
   using CF = SplitCfg<D, NS>;
-  auto kern = attn_decode_split_kernel<T, D, NT, NS>;
+  auto kern = attn_decode_split_kernel<T, D, NT, NS, false>;
+  auto kern_fused = attn_decode_split_kernel<T, D, NT, NS, true>;
   static int slots[kMaxDevices] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
@@ -978,10 +1091,15 @@ int split_slots(int* slots_out) {
   std::lock_guard<std::recursive_mutex> lock(g_cache_mutex);
   if (slots[dev] == 0) {
     int per_sm = 0;
+    int per_sm_fused = 0;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, CF::kBytes) != cudaSuccess ||
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, CF::kThreads, CF::kBytes) != cudaSuccess)
+        cudaFuncSetAttribute(kern_fused, cudaFuncAttributeMaxDynamicSharedMemorySize, CF::kBytes) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, CF::kThreads, CF::kBytes) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_fused, kern_fused, CF::kThreads, CF::kBytes) !=
+            cudaSuccess)
       return check_launch("attn_decode_split_kernel occupancy");
-    slots[dev] = std::max(1, per_sm) * sms;
+    // one grid size for both (the persistent grid must be resident either way)
+    slots[dev] = std::max(1, std::min(per_sm, per_sm_fused)) * sms;
   }
   *slots_out = slots[dev];
   return AUGUR_KV_OK;
@@ -1022,7 +1140,8 @@ int launch_split(AttnArgs a, int max_seq, int32_t* cnt, int64_t cnt_bytes, void*
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, attn_decode_split_kernel<T, D, NT, NS>, a);
+  const cudaError_t e = a.fuse ? cudaLaunchKernelEx(&cfg, attn_decode_split_kernel<T, D, NT, NS, true>, a)
+                               : cudaLaunchKernelEx(&cfg, attn_decode_split_kernel<T, D, NT, NS, false>, a);
   if (e != cudaSuccess) return fail(AUGUR_KV_ECUDA, "attn_decode_split_kernel: %s", cudaGetErrorString(e));
   return check_launch("attn_decode_split_kernel");
 }
@@ -1081,12 +1200,16 @@ AUGUR_KV_EXPORT int augur_kv_paged_decode_attention_workspace(int32_t batch, int
                                                          scratch_bytes);
 }
 
-AUGUR_KV_EXPORT int augur_kv_paged_decode_attention(
+namespace augur_kv_dev {
+
+int paged_decode_attention_impl(
     const void* q, const int64_t* q_strides, const void* k_pool, const void* v_pool, const int64_t* pool_strides,
     int64_t num_blocks, int32_t block_size, const int32_t* block_tables, int64_t tables_stride, int64_t max_blocks,
     const int32_t* seq_lens, int32_t max_seq_len, int32_t batch, int32_t n_q_heads, int32_t n_kv_heads,
     int32_t head_dim, int32_t dtype, void* out, const int64_t* out_strides, int32_t flags, int32_t* counters,
-    int64_t counters_bytes, void* scratch, int64_t scratch_bytes, int32_t* status, void* stream) {
+    int64_t counters_bytes, void* scratch, int64_t scratch_bytes, int32_t* status, void* stream, const FusedRope* fuse,
+    bool* fused) {
+  if (fused != nullptr) *fused = false;
   g_last_error[0] = '\0';
   const int es = elem_size(dtype);
   if (es == 0) return fail(AUGUR_KV_EINVAL, "paged_decode_attention: unknown dtype %d", dtype);
@@ -1148,6 +1271,28 @@ AUGUR_KV_EXPORT int augur_kv_paged_decode_attention(
                     reinterpret_cast<uintptr_t>(q) | uintptr_t(a.q_stride_b) | uintptr_t(a.q_stride_h);
   const bool mma_ok = mma_shape_ok(dtype, head_dim, a.groups) && (align & 15u) == 0 &&
                       a.row_stride == int64_t(head_dim) * es;
+  if (fuse != nullptr) {
+    // the fused RoPE write rides on the tensor-core kernel only; otherwise
+    // nothing is launched and the caller issues the two launches
+    const uintptr_t falign = reinterpret_cast<uintptr_t>(fuse->new_k) | reinterpret_cast<uintptr_t>(fuse->new_v) |
+                             uintptr_t(fuse->new_stride_b * es) | uintptr_t(fuse->new_stride_h * es) |
+                             reinterpret_cast<uintptr_t>(fuse->cos) | reinterpret_cast<uintptr_t>(fuse->sin);
+    if (flags == AUGUR_KV_ATTN_GENERIC || !mma_ok || (falign & 15u) != 0 || fuse->new_k == nullptr ||
+        fuse->new_v == nullptr || fuse->cos == nullptr || fuse->sin == nullptr || fuse->n_pos <= 0 ||
+        max_seq_len > kMaxSeq)
+      return AUGUR_KV_OK;
+    a.fuse = 1;
+    a.new_k = static_cast<const char*>(fuse->new_k);
+    a.new_v = static_cast<const char*>(fuse->new_v);
+    a.new_stride_b = fuse->new_stride_b * es;
+    a.new_stride_h = fuse->new_stride_h * es;
+    a.rope_cos = static_cast<const char*>(fuse->cos);
+    a.rope_sin = static_cast<const char*>(fuse->sin);
+    a.rope_n = fuse->n_pos;
+    a.k_w = static_cast<char*>(const_cast<void*>(k_pool));
+    a.v_w = static_cast<char*>(const_cast<void*>(v_pool));
+    if (fused != nullptr) *fused = true;
+  }
   if (flags != AUGUR_KV_ATTN_GENERIC && mma_ok) {
     if (max_seq_len > kMaxSeq)
       return fail(AUGUR_KV_EINVAL, "paged_decode_attention: max_seq_len above %d", kMaxSeq);
@@ -1178,4 +1323,19 @@ AUGUR_KV_EXPORT int augur_kv_paged_decode_attention(
   }
   attn_decode_generic_kernel<<<dim3(unsigned(n_q_heads), unsigned(batch), 1u), kGenericThreads, smem, st>>>(a);
   return check_launch("attn_decode_generic_kernel");
+}
+
+}  // namespace augur_kv_dev
+
+AUGUR_KV_EXPORT int augur_kv_paged_decode_attention(
+    const void* q, const int64_t* q_strides, const void* k_pool, const void* v_pool, const int64_t* pool_strides,
+    int64_t num_blocks, int32_t block_size, const int32_t* block_tables, int64_t tables_stride, int64_t max_blocks,
+    const int32_t* seq_lens, int32_t max_seq_len, int32_t batch, int32_t n_q_heads, int32_t n_kv_heads,
+    int32_t head_dim, int32_t dtype, void* out, const int64_t* out_strides, int32_t flags, int32_t* counters,
+    int64_t counters_bytes, void* scratch, int64_t scratch_bytes, int32_t* status, void* stream) {
+  return augur_kv_dev::paged_decode_attention_impl(q, q_strides, k_pool, v_pool, pool_strides, num_blocks, block_size,
+                                                   block_tables, tables_stride, max_blocks, seq_lens, max_seq_len,
+                                                   batch, n_q_heads, n_kv_heads, head_dim, dtype, out, out_strides,
+                                                   flags, counters, counters_bytes, scratch, scratch_bytes, status,
+                                                   stream, nullptr, nullptr);
 }

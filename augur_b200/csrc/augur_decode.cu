@@ -39,13 +39,27 @@ AUGUR_KV_EXPORT int augur_kv_decode_layer(const augur_kv_decode_args* A, int32_t
   const int64_t q_rot[4] = {0, 0, int64_t(Hq) * D, D};
   const int64_t dst[4] = {0, A->pool_strides[1], A->pool_strides[3], A->pool_strides[2]};
   const int64_t col[2] = {0, 1};
-  int rc = augur_kv_rope_scatter(key, value, kv_src, kv_src, A->batch, A->dtype, kl, vl, dst, A->block_size,
+  const int64_t dense[2] = {int64_t(Hq) * D, D};
+  const int64_t pool[3] = {A->pool_strides[1], A->pool_strides[2], A->pool_strides[3]};
+  // One launch: the attention kernel rotates q and the new k itself and
+  // writes the new k and v to their pool rows (position seq_lens[b] - 1,
+  // which is positions[b] with its slot slots[b] for a step built by
+  // DecodeStep or DecodeGraphStep).
+  const augur_kv_dev::FusedRope fr{key, value, A->kv_strides[0], A->kv_strides[1], A->rope_cos, A->rope_sin,
+                                   A->rope_positions};
+  const int64_t q_two[2] = {A->q_strides[0], A->q_strides[1]};
+  bool fused = false;
+  int rc = augur_kv_dev::paged_decode_attention_impl(
+      q, q_two, kl, vl, pool, A->num_blocks, A->block_size, A->block_tables, A->tables_stride, A->max_blocks,
+      A->seq_lens, A->max_seq_len, A->batch, Hq, A->n_kv_heads, D, A->dtype, out, dense, A->flags, A->counters,
+      A->counters_bytes, A->scratch, A->scratch_bytes, A->status, stream, &fr, &fused);
+  if (rc != AUGUR_KV_OK || fused) return rc;
+  // otherwise the RoPE write, then the attention
+  rc = augur_kv_rope_scatter(key, value, kv_src, kv_src, A->batch, A->dtype, kl, vl, dst, A->block_size,
                                  A->num_blocks, A->slots, col, 0, A->positions, col, A->rope_cos, A->rope_sin,
                                  A->rope_positions, q, q_src, A->q_rot, q_rot, Hq, A->batch, 1, A->n_kv_heads, D,
                                  A->status, stream);
   if (rc != AUGUR_KV_OK) return rc;
-  const int64_t dense[2] = {int64_t(Hq) * D, D};
-  const int64_t pool[3] = {A->pool_strides[1], A->pool_strides[2], A->pool_strides[3]};
   return augur_kv_paged_decode_attention(A->q_rot, dense, kl, vl, pool, A->num_blocks, A->block_size,
                                          A->block_tables, A->tables_stride, A->max_blocks, A->seq_lens,
                                          A->max_seq_len, A->batch, Hq, A->n_kv_heads, D, A->dtype, out, dense,

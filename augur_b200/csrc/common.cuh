@@ -25,6 +25,33 @@ int elem_size(int32_t dtype);
 // SM count of the current device (cached).
 int sm_count();
 
+// The RoPE write of a decode step's new tokens, fused into the decode
+// attention launch: new k / v (element (b, h, d) at + b*new_stride_b +
+// h*new_stride_h + d, element strides), the cos / sin tables and their rows.
+struct FusedRope {
+  const void* new_k;
+  const void* new_v;
+  int64_t new_stride_b, new_stride_h;
+  const void* cos;
+  const void* sin;
+  int64_t n_pos;
+};
+
+// augur_kv_paged_decode_attention, optionally with `fuse`: q is then before
+// RoPE, position seq_lens[b] - 1 of each sequence is its new token, taken
+// from fuse->new_k / new_v, rotated, attended and written to its pool row.
+// With `fuse`, *fused says whether the fused launch was issued; when it was
+// not (the shape or alignment needs the generic kernel), nothing was
+// launched and the call returned AUGUR_KV_OK.
+int paged_decode_attention_impl(const void* q, const int64_t* q_strides, const void* k_pool, const void* v_pool,
+                                const int64_t* pool_strides, int64_t num_blocks, int32_t block_size,
+                                const int32_t* block_tables, int64_t tables_stride, int64_t max_blocks,
+                                const int32_t* seq_lens, int32_t max_seq_len, int32_t batch, int32_t n_q_heads,
+                                int32_t n_kv_heads, int32_t head_dim, int32_t dtype, void* out,
+                                const int64_t* out_strides, int32_t flags, int32_t* counters, int64_t counters_bytes,
+                                void* scratch, int64_t scratch_bytes, int32_t* status, void* stream,
+                                const FusedRope* fuse, bool* fused);
+
 // First device-side error wins.
 __device__ __forceinline__ void record_status(int32_t* status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);

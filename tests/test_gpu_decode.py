@@ -172,3 +172,48 @@ def test_graph_step_rejects_what_it_cannot_describe(cuda):
         gs.layer(0, torch.zeros(2, 14, 1, 64, dtype=torch.float16, device=cuda),
                  torch.zeros(2, 2, 1, 64, dtype=torch.bfloat16, device=cuda),
                  torch.zeros(2, 2, 1, 64, dtype=torch.bfloat16, device=cuda))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("head_dim", [64, 128])
+def test_fused_decode_layer_matches_separate_launches(cuda, dtype, head_dim):
+    """augur_kv_decode_layer rotates q and the new k inside the attention launch and writes
+    the new k / v rows itself (bf16 / fp16); the general path runs the RoPE write and the
+    attention as two launches. Both must leave the same pool bits and return the same
+    outputs bit for bit, step after step. float32 takes the two-launch form in both."""
+    L, H, Hq, bs, NB = 2, 2, 14, 16, 96
+    prior = [1, 15, 16, 47, 300]
+    g = torch.Generator().manual_seed(77)
+
+    def setup():
+        pool = ab.PagedKVCache(keys=poison_(torch.empty(L, NB, H, bs, head_dim, dtype=dtype, device=cuda)),
+                               values=poison_(torch.empty(L, NB, H, bs, head_dim, dtype=dtype, device=cuda)),
+                               block_size=bs, allocator=ab.BlockAllocator(NB))
+        tables = [ab.SequenceBlockTable.empty(bs) for _ in prior]
+        return pool, tables
+
+    pools = [setup(), setup()]
+    T = sum(prior)
+    pk = torch.randn(L, T, H, head_dim, generator=g).to(dtype).to(cuda)
+    pv = torch.randn(L, T, H, head_dim, generator=g).to(dtype).to(cuda)
+    for pool, tables in pools:
+        sm = batched.prefill_slot_mapping(tables, prior, pool.allocator)
+        flat = np.concatenate([sm[b, :n] for b, n in enumerate(prior)])
+        batched.write_paged_kv_batch(pool, pk, pv, torch.from_numpy(flat).to(cuda))
+    B = len(prior)
+    for s in range(3):
+        q = torch.randn(L, B, Hq, 1, head_dim, generator=g).to(dtype).to(cuda)
+        k = torch.randn(L, B, H, 1, head_dim, generator=g).to(dtype).to(cuda)
+        v = torch.randn(L, B, H, 1, head_dim, generator=g).to(dtype).to(cuda)
+        outs = []
+        for i, (pool, tables) in enumerate(pools):
+            step = DecodeStep(pool, tables)
+            stream = torch.cuda.current_stream(cuda) if i == 1 else None
+            outs.append([paged_decode_layer(step, pool, layer, q[layer], k[layer], v[layer], THETA, stream=stream)
+                         for layer in range(L)])
+        torch.cuda.synchronize(cuda)
+        for layer in range(L):
+            assert_bits_equal(outs[0][layer], outs[1][layer], f"step {s} layer {layer} output")
+    assert_bits_equal(pools[0][0].keys, pools[1][0].keys, "pool keys")
+    assert_bits_equal(pools[0][0].values, pools[1][0].values, "pool values")
+    assert _ops.read_status(cuda) == _lib.OK
