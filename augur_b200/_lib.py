@@ -115,7 +115,7 @@ class DecodeArgs(ctypes.Structure):
         ("max_blocks", ctypes.c_int64),
         ("seq_lens", ctypes.c_void_p),
         ("max_seq_len", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("launches", ctypes.c_int32),
         ("counters", ctypes.c_void_p),
         ("counters_bytes", ctypes.c_int64),
         ("scratch", ctypes.c_void_p),

@@ -19,7 +19,7 @@ using augur_kv_dev::fail;
 
 #define AUGUR_KV_EXPORT extern "C" __attribute__((visibility("default")))
 
-AUGUR_KV_EXPORT int augur_kv_decode_layer(const augur_kv_decode_args* A, int32_t layer, const void* q,
+AUGUR_KV_EXPORT int augur_kv_decode_layer(augur_kv_decode_args* A, int32_t layer, const void* q,
                                           const void* key, const void* value, void* out, void* stream) {
   if (A == nullptr) return fail(AUGUR_KV_EINVAL, "decode_layer: null args");
   if (layer < 0 || layer >= A->n_layers)
@@ -53,7 +53,9 @@ AUGUR_KV_EXPORT int augur_kv_decode_layer(const augur_kv_decode_args* A, int32_t
       q, q_two, kl, vl, pool, A->num_blocks, A->block_size, A->block_tables, A->tables_stride, A->max_blocks,
       A->seq_lens, A->max_seq_len, A->batch, Hq, A->n_kv_heads, D, A->dtype, out, dense, A->flags, A->counters,
       A->counters_bytes, A->scratch, A->scratch_bytes, A->status, stream, &fr, &fused);
+  A->launches = fused ? 1 : 0;
   if (rc != AUGUR_KV_OK || fused) return rc;
+  A->launches = 2;
   // otherwise the RoPE write, then the attention
   rc = augur_kv_rope_scatter(key, value, kv_src, kv_src, A->batch, A->dtype, kl, vl, dst, A->block_size,
                                  A->num_blocks, A->slots, col, 0, A->positions, col, A->rope_cos, A->rope_sin,

@@ -4,19 +4,19 @@ augur's paged branch (augur/attention.py:53-86 with paged_cache) runs for a
 batch of one (paged_kv_cache.py:179-180, generation.py:35-40). Per layer it
 rotates q and k (apply_rope), writes the token through the block table
 (write_paged_kv), gathers the whole sequence back (read_paged_kv), repeats
-the KV heads and attends. Here a whole batch does the same in two launches
-per layer:
-- the fused RoPE write (augur_kv_rope_scatter): q rotated, k rotated into its
-  slot, v copied;
-- decode attention straight from the pool (augur_kv_paged_decode_attention)
-  over every sequence including its new token.
+the KV heads and attends. Here a whole batch does the same in one launch per
+layer: the decode attention kernel reads every sequence straight from the
+pool, rotates q and the new k itself, uses the new k and v for the token's
+row and writes them to its slot (bf16 / fp16, head_dim 64 or 128). Other
+shapes take two launches: the RoPE write (augur_kv_rope_scatter), then the
+attention (augur_kv_paged_decode_attention).
 
 The host work of a step (growing each table by one position, the slot
 mapping, the device tables) is done once per step in DecodeStep and shared
-by all layers. So is everything the two launches need apart from the layer's
+by all layers. So is everything the launch needs apart from the layer's
 own tensors: the checks, the RoPE table, the attention counters and scratch,
 gathered in one argument block (augur_kv_decode_args). A layer is then one
-foreign call, augur_kv_decode_layer, which issues both launches. The
+foreign call, augur_kv_decode_layer. The
 projections and everything after the attention core stay the model's.
 """
 
@@ -100,7 +100,7 @@ class DecodeStep:
 
     def layer(self, cache: PagedKVCache, layer_idx: int, q: Tensor, key: Tensor, value: Tensor,
               rope_theta: float) -> Tensor | None:
-        """paged_decode_layer's two launches as one augur_kv_decode_layer call with the step's
+        """paged_decode_layer's work as one augur_kv_decode_layer call with the step's
         prepared arguments, on the current stream; None when the inputs need the general path
         (anything other than the shapes, strides, dtypes, devices, cache and stream the
         arguments were prepared for, or a layer outside the cache)."""
@@ -119,7 +119,7 @@ class DecodeStep:
         code = lib.augur_kv_decode_layer(f[2], layer_idx, q.data_ptr(), key.data_ptr(), value.data_ptr(),
                                          out.data_ptr(), st.cuda_stream)
         _lib.check(code, "augur_kv_decode_layer")
-        _ops.launch_count += 2
+        _ops.launch_count += f[4].launches
         return out
 
 
@@ -239,7 +239,7 @@ class DecodeGraphStep:
                                                    value.data_ptr(), out.data_ptr(),
                                                    torch.cuda.current_stream(dev).cuda_stream)
         _lib.check(code, "augur_kv_decode_layer")
-        _ops.launch_count += 2
+        _ops.launch_count += self._args.launches
         return out
 
 

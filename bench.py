@@ -600,6 +600,7 @@ def bench_decode_step(device, pool, tables) -> dict:
     mapping, uploads) timed eagerly.
     """
     import augur_b200 as ab
+    from augur_b200 import _ops
     from augur_b200.decode import DecodeGraphStep, DecodeStep, paged_decode_layer
 
     Hq, theta = 14, 1000000.0
@@ -622,8 +623,10 @@ def bench_decode_step(device, pool, tables) -> dict:
     with torch.cuda.stream(cs):
         layers(step)
     torch.cuda.synchronize(device)
+    launches_before = _ops.launch_count
     with torch.cuda.graph(graph, stream=cs):
         layers(step)
+    launches_per_step = _ops.launch_count - launches_before
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
     times = []
     for _ in range(7):
@@ -666,11 +669,11 @@ def bench_decode_step(device, pool, tables) -> dict:
             replay.append(time.perf_counter() - t0)
     ggraph.reset()
     tokens = int(sum(t.seq_len for t in tabs))
-    return {"seqs": B, "cached_tokens_after": tokens, "launches_per_step": 2 * L,
+    return {"seqs": B, "cached_tokens_after": tokens, "launches_per_step": launches_per_step,
             "us_per_step_device": round(dev_ms * 1e3, 1), "us_per_layer_device": round(dev_ms * 1e3 / L, 2),
             "us_per_step_with_host": round(statistics.median(host) * 1e6, 1),
             "us_per_step_graph_with_host": round(statistics.median(replay) * 1e6, 1),
-            "timed": "per layer: fused RoPE append + decode attention; device: CUDA graph, L2 flushed; "
+            "timed": "per layer: decode attention with the RoPE append fused into it; device: CUDA graph, L2 flushed; "
                      "with host: eager DecodeStep, and DecodeGraphStep update + graph replay"}
 
 

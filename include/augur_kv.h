@@ -241,9 +241,9 @@ int augur_kv_paged_decode_attention_workspace(int32_t batch, int32_t n_q_heads, 
 
 /*
  * augur_kv_decode_layer — one layer of a batch's decode step, as one call:
- * the fused RoPE write of every sequence's new token (augur_kv_rope_scatter)
- * then decode attention over each whole cached sequence
- * (augur_kv_paged_decode_attention), both on `stream`. For a decode step of
+ * the RoPE write of every sequence's new token (as augur_kv_rope_scatter) and
+ * decode attention over each whole cached sequence (as
+ * augur_kv_paged_decode_attention), on `stream`. For a decode step of
  * the whole batch this replaces augur's paged branch of attention
  * (augur/attention.py:53-86 with paged_cache: apply_rope, write_paged_kv,
  * read_paged_kv, the GQA repeat and the attention core), which the reference
@@ -256,9 +256,17 @@ int augur_kv_paged_decode_attention_workspace(int32_t batch, int32_t n_q_heads, 
  * strides of q, key and value. Per layer: its index, the new token's q
  * (element (b, h, d) at q + b*q_strides[0] + h*q_strides[1] + d), key and
  * value (likewise with kv_strides) and out, a dense [batch][n_q_heads]
- * [head_dim] output. The rotated q goes to args->q_rot (dense, same shape).
- * Returns the first failing call's code; AUGUR_KV_EINVAL for a null args or a
- * layer outside [0, n_layers).
+ * [head_dim] output.
+ * The new token of sequence b is position seq_lens[b] - 1; positions[b] must
+ * equal it and slots[b] must be its slot in the block table, as DecodeStep
+ * and DecodeGraphStep build them. For bf16 / fp16 with head_dim 64 or 128
+ * and <= 16 query heads per KV head (16-byte aligned rows), this is one
+ * launch: the attention kernel rotates q and the new k itself and writes the
+ * new k and v rows, bit for bit what the two separate launches write and
+ * return. Other shapes run augur_kv_rope_scatter (the rotated q into
+ * args->q_rot, otherwise unused scratch) and then the attention.
+ * Returns the first failing code; AUGUR_KV_EINVAL for a null args or a layer
+ * outside [0, n_layers).
  */
 typedef struct augur_kv_decode_args {
   void* k_pool;                /* layer 0 of the K pool */
@@ -277,7 +285,8 @@ typedef struct augur_kv_decode_args {
   const int32_t* block_tables; /* device [batch][tables_stride] */
   int64_t tables_stride, max_blocks;
   const int32_t* seq_lens;     /* device [batch] */
-  int32_t max_seq_len, reserved;
+  int32_t max_seq_len;
+  int32_t launches;            /* out: kernels the latest augur_kv_decode_layer call launched (1 or 2) */
   int32_t* counters;           /* augur_kv_paged_decode_attention workspace */
   int64_t counters_bytes;
   void* scratch;
@@ -285,7 +294,7 @@ typedef struct augur_kv_decode_args {
   int32_t* status;             /* device int32 or NULL */
 } augur_kv_decode_args;
 
-int augur_kv_decode_layer(const augur_kv_decode_args* args, int32_t layer, const void* q, const void* key,
+int augur_kv_decode_layer(augur_kv_decode_args* args, int32_t layer, const void* q, const void* key,
                           const void* value, void* out, void* stream);
 
 /*

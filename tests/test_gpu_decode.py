@@ -211,6 +211,8 @@ def test_fused_decode_layer_matches_separate_launches(cuda, dtype, head_dim):
             stream = torch.cuda.current_stream(cuda) if i == 1 else None
             outs.append([paged_decode_layer(step, pool, layer, q[layer], k[layer], v[layer], THETA, stream=stream)
                          for layer in range(L)])
+            if i == 0:  # the prepared call: one launch per layer when the attention kernel fuses the write
+                assert step._fast[4].launches == (2 if dtype == torch.float32 else 1)
         torch.cuda.synchronize(cuda)
         for layer in range(L):
             assert_bits_equal(outs[0][layer], outs[1][layer], f"step {s} layer {layer} output")
