@@ -19,6 +19,16 @@
 //    an online softmax. Chunks of one sequence combine through
 //    caller-provided counters and scratch: the last CTA to arrive (an atomic
 //    counter; no CTA ever waits) merges the partials and writes the output.
+//    Its fused instance (template argument FUSE, launched only for
+//    augur_kv_decode_layer) also does the decode step's RoPE write, which
+//    the reference runs first (apply_rope then write_paged_kv,
+//    augur/attention.py:53-71):
+//      - q arrives before RoPE and is rotated in registers;
+//      - the new token (position seq_len - 1) is staged from the layer's k
+//        and v inputs instead of the pool, its k rotated in shared memory;
+//      - the owning warp writes that k and v to the token's pool row.
+//    The rotation uses the same packed ops as rope_scatter_kernel, so the
+//    results are those of the two separate launches, bit for bit.
 //  * attn_decode_generic_kernel (any dtype / shape): one CTA per (sequence,
 //    query head), scores of the whole sequence in shared memory, then the
 //    reference's order of operations: max, exp, sum, normalise, P.V.
