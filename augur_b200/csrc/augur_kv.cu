@@ -406,7 +406,10 @@ __global__ void __launch_bounds__(256, AUGUR_KV_SCATTER_MIN_CTAS) scatter_rows_k
     const uint32_t t = tg * TPW + sub;
     if (t >= a.n_tokens) continue;
     int64_t row, col, major, off;
-    if (!scatter_resolve(a, t, row, col, major, off)) continue;
+    // the source rows depend only on the token: their loads go out together
+    // with the slot-index load, and only the stores wait for the slot
+    scatter_rowcol(a, t, row, col);
+    const int64_t idx = __ldg(a.index + row * a.index_stride[0] + col * a.index_stride[1]);
     const int l0 = int(lg) * LU;
     const int nl = (n_layers - l0) < LU ? (n_layers - l0) : LU;
     T val[LU][UPL];
@@ -418,6 +421,7 @@ __global__ void __launch_bounds__(256, AUGUR_KV_SCATTER_MIN_CTAS) scatter_rows_k
           val[k][i] = load_stream<VEC>(sb[i] + int64_t(l0 + k) * s_layer[i] + row * s_row[i] + col * s_col[i]);
       }
     }
+    if (!scatter_slot(a, row, idx, major, off)) continue;
     const int64_t dbase = major * d_major + off * d_row;
 #pragma unroll
     for (int k = 0; k < LU; ++k) {
