@@ -217,29 +217,6 @@ __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// RoPE of two packed element pairs (x1 from the first half of a row, x2 the
-// same dims of the second half) with packed cos / sin c, s, in the cache
-// dtype: x1' = x1 c - x2 s, x2' = x2 c + x1 s, each product and the sum
-// rounded to the dtype as the reference's three tensor ops round them (the
-// same packed mul.rn / sub.rn / add.rn sequence as rope_scatter_kernel, so
-// the fused and separate RoPE writes give the same bits).
-template <typename T>
-__device__ __forceinline__ void rope_pair(uint32_t& x1, uint32_t& x2, uint32_t c, uint32_t s);
-#define AUGUR_ATTN_ROPE_PAIR(TYPE, SUFFIX)                                                         \
-  template <>                                                                                      \
-  __device__ __forceinline__ void rope_pair<TYPE>(uint32_t & x1, uint32_t & x2, uint32_t c, uint32_t s) { \
-    uint32_t ac, bs, bc, as;                                                                        \
-    asm("mul.rn." SUFFIX " %0, %1, %2;" : "=r"(ac) : "r"(x1), "r"(c));                              \
-    asm("mul.rn." SUFFIX " %0, %1, %2;" : "=r"(bs) : "r"(x2), "r"(s));                              \
-    asm("mul.rn." SUFFIX " %0, %1, %2;" : "=r"(bc) : "r"(x2), "r"(c));                              \
-    asm("mul.rn." SUFFIX " %0, %1, %2;" : "=r"(as) : "r"(x1), "r"(s));                              \
-    asm("sub.rn." SUFFIX " %0, %1, %2;" : "=r"(x1) : "r"(ac), "r"(bs));                             \
-    asm("add.rn." SUFFIX " %0, %1, %2;" : "=r"(x2) : "r"(bc), "r"(as));                             \
-  }
-AUGUR_ATTN_ROPE_PAIR(__nv_bfloat16, "bf16x2")
-AUGUR_ATTN_ROPE_PAIR(__half, "f16x2")
-#undef AUGUR_ATTN_ROPE_PAIR
-
 constexpr int kStageTok = 32;       // tokens a warp stages and processes at a time
 constexpr int kMaxChunks = 256;     // chunks per (sequence, KV head)
 constexpr int kMaxSeq = 1 << 30;    // longest sequence a launch accepts

@@ -168,32 +168,26 @@ struct Rotate {
   }
 };
 
-#define AUGUR_ROPE_PACKED(TYPE, SUFFIX)                                                                     \
-  template <>                                                                                               \
-  struct Rotate<TYPE, 8> {                                                                                  \
-    static __device__ __forceinline__ void run(const Piece<TYPE, 8>& x1, const Piece<TYPE, 8>& x2,          \
-                                               const Piece<TYPE, 8>& c, const Piece<TYPE, 8>& s,            \
-                                               Piece<TYPE, 8>& o1, Piece<TYPE, 8>& o2) {                    \
-      const uint32_t* a = reinterpret_cast<const uint32_t*>(&x1);                                           \
-      const uint32_t* b = reinterpret_cast<const uint32_t*>(&x2);                                           \
-      const uint32_t* cc = reinterpret_cast<const uint32_t*>(&c);                                           \
-      const uint32_t* ss = reinterpret_cast<const uint32_t*>(&s);                                           \
-      uint32_t* p = reinterpret_cast<uint32_t*>(&o1);                                                       \
-      uint32_t* q = reinterpret_cast<uint32_t*>(&o2);                                                       \
-      _Pragma("unroll") for (int e = 0; e < 4; ++e) {                                                       \
-        uint32_t ac, bs, bc, as;                                                                            \
-        asm("mul.rn." SUFFIX " %0, %1, %2;" : "=r"(ac) : "r"(a[e]), "r"(cc[e]));                              \
-        asm("mul.rn." SUFFIX " %0, %1, %2;" : "=r"(bs) : "r"(b[e]), "r"(ss[e]));                              \
-        asm("mul.rn." SUFFIX " %0, %1, %2;" : "=r"(bc) : "r"(b[e]), "r"(cc[e]));                              \
-        asm("mul.rn." SUFFIX " %0, %1, %2;" : "=r"(as) : "r"(a[e]), "r"(ss[e]));                              \
-        asm("sub.rn." SUFFIX " %0, %1, %2;" : "=r"(p[e]) : "r"(ac), "r"(bs));                                 \
-        asm("add.rn." SUFFIX " %0, %1, %2;" : "=r"(q[e]) : "r"(bc), "r"(as));                                 \
-      }                                                                                                     \
-    }                                                                                                       \
-  };
-AUGUR_ROPE_PACKED(__nv_bfloat16, "bf16x2")
-AUGUR_ROPE_PACKED(__half, "f16x2")
-#undef AUGUR_ROPE_PACKED
+// 16-bit types: the eight elements of a piece as four packed pairs through
+// rope_pair (common.cuh), the sequence the fused decode attention uses too.
+template <typename T>
+struct RotatePacked {
+  static __device__ __forceinline__ void run(const Piece<T, 8>& x1, const Piece<T, 8>& x2, const Piece<T, 8>& c,
+                                             const Piece<T, 8>& s, Piece<T, 8>& o1, Piece<T, 8>& o2) {
+    const uint32_t* cc = reinterpret_cast<const uint32_t*>(&c);
+    const uint32_t* ss = reinterpret_cast<const uint32_t*>(&s);
+    o1 = x1;
+    o2 = x2;
+    uint32_t* p = reinterpret_cast<uint32_t*>(&o1);
+    uint32_t* q = reinterpret_cast<uint32_t*>(&o2);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) rope_pair<T>(p[e], q[e], cc[e], ss[e]);
+  }
+};
+template <>
+struct Rotate<__nv_bfloat16, 8> : RotatePacked<__nv_bfloat16> {};
+template <>
+struct Rotate<__half, 8> : RotatePacked<__half> {};
 
 // One thread per piece (VEC elements of each half of a rotated row, or VEC
 // elements of a v row; VEC = 16 bytes, or 1 on the unaligned path) of every

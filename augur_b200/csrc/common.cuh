@@ -1,6 +1,8 @@
 // common.cuh — helpers shared by the source files of libaugur_kv.so (internal).
 #pragma once
 
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -56,5 +58,32 @@ int paged_decode_attention_impl(const void* q, const int64_t* q_strides, const v
 __device__ __forceinline__ void record_status(int32_t* status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);
 }
+
+// RoPE of two packed element pairs (x1 from the first half of a row, x2 the
+// same dims of the second half) with packed cos / sin c, s, in the cache
+// dtype: x1' = x1 c - x2 s, x2' = x2 c + x1 s, each product and the sum
+// rounded to the dtype as the reference's three tensor ops round them (the
+// single definition rope_scatter_kernel and the fused decode attention both
+// use, so the fused and separate RoPE writes give the same bits). Each
+// packed op rounds the exact result once; the reference rounds the float32
+// result (itself exact for the products) to T, and since 24 >= 2 x 11 + 2
+// that double rounding gives the same bits. The explicit .rn keeps the
+// compiler from contracting a product and a sum into a fused multiply-add.
+template <typename T>
+__device__ __forceinline__ void rope_pair(uint32_t& x1, uint32_t& x2, uint32_t c, uint32_t s);
+#define AUGUR_KV_ROPE_PAIR(TYPE, SUFFIX)                                                         \
+  template <>                                                                                      \
+  __device__ __forceinline__ void rope_pair<TYPE>(uint32_t & x1, uint32_t & x2, uint32_t c, uint32_t s) { \
+    uint32_t ac, bs, bc, as;                                                                        \
+    asm("mul.rn." SUFFIX " %0, %1, %2;" : "=r"(ac) : "r"(x1), "r"(c));                              \
+    asm("mul.rn." SUFFIX " %0, %1, %2;" : "=r"(bs) : "r"(x2), "r"(s));                              \
+    asm("mul.rn." SUFFIX " %0, %1, %2;" : "=r"(bc) : "r"(x2), "r"(c));                              \
+    asm("mul.rn." SUFFIX " %0, %1, %2;" : "=r"(as) : "r"(x1), "r"(s));                              \
+    asm("sub.rn." SUFFIX " %0, %1, %2;" : "=r"(x1) : "r"(ac), "r"(bs));                             \
+    asm("add.rn." SUFFIX " %0, %1, %2;" : "=r"(x2) : "r"(bc), "r"(as));                             \
+  }
+AUGUR_KV_ROPE_PAIR(__nv_bfloat16, "bf16x2")
+AUGUR_KV_ROPE_PAIR(__half, "f16x2")
+#undef AUGUR_KV_ROPE_PAIR
 
 }  // namespace augur_kv_dev
