@@ -11,7 +11,6 @@ end with every block free.
 
 from __future__ import annotations
 
-import numpy as np
 import pytest
 import torch
 
