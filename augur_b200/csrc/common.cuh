@@ -26,6 +26,9 @@ int check_launch(const char* what);
 int elem_size(int32_t dtype);
 // SM count of the current device (cached).
 int sm_count();
+// Resident CTAs per SM of `kernel` at `threads` threads, no dynamic shared
+// memory (occupancy calculator; cached per device and kernel).
+int resident_ctas(const void* kernel, int threads);
 
 // The RoPE write of a decode step's new tokens, fused into the decode
 // attention launch: new k / v (element (b, h, d) at + b*new_stride_b +
