@@ -104,6 +104,12 @@ struct AttnArgs {
   int64_t rope_n;
   char* k_w;  // the pools, writable (fused launches only)
   char* v_w;
+  // fused launches: the step's positions and slots as the caller built them
+  // (may be null). The kernel takes the new token's position from seq_len - 1
+  // and its slot from the block table; it records AUGUR_KV_EBOUNDS where
+  // these disagree with them (the two-launch path uses them directly).
+  const int64_t* chk_pos;
+  const int64_t* chk_slot;
 };
 
 constexpr float kNegInf = -INFINITY;
@@ -162,6 +168,10 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// 8-byte async copy global -> shared (both addresses 8-byte aligned).
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
 // 16-byte async copy global -> shared; src_bytes = 0 writes 16 zero bytes.
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
@@ -243,7 +253,8 @@ struct SplitCfg {
   // the new token's cos and sin rows and its pool offset
   static constexpr int kTailNew = 768;
   static_assert((kWarps * 16 + 16 + 16 + 16) * 4 + 2 * 6 * 4 <= kTailNew, "tail layout");
-  static constexpr int kTail = kTailNew + D * 2 + 16;
+  // pool offset, then the caller's position and slot of the new token, as read
+  static constexpr int kTail = kTailNew + D * 2 + 32;
   static constexpr int kBytes = kPipe + kTail;
 };
 
@@ -449,6 +460,7 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
   unsigned char* new_cs = smem + CF::kPipe + CF::kTailNew;
   unsigned char* new_sn = new_cs + D;
   int64_t* new_ofs = reinterpret_cast<int64_t*>(new_sn + D);
+  int64_t* new_chk = new_ofs + 1;  // [0] caller's position, [1] caller's slot, [2] the table's slot
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   // Launched as a programmatic dependent of the previous kernel on the
@@ -595,10 +607,16 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
           kp = a.new_k + src;
           vp = a.new_v + src;
           bytes = 16;
-          if (part == 0)
+          if (part == 0) {
             *new_ofs = blk_ok ? int64_t(blk) * a.blk_stride + int64_t(hk) * a.head_stride +
                                     int64_t(off) * a.row_stride
                               : int64_t(-1);
+            new_chk[2] = int64_t(blk) * a.block_size + off;
+            if (a.chk_pos != nullptr) {  // arrive with the stage; compared when the row is written
+              cp_async8(new_chk, a.chk_pos + b);
+              cp_async8(new_chk + 1, a.chk_slot + b);
+            }
+          }
           if (part < PARTS / 2) {
             const bool in_table = pos < a.rope_n;
             const int64_t row = in_table ? int64_t(pos) * D : 0;  // D/2 elements of 2 bytes
@@ -668,6 +686,8 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
       unsigned char* kr = const_cast<unsigned char*>(Ks) + (new_pos - s0) * CF::kRowBytes;
       unsigned char* vr = const_cast<unsigned char*>(Vs) + (new_pos - s0) * CF::kRowBytes;
       const int64_t dofs = *new_ofs;
+      if (lane == 0 && a.chk_pos != nullptr && (new_chk[0] != int64_t(new_pos) || new_chk[1] != new_chk[2]))
+        record_status(a.status, AUGUR_KV_EBOUNDS);  // the caller's position or slot is not the table's
       if (lane < PARTS / 2) {
         uint4 x1 = *reinterpret_cast<const uint4*>(kr + lane * 16);
         uint4 x2 = *reinterpret_cast<const uint4*>(kr + (lane + PARTS / 2) * 16);
@@ -1276,6 +1296,11 @@ int paged_decode_attention_impl(
     a.rope_cos = static_cast<const char*>(fuse->cos);
     a.rope_sin = static_cast<const char*>(fuse->sin);
     a.rope_n = fuse->n_pos;
+    a.chk_pos = fuse->positions;
+    a.chk_slot = fuse->positions != nullptr ? fuse->slots : nullptr;
+    if ((fuse->positions == nullptr) != (fuse->slots == nullptr) ||
+        ((reinterpret_cast<uintptr_t>(fuse->positions) | reinterpret_cast<uintptr_t>(fuse->slots)) & 7u) != 0)
+      return fail(AUGUR_KV_EINVAL, "decode_layer: positions and slots must both be given, 8-byte aligned");
     a.k_w = static_cast<char*>(const_cast<void*>(k_pool));
     a.v_w = static_cast<char*>(const_cast<void*>(v_pool));
     if (fused != nullptr) *fused = true;

@@ -42,11 +42,13 @@ AUGUR_KV_EXPORT int augur_kv_decode_layer(augur_kv_decode_args* A, int32_t layer
   const int64_t dense[2] = {int64_t(Hq) * D, D};
   const int64_t pool[3] = {A->pool_strides[1], A->pool_strides[2], A->pool_strides[3]};
   // One launch: the attention kernel rotates q and the new k itself and
-  // writes the new k and v to their pool rows (position seq_lens[b] - 1,
-  // which is positions[b] with its slot slots[b] for a step built by
-  // DecodeStep or DecodeGraphStep).
-  const augur_kv_dev::FusedRope fr{key, value, A->kv_strides[0], A->kv_strides[1], A->rope_cos, A->rope_sin,
-                                   A->rope_positions};
+  // writes the new k and v to their pool rows (position seq_lens[b] - 1 and
+  // its slot in the block table; positions[b] and slots[b] must name the
+  // same, as DecodeStep and DecodeGraphStep build them, and the kernel
+  // records AUGUR_KV_EBOUNDS where they do not).
+  const augur_kv_dev::FusedRope fr{key,         value,       A->kv_strides[0], A->kv_strides[1],
+                                   A->rope_cos, A->rope_sin, A->rope_positions, A->positions,
+                                   A->slots};
   const int64_t q_two[2] = {A->q_strides[0], A->q_strides[1]};
   bool fused = false;
   int rc = augur_kv_dev::paged_decode_attention_impl(

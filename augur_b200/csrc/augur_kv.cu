@@ -1042,14 +1042,18 @@ AUGUR_KV_EXPORT int augur_kv_scatter(const void* src_k, const void* src_v, const
   return check_launch("scatter_vec_kernel");
 }
 
-AUGUR_KV_EXPORT int augur_kv_copy_runs(const void* src_k, const void* src_v, const int64_t* src_strides,
-                                  int64_t src_majors, int64_t src_rows_per_major, int32_t src_dtype,
-                                  void* dst_k, void* dst_v, const int64_t* dst_strides,
-                                  int64_t dst_majors, int64_t dst_rows_per_major, int32_t dst_dtype,
-                                  const int32_t* runs, int64_t n_runs, int32_t max_rows,
-                                  int32_t n_layers, int32_t n_heads, int32_t head_dim,
-                                  int32_t flags, int32_t* status, void* stream) {
-  g_last_error[0] = '\0';
+namespace augur_kv_dev {
+
+// Shared body of augur_kv_copy_runs and augur_kv_copy_runs_noalloc. With
+// launch = false it runs every host-side check and returns before the first
+// CUDA call, so a caller can reject bad arguments before it touches anything.
+int copy_runs_impl(const void* src_k, const void* src_v, const int64_t* src_strides,
+                   int64_t src_majors, int64_t src_rows_per_major, int32_t src_dtype,
+                   void* dst_k, void* dst_v, const int64_t* dst_strides,
+                   int64_t dst_majors, int64_t dst_rows_per_major, int32_t dst_dtype,
+                   const int32_t* runs, int64_t n_runs, int32_t max_rows,
+                   int32_t n_layers, int32_t n_heads, int32_t head_dim,
+                   int32_t flags, int32_t* status, void* stream, bool launch) {
   const int es = elem_size(src_dtype), ed = elem_size(dst_dtype);
   if (es == 0 || ed == 0) return fail(AUGUR_KV_EINVAL, "copy_runs: unknown dtype %d/%d", src_dtype, dst_dtype);
   if (n_runs < 0 || n_layers < 0) return fail(AUGUR_KV_EINVAL, "copy_runs: negative sizes");
@@ -1108,6 +1112,7 @@ AUGUR_KV_EXPORT int augur_kv_copy_runs(const void* src_k, const void* src_v, con
     a.vpr = head_dim;
     a.unit_bytes_src = es;
     a.unit_bytes_dst = ed;
+    if (!launch) return AUGUR_KV_OK;
     const dim3 grid{grid_x(uint64_t(n_runs), 8, planes, uint64_t(sms) * 16), unsigned(planes), 1u};
     copy_runs_convert_kernel<<<grid, 256, 0, st>>>(a);
     return check_launch("copy_runs_convert_kernel");
@@ -1126,6 +1131,7 @@ AUGUR_KV_EXPORT int augur_kv_copy_runs(const void* src_k, const void* src_v, con
   // AUTO takes the vector path: on B200 it measured faster than the bulk
   // pipeline for 2 KiB runs (config-3 handoff 6.1 vs 5.4 TB/s).
   if (bulk_ok && flags == AUGUR_KV_COPY_BULK) {
+    if (!launch) return AUGUR_KV_OK;
     a.stage_bytes = int32_t(((int64_t(max_rows) * row_bytes + 127) / 128) * 128);
     int stages = (kBulkSmemBudget - kBulkBarBytes) / (kBulkWarps * a.stage_bytes);
     if (stages > kBulkMaxStages) stages = kBulkMaxStages;
@@ -1155,6 +1161,7 @@ AUGUR_KV_EXPORT int augur_kv_copy_runs(const void* src_k, const void* src_v, con
     return check_launch("copy_runs_bulk_kernel");
   }
 
+  if (!launch) return AUGUR_KV_OK;
   int vec = 16;
   while (vec > 1 && (align_bits & uintptr_t(vec - 1)) != 0) vec >>= 1;
   a.vpr = int32_t(row_bytes / vec);
@@ -1174,6 +1181,21 @@ AUGUR_KV_EXPORT int augur_kv_copy_runs(const void* src_k, const void* src_v, con
   }
 #undef AUGUR_RUNS_LAUNCH
   return check_launch("copy_runs_vec_kernel");
+}
+
+}  // namespace augur_kv_dev
+
+AUGUR_KV_EXPORT int augur_kv_copy_runs(const void* src_k, const void* src_v, const int64_t* src_strides,
+                                  int64_t src_majors, int64_t src_rows_per_major, int32_t src_dtype,
+                                  void* dst_k, void* dst_v, const int64_t* dst_strides,
+                                  int64_t dst_majors, int64_t dst_rows_per_major, int32_t dst_dtype,
+                                  const int32_t* runs, int64_t n_runs, int32_t max_rows,
+                                  int32_t n_layers, int32_t n_heads, int32_t head_dim,
+                                  int32_t flags, int32_t* status, void* stream) {
+  g_last_error[0] = '\0';
+  return copy_runs_impl(src_k, src_v, src_strides, src_majors, src_rows_per_major, src_dtype, dst_k, dst_v,
+                        dst_strides, dst_majors, dst_rows_per_major, dst_dtype, runs, n_runs, max_rows,
+                        n_layers, n_heads, head_dim, flags, status, stream, true);
 }
 
 // ---------------------------------------------------------------------------
@@ -1350,8 +1372,15 @@ AUGUR_KV_EXPORT int augur_kv_copy_runs_noalloc(
                 (long long)n_runs, AUGUR_KV_NOALLOC_MAX_RUNS);
   if (n_runs == 0 || n_layers == 0) return AUGUR_KV_OK;
   if (host_runs == nullptr) return fail(AUGUR_KV_EINVAL, "copy_runs_noalloc: null host_runs");
+  // Every argument check of the copy runs first: a call that is rejected must
+  // not overwrite the shared array, which an earlier call on another stream
+  // may still be reading.
+  int rc = copy_runs_impl(src_k, src_v, src_strides, src_majors, src_rows_per_major, src_dtype, dst_k, dst_v,
+                          dst_strides, dst_majors, dst_rows_per_major, dst_dtype, host_runs, n_runs, max_rows,
+                          n_layers, n_heads, head_dim, flags, status, stream, false);
+  if (rc != AUGUR_KV_OK) return rc;
   int32_t* scratch = nullptr;
-  const int rc = noalloc_runs_ptr(&scratch);
+  rc = noalloc_runs_ptr(&scratch);
   if (rc != AUGUR_KV_OK) return rc;
   // Stream-ordered staging of the descriptors, then the same launch as
   // augur_kv_copy_runs reading them from the scratch array.
@@ -1359,7 +1388,7 @@ AUGUR_KV_EXPORT int augur_kv_copy_runs_noalloc(
                                         cudaMemcpyHostToDevice, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess)
     return fail(AUGUR_KV_ECUDA, "copy_runs_noalloc: staging runs: %s", cudaGetErrorString(e));
-  return augur_kv_copy_runs(src_k, src_v, src_strides, src_majors, src_rows_per_major, src_dtype, dst_k,
-                            dst_v, dst_strides, dst_majors, dst_rows_per_major, dst_dtype, scratch, n_runs,
-                            max_rows, n_layers, n_heads, head_dim, flags, status, stream);
+  return copy_runs_impl(src_k, src_v, src_strides, src_majors, src_rows_per_major, src_dtype, dst_k, dst_v,
+                        dst_strides, dst_majors, dst_rows_per_major, dst_dtype, scratch, n_runs, max_rows,
+                        n_layers, n_heads, head_dim, flags, status, stream, true);
 }

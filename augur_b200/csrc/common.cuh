@@ -40,6 +40,10 @@ struct FusedRope {
   const void* cos;
   const void* sin;
   int64_t n_pos;
+  // the step's positions and slots as the caller built them (device int64
+  // [batch], or both null): checked against seq_lens - 1 and the block table
+  const int64_t* positions;
+  const int64_t* slots;
 };
 
 // augur_kv_paged_decode_attention, optionally with `fuse`: q is then before

@@ -352,8 +352,14 @@ int augur_kv_wait(const int32_t* flag, int32_t value, int64_t timeout_ns, int32_
  * themselves. It calls no cudaMalloc, cudaFree or other allocating routine.
  *
  * - n_runs > AUGUR_KV_NOALLOC_MAX_RUNS is rejected with AUGUR_KV_EINVAL.
- * - The first call on each device looks up the array's device address
- *   (cudaGetSymbolAddress); make that first call before any stream capture.
+ * - The first call on each device with work to do (n_runs > 0; a call with
+ *   no runs returns before this) looks up the array's device address
+ *   (cudaGetSymbolAddress). Under lazy module loading (the CUDA 12 default)
+ *   that lookup may load this library's module onto the device and commit
+ *   the array there, so make that first call before the engine reserves its
+ *   device memory and before any stream capture.
+ * - Every argument check runs before anything is staged: a call rejected
+ *   with AUGUR_KV_EINVAL leaves the array as it was.
  * - host_runs is read by a stream-ordered host-to-device copy: pageable memory
  *   may be reused when the call returns; pinned memory must stay unchanged
  *   until the stream has passed this call.

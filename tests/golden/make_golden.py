@@ -1,9 +1,9 @@
 """Generate the golden fixtures by running the reference (semioz/augur) itself.
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <checkout of semioz/augur>
 
-This script needs the reference source tree (pure Python + torch) and runs
-only in the build container; the fixtures it writes are committed and are
+(or set AUGUR_REFERENCE to the checkout). This script needs the reference
+source tree (pure Python + torch) and runs only where that tree exists; the fixtures it writes are committed and are
 all that the tests read. Every case starts from caches filled with the byte
 0xFF (a NaN pattern), runs the reference's own functions, and stores inputs
 plus the resulting cache contents, so a comparison covers both the written
@@ -460,9 +460,13 @@ def config1(ref):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("AUGUR_REFERENCE"),
+                    help="root of a semioz/augur checkout (its src/ holds the augur package); "
+                         "defaults to $AUGUR_REFERENCE")
     ap.add_argument("--skip-config1", action="store_true")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference <augur checkout> or set AUGUR_REFERENCE")
     sys.path.insert(0, os.path.join(args.reference, "src"))
     import augur.attention  # noqa: F401
     import augur.config

@@ -219,3 +219,28 @@ def test_fused_decode_layer_matches_separate_launches(cuda, dtype, head_dim):
     assert_bits_equal(pools[0][0].keys, pools[1][0].keys, "pool keys")
     assert_bits_equal(pools[0][0].values, pools[1][0].values, "pool values")
     assert _ops.read_status(cuda) == _lib.OK
+
+
+@pytest.mark.parametrize("field", ["positions", "slots"])
+def test_fused_decode_layer_flags_positions_or_slots_off_the_table(cuda, field):
+    """The one-launch layer takes each new token's position from seq_len - 1 and its slot
+    from the block table; a caller's positions or slots that disagree are reported as
+    AUGUR_KV_EBOUNDS (the kernel still writes where the table says)."""
+    L, H, Hq, D, bs, NB = 1, 2, 14, 64, 16, 32
+    pool = ab.PagedKVCache(keys=torch.zeros(L, NB, H, bs, D, dtype=torch.bfloat16, device=cuda),
+                           values=torch.zeros(L, NB, H, bs, D, dtype=torch.bfloat16, device=cuda),
+                           block_size=bs, allocator=ab.BlockAllocator(NB))
+    tables = [ab.SequenceBlockTable.empty(bs) for _ in range(3)]
+    batched.prefill_slot_mapping(tables, [5, 16, 40], pool.allocator)
+    g = torch.Generator(device=cuda).manual_seed(3)
+    q = torch.randn(3, Hq, 1, D, generator=g, device=cuda).to(torch.bfloat16)
+    k = torch.randn(3, H, 1, D, generator=g, device=cuda).to(torch.bfloat16)
+    _ops.read_status(cuda)
+    step = DecodeStep(pool, tables)
+    assert step.layer(pool, 0, q, k, k, THETA) is not None
+    torch.cuda.synchronize()
+    assert _ops.read_status(cuda) == _lib.OK  # consistent step: no report
+    getattr(step, field)[1] += 1  # sequence 1's position or slot no longer matches its table
+    assert step.layer(pool, 0, q, k, k, THETA) is not None
+    torch.cuda.synchronize()
+    assert _ops.read_status(cuda) == _lib.EBOUNDS

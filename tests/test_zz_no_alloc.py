@@ -8,7 +8,12 @@ stages them in a fixed array inside the library. These tests call it through
 the C ABI and require its results to be bit-identical to the regular entry
 point's, over two calls in a row that share the library's array (the second
 with fewer runs, so stale descriptors from the first are present), plus the
-size limit. This file is collected last on purpose.
+size limit. The second call must also leave the device's free memory as it
+was: the entry point allocates nothing.
+
+The tests here depend on no other test and pass alone or after the rest of
+the suite. The file name sorts last only so that a run stopped at its first
+failure (pytest -x) has already run every other test if one of these fails.
 """
 
 from __future__ import annotations
@@ -86,10 +91,14 @@ def test_noalloc_matches_copy_runs_on_two_calls(cuda):
     assert _call(lib.augur_kv_copy_runs, pools[0][0], pools[0][1], *outs[0], gather_dev.data_ptr(),
                  gather.shape[0], 8, _lib.COPY_VECTOR, status) == _lib.OK
     gather_host = np.ascontiguousarray(gather, dtype=np.int32)
+    torch.cuda.synchronize()
+    free_before, _ = torch.cuda.mem_get_info(cuda)
     assert _call(lib.augur_kv_copy_runs_noalloc, pools[0][0], pools[0][1], *outs[1],
                  gather_host.ctypes.data_as(ctypes.c_void_p), gather.shape[0], 8, _lib.COPY_VECTOR,
                  status) == _lib.OK
     torch.cuda.synchronize()
+    free_after, _ = torch.cuda.mem_get_info(cuda)
+    assert free_after == free_before, "the no-allocation entry point changed the device's free memory"
     assert_bits_equal(outs[1][0], outs[0][0], "call 2 keys")
     assert_bits_equal(outs[1][1], outs[0][1], "call 2 values")
     # and the gather really moved data: rows [0, n_0) of batch row 0 equal the source
@@ -105,3 +114,15 @@ def test_noalloc_rejects_more_runs_than_its_scratch(cuda):
                  _lib.NOALLOC_MAX_RUNS + 1, 16, _lib.COPY_AUTO, _ops.status_word(cuda))
     assert code == _lib.EINVAL
     assert b"exceed the fixed scratch" in lib.augur_kv_last_error()
+
+
+def test_noalloc_checks_arguments_before_staging(cuda):
+    # an argument the copy itself rejects (unknown flags) fails the call with
+    # the copy's own message, before any descriptor is staged
+    lib = _lib.load()
+    t = torch.empty(1, 1, 1, 16, 64, dtype=torch.bfloat16, device=cuda)
+    runs = np.zeros((1, 5), dtype=np.int32)
+    code = _call(lib.augur_kv_copy_runs_noalloc, t, t, t, t, runs.ctypes.data_as(ctypes.c_void_p), 1, 16,
+                 64, _ops.status_word(cuda))
+    assert code == _lib.EINVAL
+    assert b"copy_runs: unknown flags" in lib.augur_kv_last_error()
