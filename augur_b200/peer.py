@@ -123,21 +123,39 @@ def open_pool(exported: ExportedPool, device: torch.device | None = None) -> Pee
     return PeerPool(exported, device)
 
 
-def push_runs(src: PagedKVCache, dst: PeerPool, runs: np.ndarray, stream: torch.cuda.Stream | None = None) -> int:
-    """Copy row runs {src_block, src_row, dst_block, dst_row, n_rows} from a local pool into the peer pool.
+@dataclass
+class PreparedPush:
+    """A push whose run list is already on the prefill GPU: launching it moves no host data."""
 
-    One launch on this process's device; returns the payload bytes moved.
-    """
+    src: PagedKVCache
+    dst: PeerPool
+    runs: torch.Tensor  # int32 [n_runs, 5] on the source device, each run at most max_rows rows
+    max_rows: int
+    payload_bytes: int
+
+
+def prepare_push(src: PagedKVCache, dst: PeerPool, runs: np.ndarray) -> PreparedPush:
+    """Check the two pools against each other, cut the runs {src_block, src_row, dst_block,
+    dst_row, n_rows} to the copy's row limit and upload them once (for pushes repeated with the
+    same blocks, or issued from inside a CUDA graph)."""
     L, NB, H, bs, D = src.keys.shape
     if dst.shape[0] != L or dst.shape[2] != H or dst.shape[4] != D or dst.dtype != src.keys.dtype:
         raise ValueError("source and destination pools have different layer/head/dim/dtype")
     max_rows = _ops.max_rows_for(D, src.keys.element_size(), cap_rows=max(bs, dst.block_size))
     runs = split_runs(np.asarray(runs, dtype=np.int64).reshape(-1, 5), max_rows)
-    if runs.shape[0] == 0:
+    runs_t = torch.from_numpy(np.ascontiguousarray(runs, dtype=np.int32)).to(src.keys.device)
+    payload = int(runs[:, 4].astype(np.int64).sum()) * L * 2 * H * D * src.keys.element_size()
+    return PreparedPush(src, dst, runs_t, max_rows, payload)
+
+
+def push_prepared(p: PreparedPush, stream: torch.cuda.Stream | None = None) -> int:
+    """Launch a prepared push on the source GPU (one kernel); returns the payload bytes moved."""
+    if p.runs.shape[0] == 0:
         return 0
+    src, dst = p.src, p.dst
+    L, NB, H, bs, D = src.keys.shape
     lib = _lib.load()
     device = src.keys.device
-    runs_t = torch.from_numpy(np.ascontiguousarray(runs)).to(device)
     st = stream if stream is not None else torch.cuda.current_stream(device)
     sk = src.keys
     s_str = (sk.stride(0), sk.stride(1), sk.stride(3), sk.stride(2))
@@ -147,7 +165,7 @@ def push_runs(src: PagedKVCache, dst: PeerPool, runs: np.ndarray, stream: torch.
         code = lib.augur_kv_copy_runs(
             sk.data_ptr(), src.values.data_ptr(), _lib.i64_array(s_str), NB, bs, _ops.dtype_code(sk),
             dst.keys_ptr, dst.values_ptr, _lib.i64_array(d_str), dst.shape[1], dst.shape[3],
-            _ops.dtype_code(sk), runs_t.data_ptr(), runs_t.shape[0], max_rows, L, H, D,
+            _ops.dtype_code(sk), p.runs.data_ptr(), p.runs.shape[0], p.max_rows, L, H, D,
             # plain stores to peer memory (no bulk/TMA path), each thread
             # ending with a system-scope fence so a later signal() cannot
             # become visible on the peer before the data
@@ -155,8 +173,21 @@ def push_runs(src: PagedKVCache, dst: PeerPool, runs: np.ndarray, stream: torch.
             _ops.status_word(device).data_ptr(), st.cuda_stream)
     _lib.check(code, "augur_kv_copy_runs (peer push)")
     _ops.launch_count += 1
-    _ops.keep_until_done(st, runs_t)
-    return int(runs[:, 4].sum()) * L * 2 * H * D * sk.element_size()
+    return p.payload_bytes
+
+
+def push_runs(src: PagedKVCache, dst: PeerPool, runs: np.ndarray, stream: torch.cuda.Stream | None = None) -> int:
+    """Copy row runs {src_block, src_row, dst_block, dst_row, n_rows} from a local pool into the peer pool.
+
+    One launch on this process's device; returns the payload bytes moved.
+    """
+    p = prepare_push(src, dst, runs)
+    if p.runs.shape[0] == 0:
+        return 0
+    st = stream if stream is not None else torch.cuda.current_stream(src.keys.device)
+    moved = push_prepared(p, stream=st)
+    _ops.keep_until_done(st, p.runs)
+    return moved
 
 
 def push_blocks(src: PagedKVCache, src_blocks: Sequence[int], dst: PeerPool, dst_blocks: Sequence[int],

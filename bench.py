@@ -18,9 +18,18 @@ U[512,2048] tokens (us per sequence), the decode append (us per step), the
 prefix fork with copy-on-write, the roofline of the scatter kernel and the
 CPU baseline (the C oracle on this host's cores).
 
-Under torchrun (N>1) every rank owns its own GPU, pool and seeded batches
-(weak scaling, no data-path collective); the timed region is bracketed by a
-barrier and device synchronisation and the max over ranks is taken.
+Under torchrun (N>1) every rank owns its own GPU, pool and seeded batches:
+the headline config-2 batch is replicated per rank (weak scaling, no
+data-path collective); the timed region is bracketed by a barrier and device
+synchronisation and the max over ranks is taken.
+
+At every N the line's extra.box carries config 5: 2,048 lognormal sequences
+sharded by tokens (LPT) over the N ranks, total work fixed (strong scaling),
+step = prefill scatter + 128 decode appends as one CUDA graph per rank. At
+even N, extra.disagg carries the disaggregated push: ranks [0, N/2) prefill
+config 5 and push the finished blocks over NVLink to rank + N/2, which runs
+the appends. Both report bit_exact from a parity check of a seeded sample of
+sequences on every rank against the oracle, made after the timed regions.
 
 --impl reference times the reference algorithm on the host CPU (the C
 restatement in oracle/, all host threads) on the same workload; the
@@ -441,6 +450,17 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
         extra = run_extras(device)
     del pool
     torch.cuda.empty_cache()
+    if not args.skip_scaleout:
+        # north_star's multi-GPU workloads, every rank taking part: config 5
+        # sharded over the ranks (strong scaling) and, at even N, the
+        # disaggregated push; both checked against the oracle on every rank
+        box = box_phase(world, rank, local)
+        if rank == 0:
+            extra["box"] = box
+        if world >= 2 and world % 2 == 0:
+            dis = disagg_phase(world, rank, local)
+            if rank == 0:
+                extra["disagg"] = dis
 
     if rank != 0:
         return None
@@ -461,7 +481,9 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
                                "block 16, 65536-block pool (config 2)",
                    "tokens_per_step": T, "bytes_per_step": step_bytes,
                    "l2": "4 rotating seeded batches with disjoint blocks: 805 MB touched per rotation > 126 MB L2",
-                   "parallelism": f"sequence-sharded dp{world} (one pool per GPU)",
+                   "parallelism": f"replicated per rank (weak scaling): each of the {world} GPU(s) scatters "
+                                  "its own config-2 batch into its own pool; config 5 sharded over the "
+                                  "ranks (strong scaling) is extra.box",
                    "timed": "CUDA graph replays of one launch per step, CUDA events"},
         "e2e": e2e, "gpu_launches": gpu_launches, "roofline": roofline, "clocks": clocks.summary(),
         "extra": extra,
@@ -890,196 +912,394 @@ def run_extras(device, handoff_only: bool = False, attention_only: bool = False,
 
 
 # ---------------------------------------------------------------------------
-# box scale-out (config 5): 2048 sequences sharded by LPT, strong scaling
+# box scale-out (config 5) and the disaggregated push, with a parity check
 # ---------------------------------------------------------------------------
 
+BOX_APPENDS = 128
+NVLINK_NOMINAL_GBS = 900.0  # per direction per GPU (NVLink 5), the disaggregated mode's roofline
+NVLINK_POOL_PEER_COPY_GBS = 770.0  # copy-engine peer copy per direction measured on these B200s
 
-def run_box(args, world: int, rank: int, local: int) -> dict | None:
-    """Each rank: prefill scatter of its LPT shard + 128 decode appends; total work fixed."""
+
+def box_sequence_kv(index: int, n: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """K and V [layers, n, heads, dim] of box sequence `index`: N(0,1) bf16 from a per-sequence
+    seed, so a sequence holds the same values on whichever rank (and GPU) generates it."""
+    g = torch.Generator(device=device)
+    g.manual_seed(50_000 + int(index))
+    k = torch.randn(L, int(n), H, D, generator=g, device=device, dtype=torch.bfloat16)
+    v = torch.randn(L, int(n), H, D, generator=g, device=device, dtype=torch.bfloat16)
+    return k, v
+
+
+def oracle_check_sequences(pool, samples: list[dict]) -> tuple[bool, int]:
+    """Parity check, outside every timed region: the oracle's scatter (the reference's
+    write_paged_kv, augur/paged_kv_cache.py:188-192, restated in C) of each sampled
+    sequence's prefill tokens and appended tokens, through the same slots, into a
+    0xFF-poisoned host pool of just those sequences' blocks, against the device pool's
+    copies of the same blocks, bit for bit (the device pool was poisoned the same way,
+    so untouched rows compare too). Returns (equal, tokens checked)."""
+    from oracle import kv_oracle
+
+    ids = np.concatenate([np.asarray(x["ids"], dtype=np.int64) for x in samples])
+    if np.unique(ids).size != ids.size:
+        raise RuntimeError("sampled sequences share blocks")
+    compact = np.full(int(ids.max()) + 1, -1, dtype=np.int64)
+    compact[ids] = np.arange(ids.size)
+
+    def remap(slots: np.ndarray) -> np.ndarray:
+        return compact[slots // BS] * BS + slots % BS
+
+    hk = kv_oracle.poison_(torch.empty(L, ids.size, H, BS, D, dtype=torch.bfloat16))
+    hv = kv_oracle.poison_(torch.empty_like(hk))
+    tokens = 0
+    for x in samples:
+        kv_oracle.scatter_slots(x["k"], x["v"], remap(x["pre"]), hk, hv, BS)
+        kv_oracle.scatter_slots(x["ak"], x["av"], remap(x["app"]), hk, hv, BS)
+        tokens += x["pre"].size + x["app"].size
+    idx = torch.from_numpy(ids).to(pool.keys.device)
+    dk = pool.keys.index_select(1, idx).cpu()
+    dv = pool.values.index_select(1, idx).cpu()
+    ok = torch.equal(kv_oracle.bits(dk), kv_oracle.bits(hk)) and torch.equal(kv_oracle.bits(dv), kv_oracle.bits(hv))
+    return bool(ok), tokens
+
+
+def _sample_local(lens: np.ndarray, rank: int, n: int = 8) -> list[int]:
+    """Seeded sample of local sequence indices: n at random plus the longest."""
+    rng = np.random.default_rng(777 + rank)
+    pick = set(rng.choice(len(lens), size=min(n, len(lens)), replace=False).tolist())
+    pick.add(int(np.argmax(lens)))
+    return sorted(pick)
+
+
+def _append_inputs(n_seqs: int, seed: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    nk = torch.randn(BOX_APPENDS, L, n_seqs, H, D, generator=g, device=device, dtype=torch.bfloat16)
+    nv = torch.randn(BOX_APPENDS, L, n_seqs, H, D, generator=g, device=device, dtype=torch.bfloat16)
+    return nk, nv
+
+
+def _time_graph(graph, reps: int, device) -> float:
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        graph.replay()
+    b.record()
+    torch.cuda.synchronize(device)
+    return a.elapsed_time(b) / reps
+
+
+def _gather(obj, world: int):
+    if world == 1:
+        return [obj]
+    import torch.distributed as dist
+
+    out: list = [None] * world
+    dist.all_gather_object(out, obj)
+    return out
+
+
+def box_phase(world: int, rank: int, local: int, steps: int = 10, warmup: int = 3,
+              n_seqs: int = 2048) -> dict | None:
+    """Config 5 on `world` GPUs: 2,048 lognormal sequences LPT-sharded by tokens, each rank with
+    its own pool sized to its shard plus 128 appends; step = prefill scatter of the shard +
+    128 decode appends, captured in one CUDA graph (129 launches). Total work is fixed
+    (strong scaling). Every rank checks a seeded sample of its sequences against the oracle."""
     import augur_b200 as ab
     from augur_b200 import _lib, _ops, batched, sharding
 
     device = torch.device("cuda", local)
-    lens_all = sharding.box_lengths(n_seqs=args.box_seqs)
+    lens_all = sharding.box_lengths(n_seqs=n_seqs)
     mine = sharding.lpt_assign(lens_all, world)[rank]
     lens = lens_all[mine]
-    appends = 128
-    nblk = int(sum(-(-(int(n) + appends) // BS) for n in lens))
+    B, T = len(lens), int(lens.sum())
+    nblk = int(sum(-(-(int(n) + BOX_APPENDS) // BS) for n in lens))
     pool = ab.PagedKVCache(keys=torch.empty(L, nblk, H, BS, D, dtype=torch.bfloat16, device=device),
                            values=torch.empty(L, nblk, H, BS, D, dtype=torch.bfloat16, device=device),
                            block_size=BS, allocator=ab.BlockAllocator(nblk))
-    T = int(lens.sum())
-    # per-sequence seeds: sequence i carries the same K/V whatever the number of ranks
+    pool.keys.view(torch.uint8).fill_(0xFF)  # poison: rows nothing writes compare in the parity check
+    pool.values.view(torch.uint8).fill_(0xFF)
     k = torch.empty(L, T, H, D, dtype=torch.bfloat16, device=device)
     v = torch.empty_like(k)
-    g = torch.Generator(device=device)
-    pos = 0
-    for i, n in zip(mine, lens):
-        g.manual_seed(50_000 + int(i))
-        k[:, pos : pos + n].copy_(torch.randn(L, int(n), H, D, generator=g, device=device))
-        v[:, pos : pos + n].copy_(torch.randn(L, int(n), H, D, generator=g, device=device))
-        pos += int(n)
+    offs = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+    for j, (i, n) in enumerate(zip(mine, lens)):
+        sk, sv = box_sequence_kv(i, n, device)
+        k[:, offs[j] : offs[j + 1]].copy_(sk)
+        v[:, offs[j] : offs[j + 1]].copy_(sv)
+    del sk, sv
+    nk, nv = _append_inputs(B, 60_000 + rank, device)
     tables = [ab.SequenceBlockTable.empty(BS) for _ in lens]
     sm = batched.prefill_slot_mapping(tables, lens, pool.allocator)
-    flat = torch.from_numpy(np.concatenate([sm[b, :n] for b, n in enumerate(lens)])).to(device)
-    dec_slots = torch.from_numpy(np.stack([batched.decode_slot_mapping(tables, pool.allocator)
-                                           for _ in range(appends)])).to(device)
-    nk = torch.randn(appends, L, len(lens), H, D, device=device).to(torch.bfloat16)
+    pre = [sm[b, : int(n)].copy() for b, n in enumerate(lens)]
+    flat = torch.from_numpy(np.concatenate(pre)).to(device)
+    del sm
+    dec_np = np.stack([batched.decode_slot_mapping(tables, pool.allocator) for _ in range(BOX_APPENDS)])
+    dec = torch.from_numpy(dec_np).to(device)
 
-    def step() -> None:
+    def scatter() -> None:
         batched.write_paged_kv_batch(pool, k, v, flat)
-        for s in range(appends):
-            batched.append_decode(pool, None, nk[s], nk[s], slot_mapping=dec_slots[s])
 
-    for _ in range(max(1, args.warmup)):
-        step()
+    def appends() -> None:
+        for s in range(BOX_APPENDS):
+            batched.append_decode(pool, None, nk[s], nv[s], slot_mapping=dec[s])
+
+    scatter()
+    appends()
+    torch.cuda.synchronize(device)
+    cs = torch.cuda.Stream(device)
+    cs.wait_stream(torch.cuda.current_stream(device))
+    graphs = {}
+    for name, fns in (("step", (scatter, appends)), ("scatter", (scatter,)), ("appends", (appends,))):
+        gr = torch.cuda.CUDAGraph()
+        n0 = _ops.launch_count
+        with torch.cuda.graph(gr, stream=cs):
+            for fn in fns:
+                fn()
+        graphs[name] = (gr, _ops.launch_count - n0)
+    for _ in range(warmup):
+        graphs["step"][0].replay()
     torch.cuda.synchronize(device)
     barrier(world, device)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    launches0 = _ops.launch_count
     with ClockSampler(local) as clocks:
-        a.record()
-        for _ in range(args.steps):
-            step()
-        b.record()
-        torch.cuda.synchronize(device)
-    ms = a.elapsed_time(b)
-    launches = _ops.launch_count - launches0
+        ms_step = _time_graph(graphs["step"][0], steps, device)
+    barrier(world, device)
+    ms_scatter = _time_graph(graphs["scatter"][0], steps, device)
+    ms_app = _time_graph(graphs["appends"][0], steps, device)
     if _ops.read_status(device) != _lib.OK:
         raise RuntimeError("device status error in the box workload")
-    barrier(world, device)
-    ms_max = max_over_ranks(ms, world, device)
-    total_tokens = int(lens_all.sum())
-    step_bytes_total = scatter_bytes(total_tokens) + appends * scatter_bytes(args.box_seqs)
+    for gr, _ in graphs.values():
+        gr.reset()
+    # parity: a seeded sample of this rank's sequences against the oracle
+    samples = []
+    for b in _sample_local(lens, rank):
+        sl = slice(int(offs[b]), int(offs[b + 1]))
+        samples.append({"ids": list(tables[b].block_ids), "k": k[:, sl].cpu(), "v": v[:, sl].cpu(),
+                        "pre": pre[b], "ak": nk[:, :, b].permute(1, 0, 2, 3).contiguous().cpu(),
+                        "av": nv[:, :, b].permute(1, 0, 2, 3).contiguous().cpu(), "app": dec_np[:, b].copy()})
+    ok, checked = oracle_check_sequences(pool, samples)
+    bytes_rank = scatter_bytes(T) + BOX_APPENDS * scatter_bytes(B)
+    mine_out = {"rank": rank, "seqs": B, "tokens": T, "ms_step": ms_step, "ms_scatter": ms_scatter,
+                "ms_appends": ms_app, "bytes": bytes_rank, "bit_exact": ok, "checked_seqs": len(samples),
+                "checked_tokens": checked}
+    del k, v, nk, nv, pool, flat, dec, samples
+    torch.cuda.empty_cache()
+    reports = _gather(mine_out, world)
     if rank != 0:
         return None
     peak, peak_kind = load_peaks()
-    per_gpu = step_bytes_total / world / (ms_max / args.steps / 1e3) / 1e9
+    job_ms = max(r["ms_step"] for r in reports)
+    total_bytes = sum(r["bytes"] for r in reports)
+    scatter_job_ms = max(r["ms_scatter"] for r in reports)
+    per_rank = [{"rank": r["rank"], "seqs": r["seqs"], "tokens": r["tokens"],
+                 "ms_step": round(r["ms_step"], 4), "ms_scatter": round(r["ms_scatter"], 4),
+                 "ms_appends": round(r["ms_appends"], 4),
+                 "GBps": round(r["bytes"] / (r["ms_step"] / 1e3) / 1e9, 1),
+                 "frac_of_hbm_peak": round(r["bytes"] / (r["ms_step"] / 1e3) / 1e9 / peak, 4),
+                 "us_per_seq_scatter": round(r["ms_scatter"] * 1e3 / max(1, r["seqs"]), 3),
+                 "bit_exact": r["bit_exact"], "checked_seqs": r["checked_seqs"]} for r in reports]
+    tokens = [r["tokens"] for r in reports]
     return {
-        "metric": "KV prefill scatter + 128 decode appends GB/s (box scale-out)",
-        "value": round(step_bytes_total * args.steps / (ms_max / 1e3) / 1e9, 2), "unit": "GB/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (per-sequence seeds)",
-        "config": {"workload": f"{args.box_seqs} seqs, lognormal(ln 1024, 0.8) clipped [64, 8192], "
-                               f"{total_tokens} tokens, LPT-sharded over {world} GPUs; step = prefill "
-                               "scatter of every shard + 128 decode appends",
-                   "bytes_per_step": step_bytes_total, "tokens_rank0": T, "seqs_rank0": len(lens),
-                   "l2": "inputs larger than L2"},
-        "gpu_launches": launches, "clocks": clocks.summary(),
-        "roofline": {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s per GPU",
-                     "frac": round(per_gpu / peak, 4), "peak_source": f"hbm_gbs of {peak_kind}"},
+        "workload": f"config 5: {n_seqs} seqs, lognormal(ln 1024, 0.8) clipped [64, 8192], "
+                    f"{int(lens_all.sum())} tokens, LPT-sharded by tokens over {world} GPU(s), one pool "
+                    f"per GPU; step = prefill scatter of each shard + {BOX_APPENDS} decode appends "
+                    "(one CUDA graph of 129 launches per rank)",
+        "scaling": "strong", "n_gpus": world, "steps": steps, "warmup": warmup,
+        "bytes_per_step": total_bytes,
+        "aggregate_GBps": round(total_bytes / (job_ms / 1e3) / 1e9, 1),
+        "ms_per_step": round(job_ms, 4),
+        "scatter_ms_job": round(scatter_job_ms, 4),
+        "handoff_us_per_seq": round(scatter_job_ms * 1e3 / n_seqs, 4),
+        "appends_us_per_step_job": round(max(r["ms_appends"] for r in reports) * 1e3 / BOX_APPENDS, 3),
+        "token_imbalance": round(max(tokens) / (sum(tokens) / len(tokens)), 4),
+        "roofline": {"bound": "hbm", "unit": "GB/s per GPU", "peak": peak, "peak_source": f"hbm_gbs of {peak_kind}",
+                     "achieved_min_rank": min(x["GBps"] for x in per_rank),
+                     "frac_min_rank": min(x["frac_of_hbm_peak"] for x in per_rank)},
+        "bit_exact": all(r["bit_exact"] for r in reports),
+        "parity": "every rank: a seeded sample of its sequences (8 + its longest) scattered by the oracle "
+                  "(C restatement of write_paged_kv) through the same slots into a poisoned host pool, "
+                  "compared bit for bit with the device pool's blocks after the timed steps",
+        "gpu_launches_per_step": graphs["step"][1], "clocks_rank0": clocks.summary(),
+        "per_rank": per_rank,
     }
 
 
-# ---------------------------------------------------------------------------
-# disaggregated mode: prefill ranks push finished blocks to decode ranks
-# ---------------------------------------------------------------------------
-
-NVLINK_PEER_GBS = 770.0  # measured peer copy per direction on this B200 pool (900 nominal)
-
-
-def run_disagg(args, world: int, rank: int, local: int) -> dict | None:
-    """Ranks [0, N/2) prefill a config-2 batch and push its blocks to rank + N/2 over NVLink."""
+def disagg_phase(world: int, rank: int, local: int, steps: int = 5, warmup: int = 3,
+                 n_seqs: int = 2048) -> dict | None:
+    """Disaggregated config 5: ranks [0, N/2) prefill the 2,048 sequences (LPT-sharded over the
+    prefill ranks) into local staging pools and push the finished blocks to rank + N/2 over
+    NVLink (plain 16-byte peer stores; no TMA, no multicast); each decode rank then runs the
+    128 appends. Timed: the push (prefill ranks), the appends (decode ranks). Every decode rank
+    checks a seeded sample of its sequences against the oracle."""
     import torch.distributed as dist
 
     import augur_b200 as ab
-    from augur_b200 import _lib, _ops, batched, peer
+    from augur_b200 import _lib, _ops, batched, peer, sharding
 
-    if world < 2 or world % 2:
-        raise SystemExit("--workload disagg needs an even number of ranks >= 2")
     device = torch.device("cuda", local)
     half = world // 2
     prefill = rank < half
+    pair = rank % half
     partner = rank + half if prefill else rank - half
-    nblocks = 8192
-    pool = ab.PagedKVCache(keys=torch.empty(L, nblocks, H, BS, D, dtype=torch.bfloat16, device=device),
-                           values=torch.empty(L, nblocks, H, BS, D, dtype=torch.bfloat16, device=device),
-                           block_size=BS, allocator=ab.BlockAllocator(nblocks))
-    pair_seed = 7000 + min(rank, partner)
-    lens = config2_lengths(pair_seed)
-    # decode side: destination tables from its own allocator; exported with the pool
-    objs: list = [None] * world
-    mine = None
-    if not prefill:
-        pool.allocator.allocate_many(17)  # the decode pool already serves other sequences
-        dst_tables = [ab.SequenceBlockTable.empty(BS) for _ in lens]
-        batched.prefill_slot_mapping(dst_tables, lens, pool.allocator)
-        mine = (peer.export_pool(pool), [t.block_ids for t in dst_tables])
-    dist.all_gather_object(objs, mine)
-    n_sets = 4
+    lens_all = sharding.box_lengths(n_seqs=n_seqs)
+    mine = sharding.lpt_assign(lens_all, half)[pair]
+    lens = lens_all[mine]
+    B, T = len(lens), int(lens.sum())
+    payload = T * TOKEN_BYTES
+    mine_out: dict = {"rank": rank, "role": "prefill" if prefill else "decode", "seqs": B, "tokens": T}
+    exported = None
     if prefill:
-        exported, dst_ids = objs[partner]
-        remote = peer.open_pool(exported, device)
-        runs_sets, offset = [], 0
-        for s in range(n_sets):
-            _, slots, k, v, used = config2_batch(seed=pair_seed, block_offset=offset, num_blocks=nblocks)
-            batched.write_paged_kv_batch(pool, k.to(device), v.to(device), torch.from_numpy(slots).to(device))
-            runs, pos = [], 0
-            for n, ids in zip(lens, dst_ids):
-                for j in range(-(-int(n) // BS)):
-                    rows = min(BS, int(n) - j * BS)
-                    runs.append((int(slots[pos + j * BS]) // BS, 0, ids[j], 0, rows))
-                pos += int(n)
-            runs_sets.append(np.asarray(runs, dtype=np.int64))
-            offset += used
-        payload = int(lens.sum()) * TOKEN_BYTES
-        for i in range(max(3, args.warmup)):
-            peer.push_runs(pool, remote, runs_sets[i % n_sets])
+        nblk = int(sum(-(-int(n) // BS) for n in lens))
+        pool = ab.PagedKVCache(keys=torch.empty(L, nblk, H, BS, D, dtype=torch.bfloat16, device=device),
+                               values=torch.empty(L, nblk, H, BS, D, dtype=torch.bfloat16, device=device),
+                               block_size=BS, allocator=ab.BlockAllocator(nblk))
+        k = torch.empty(L, T, H, D, dtype=torch.bfloat16, device=device)
+        v = torch.empty_like(k)
+        offs = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+        for j, (i, n) in enumerate(zip(mine, lens)):
+            sk, sv = box_sequence_kv(i, n, device)
+            k[:, offs[j] : offs[j + 1]].copy_(sk)
+            v[:, offs[j] : offs[j + 1]].copy_(sv)
+        del sk, sv
+        tables = [ab.SequenceBlockTable.empty(BS) for _ in lens]
+        sm = batched.prefill_slot_mapping(tables, lens, pool.allocator)
+        flat = torch.from_numpy(np.concatenate([sm[b, : int(n)] for b, n in enumerate(lens)])).to(device)
+        del sm
+        batched.write_paged_kv_batch(pool, k, v, flat)  # the staging pool the push reads
         torch.cuda.synchronize(device)
-    barrier(world, device)
-    ms = 0.0
-    if prefill:
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        for i in range(args.steps):
-            peer.push_runs(pool, remote, runs_sets[i % n_sets])
+        batched.write_paged_kv_batch(pool, k, v, flat)
         b.record()
         torch.cuda.synchronize(device)
-        ms = a.elapsed_time(b)
-        if _ops.read_status(device) != _lib.OK:
-            raise RuntimeError("device status error during the push")
-    barrier(world, device)
-    ms_max = max_over_ranks(ms, world, device)
-    # decode side: the pushed blocks must equal a local write of the pair's batch
-    # (the rotating source sets hold the same seeded K/V in different blocks)
-    ok = 1.0
-    if not prefill:
-        _, _, k, v, _ = config2_batch(seed=pair_seed, block_offset=0, num_blocks=nblocks)
-        ref = ab.PagedKVCache(keys=torch.zeros_like(pool.keys), values=torch.zeros_like(pool.values),
-                              block_size=BS, allocator=ab.BlockAllocator(nblocks))
-        tables = [ab.SequenceBlockTable(block_ids=list(ids), block_size=BS, seq_len=int(n))
-                  for ids, n in zip(mine[1], lens)]
-        pos = [np.arange(int(n)) for n in lens]
-        flat = np.concatenate([np.asarray(t.block_ids)[p // BS] * BS + p % BS for t, p in zip(tables, pos)])
-        batched.write_paged_kv_batch(ref, k.to(device), v.to(device), torch.from_numpy(flat).to(device))
-        gk, gv = batched.read_paged_kv_batch(pool, tables)
-        rk, rv = batched.read_paged_kv_batch(ref, tables)
-        ok = float(torch.equal(gk.view(torch.int16), rk.view(torch.int16)) and
-                   torch.equal(gv.view(torch.int16), rv.view(torch.int16)))
-        del ref
-    t = torch.tensor([ok], dtype=torch.float64, device=device)
-    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        mine_out["ms_prefill_scatter"] = a.elapsed_time(b)
+        del k, v, flat
+    else:
+        spare = 17  # the decode pool already serves other sequences: destination ids differ from the source's
+        nblk = int(sum(-(-(int(n) + BOX_APPENDS) // BS) for n in lens)) + spare
+        pool = ab.PagedKVCache(keys=torch.empty(L, nblk, H, BS, D, dtype=torch.bfloat16, device=device),
+                               values=torch.empty(L, nblk, H, BS, D, dtype=torch.bfloat16, device=device),
+                               block_size=BS, allocator=ab.BlockAllocator(nblk))
+        pool.keys.view(torch.uint8).fill_(0xFF)
+        pool.values.view(torch.uint8).fill_(0xFF)
+        pool.allocator.allocate_many(spare)
+        tables = [ab.SequenceBlockTable.empty(BS) for _ in lens]
+        sm = batched.prefill_slot_mapping(tables, lens, pool.allocator)
+        pre = [sm[b, : int(n)].copy() for b, n in enumerate(lens)]
+        del sm
+        torch.cuda.synchronize(device)
+        exported = (peer.export_pool(pool), [list(t.block_ids) for t in tables])
+    objs: list = [None] * world
+    dist.all_gather_object(objs, exported)
+    if prefill:
+        ex, dst_ids = objs[partner]
+        remote = peer.open_pool(ex, device)
+        runs = []
+        for t, ids, n in zip(tables, dst_ids, lens):
+            nb = -(-int(n) // BS)
+            r = np.zeros((nb, 5), dtype=np.int64)
+            r[:, 0] = t.block_ids[:nb]
+            r[:, 2] = ids[:nb]
+            r[:, 4] = np.minimum(BS, int(n) - BS * np.arange(nb))
+            runs.append(r)
+        prep = peer.prepare_push(pool, remote, np.concatenate(runs))
+        assert prep.payload_bytes == payload
+        for _ in range(warmup):
+            peer.push_prepared(prep)
+        torch.cuda.synchronize(device)
     barrier(world, device)
     if prefill:
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clocks:
+            a.record()
+            for _ in range(steps):
+                peer.push_prepared(prep)
+            b.record()
+            torch.cuda.synchronize(device)
+        mine_out["ms_push"] = a.elapsed_time(b) / steps
+        mine_out["clocks"] = clocks.summary()
+        mine_out["launches"] = steps
+        if _ops.read_status(device) != _lib.OK:
+            raise RuntimeError("device status error during the push")
+    barrier(world, device)  # every push has landed before any decode rank appends
+    if prefill:
         remote.close()
-    barrier(world, device)
+        del prep
+    else:
+        nk, nv = _append_inputs(B, 70_000 + rank, device)
+        dec_np = np.stack([batched.decode_slot_mapping(tables, pool.allocator) for _ in range(BOX_APPENDS)])
+        dec = torch.from_numpy(dec_np).to(device)
+        gr = torch.cuda.CUDAGraph()
+        cs = torch.cuda.Stream(device)
+        cs.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.graph(gr, stream=cs):
+            for s in range(BOX_APPENDS):
+                batched.append_decode(pool, None, nk[s], nv[s], slot_mapping=dec[s])
+        mine_out["ms_appends"] = _time_graph(gr, steps, device)
+        gr.reset()
+        if _ops.read_status(device) != _lib.OK:
+            raise RuntimeError("device status error in the decode appends")
+        samples = []
+        for b in _sample_local(lens, rank):
+            sk, sv = box_sequence_kv(mine[b], lens[b], device)  # the prefill rank's values, by seed
+            samples.append({"ids": list(tables[b].block_ids), "k": sk.cpu(), "v": sv.cpu(), "pre": pre[b],
+                            "ak": nk[:, :, b].permute(1, 0, 2, 3).contiguous().cpu(),
+                            "av": nv[:, :, b].permute(1, 0, 2, 3).contiguous().cpu(),
+                            "app": dec_np[:, b].copy()})
+        ok, checked = oracle_check_sequences(pool, samples)
+        mine_out.update(bit_exact=ok, checked_seqs=len(samples), checked_tokens=checked)
+        del nk, nv, dec, samples
+    barrier(world, device)  # the prefill ranks have closed their mappings of the decode pools
+    del pool
+    torch.cuda.empty_cache()
+    reports = _gather(mine_out, world)
     if rank != 0:
         return None
-    per_pair = payload * args.steps / (ms_max / 1e3) / 1e9
+    pre_r = [r for r in reports if r["role"] == "prefill"]
+    dec_r = [r for r in reports if r["role"] == "decode"]
+    push_ms = max(r["ms_push"] for r in pre_r)
+    total_payload = sum(r["tokens"] for r in pre_r) * TOKEN_BYTES
+    per_pair = [{"pair": f"{r['rank']}->{r['rank'] + half}", "seqs": r["seqs"], "tokens": r["tokens"],
+                 "ms_push": round(r["ms_push"], 4),
+                 "GBps": round(r["tokens"] * TOKEN_BYTES / (r["ms_push"] / 1e3) / 1e9, 1),
+                 "us_per_seq": round(r["ms_push"] * 1e3 / max(1, r["seqs"]), 3),
+                 "ms_prefill_scatter": round(r["ms_prefill_scatter"], 4)} for r in pre_r]
+    worst = min(p["GBps"] for p in per_pair)
     return {
-        "metric": "KV block push GB/s over NVLink (disaggregated prefill -> decode)",
-        "value": round(per_pair * half, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"{half} prefill->decode pairs, each pushing a config-2 batch "
-                               "(8192 tokens x 24 layers, whole 16-token blocks) per step",
-                   "payload_bytes_per_pair_step": payload, "bit_exact_on_decode": bool(t.item() == 1.0),
-                   "l2": "4 rotating source batches per prefill rank"},
-        "roofline": {"bound": "nvlink", "achieved": round(per_pair, 1), "peak": NVLINK_PEER_GBS,
-                     "unit": "GB/s per direction per GPU", "frac": round(per_pair / NVLINK_PEER_GBS, 4),
-                     "peak_source": "measured peer copy on this pool (900 nominal)"},
+        "workload": f"config 5 disaggregated: {n_seqs} seqs ({int(lens_all.sum())} tokens) LPT-sharded over "
+                    f"{half} prefill GPU(s); each prefill GPU i pushes its finished blocks (every layer, K and "
+                    f"V, partial last blocks by their rows) into decode GPU i + {half}'s pool, which then runs "
+                    f"{BOX_APPENDS} appends",
+        "n_gpus": world, "pairs": half, "steps": steps, "warmup": warmup,
+        "payload_bytes_per_push": total_payload,
+        "aggregate_push_GBps": round(total_payload / (push_ms / 1e3) / 1e9, 1),
+        "ms_per_push_job": round(push_ms, 4),
+        "handoff_us_per_seq": round(push_ms * 1e3 / n_seqs, 4),
+        "roofline": {"bound": "nvlink", "unit": "GB/s per direction per GPU", "achieved_min_pair": worst,
+                     "peak": NVLINK_NOMINAL_GBS, "frac_min_pair": round(worst / NVLINK_NOMINAL_GBS, 4),
+                     "peak_source": "NVLink 5 nominal per direction (900 GB/s)",
+                     "frac_of_pool_peer_copy": round(worst / NVLINK_POOL_PEER_COPY_GBS, 4),
+                     "pool_peer_copy_GBps": NVLINK_POOL_PEER_COPY_GBS},
+        "appends_us_per_step_job": round(max(r["ms_appends"] for r in dec_r) * 1e3 / BOX_APPENDS, 3),
+        "bit_exact": all(r["bit_exact"] for r in dec_r),
+        "parity": "every decode rank: a seeded sample of its sequences (8 + its longest) regenerated from "
+                  "their seeds and scattered by the oracle, with the appends, into a poisoned host pool, "
+                  "compared bit for bit with the decode pool's blocks after the pushes and appends",
+        "clocks_rank0": reports[0].get("clocks"),
+        "per_pair": per_pair,
     }
+
+
+def run_phase(args, world: int, rank: int, local: int) -> dict | None:
+    """--workload box | disagg alone: the phase's result as the line's body."""
+    torch.cuda.set_device(local)
+    if args.workload == "box":
+        out = box_phase(world, rank, local, steps=args.steps, warmup=args.warmup, n_seqs=args.box_seqs)
+    else:
+        if world < 2 or world % 2:
+            raise SystemExit("--workload disagg needs an even number of ranks >= 2")
+        out = disagg_phase(world, rank, local, steps=args.steps, warmup=args.warmup, n_seqs=args.box_seqs)
+    if out is None:
+        return None
+    return {"metric": METRIC, "workload": args.workload, "n_gpus": world, "data": "synthetic", **out}
 
 
 # ---------------------------------------------------------------------------
@@ -1145,6 +1365,8 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-extras", action="store_true")
+    ap.add_argument("--skip-scaleout", action="store_true",
+                    help="leave out config 5 (box, strong scaling) and the disaggregated push")
     ap.add_argument("--small", action="store_true", help="profiling case: 8192-block pool, no extras/CPU")
     ap.add_argument("--handoff-only", action="store_true", help="profiling case: config-3 handoff only")
     ap.add_argument("--attention-only", action="store_true",
@@ -1163,9 +1385,9 @@ def main() -> None:
     if args.warmup < 3:
         args.warmup = 3
     if args.steps is None:  # each default keeps its timed region well under a minute
-        args.steps = 2000 if args.impl == "reference" else {"scatter": 20000, "box": 20, "disagg": 50}[args.workload]
+        args.steps = 2000 if args.impl == "reference" else {"scatter": 20000, "box": 10, "disagg": 5}[args.workload]
     if args.small:
-        args.skip_cpu = args.skip_extras = True
+        args.skip_cpu = args.skip_extras = args.skip_scaleout = True
     if args.handoff_only:  # profiling case: only the config-3 handoff (about 3 GB on the device)
         torch.cuda.set_device(0)
         emit(run_extras(torch.device("cuda", 0), handoff_only=True))
@@ -1201,10 +1423,8 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     try:
-        if args.workload == "disagg":
-            line = run_disagg(args, world, rank, local)
-        elif args.workload == "box":
-            line = run_box(args, world, rank, local)
+        if args.workload in ("disagg", "box"):
+            line = run_phase(args, world, rank, local)
         else:
             line = run_ours(args, world, rank, local)
         if line is not None:
