@@ -284,3 +284,23 @@ def host_index_ok(n_tokens: int, src: Tensor, dst: Tensor) -> bool:
 def max_rows_for(head_dim: int, elem_size: int, cap_rows: int = 64, cap_bytes: int = 8192) -> int:
     """Largest run length (rows) to cut copies into: at most cap_rows rows and cap_bytes bytes."""
     return max(1, min(cap_rows, cap_bytes // max(1, head_dim * elem_size)))
+
+
+def keep_last(index: np.ndarray) -> np.ndarray:
+    """``index`` with every earlier occurrence of a repeated value replaced by -1.
+
+    The kernels write tokens in parallel and skip a negative index, so this
+    gives duplicate destinations in one call the reference's result: its
+    per-token loop (paged_kv_cache.py:188-192) writes them in order and the
+    last one stays. An index without repeats is returned as is.
+    """
+    n = int(index.shape[0])
+    if n < 2:
+        return index
+    uniq, first_in_reversed = np.unique(index[::-1], return_index=True)
+    if uniq.size == n:
+        return index
+    last = n - 1 - first_in_reversed
+    out = np.full(n, -1, dtype=np.int64)
+    out[last] = index[last]
+    return out

@@ -93,6 +93,26 @@ def _dtype_name(dtype: torch.dtype) -> str:
     return _DTYPE_NAMES.get(dtype, str(dtype).replace("torch.", ""))
 
 
+def position_range(position_ids: Tensor) -> tuple[int, int, bool]:
+    """(max, min, whether a batch row repeats a position) of ``[batch, seq]`` positions, with
+    one host read of a device tensor (the reference reads max and min with two)."""
+    seq = position_ids.shape[1]
+    parts = [position_ids.max(), position_ids.min()]
+    if seq > 1:
+        srt = position_ids.sort(dim=1).values
+        parts.append((srt[:, 1:] == srt[:, :-1]).any())
+    vals = torch.stack([x.to(torch.int64) for x in parts]).tolist()
+    return vals[0], vals[1], bool(vals[2]) if seq > 1 else False
+
+
+def keep_last_per_row(position_ids: Tensor) -> Tensor:
+    """Host int64 copy of ``[batch, seq]`` positions with every earlier repeat of a position
+    within a row set to -1, so the last token written to a position is the one that stays
+    (a negative index skips its token)."""
+    rows = position_ids.detach().to("cpu", torch.int64).numpy()
+    return torch.from_numpy(np.stack([_ops.keep_last(r) for r in rows]).astype(np.int64))
+
+
 def _head_dim_contiguous(t: Tensor) -> Tensor:
     return t if t.stride(-1) == 1 else t.contiguous()
 
@@ -128,8 +148,7 @@ def write_kv(
         raise ValueError("key/value tensors must be on the same device as the cache")
     _ops.require_cuda("write_kv", cache.keys, cache.values)
 
-    max_position = int(position_ids.max().item())
-    min_position = int(position_ids.min().item())
+    max_position, min_position, repeats = position_range(position_ids)
     if min_position < 0:
         raise ValueError("cache positions must be non-negative")
     if max_position >= cache.max_seq_len:
@@ -142,7 +161,7 @@ def write_kv(
                 f"{_dtype_name(dst.dtype)} for the destination and {_dtype_name(src.dtype)} for the source."
             )
 
-    scatter_rows(cache, layer_idx, position_ids, key, value)
+    scatter_rows(cache, layer_idx, keep_last_per_row(position_ids) if repeats else position_ids, key, value)
 
     cache.seq_len = max(cache.seq_len, max_position + 1)
     return (

@@ -23,6 +23,7 @@ import torch
 from torch import Tensor
 
 from . import _ops
+from ._ops import keep_last
 from .config import QwenConfig
 
 
@@ -320,7 +321,8 @@ def write_paged_kv(
     Same checks, messages, lazy block allocation and partial-write-on-error
     behaviour as augur's write_paged_kv (paged_kv_cache.py:167-192); the data
     moves in one augur_kv_scatter launch. Reading position_ids is a host sync
-    when it lives on the GPU, as in the reference (.tolist()).
+    when it lives on the GPU, as in the reference (.tolist()). A position given
+    twice keeps the later token's K/V, as the reference's loop does.
     """
     if key.shape != value.shape:
         raise ValueError("key and value must have the same shape")
@@ -341,7 +343,7 @@ def write_paged_kv(
     if n_ok:
         if block_table.block_size > cache.keys.shape[3]:
             raise IndexError("block table block_size exceeds the cache block size")
-        slots = slots_for_positions(block_table, positions[:n_ok])
+        slots = keep_last(slots_for_positions(block_table, positions[:n_ok]))
         if not (_ops.host_index_ok(n_ok, key, cache.keys) and key.dtype == value.dtype):
             slots = torch.from_numpy(slots).to(device=cache.keys.device)
         scatter_slots_one_layer(cache, layer_idx, key[0], value[0], slots, block_table.block_size)

@@ -24,8 +24,8 @@ import torch
 from torch import Tensor
 
 from . import _lib, _ops
-from .kv_cache import KVCache
-from .paged_kv_cache import PagedKVCache, SequenceBlockTable, ensure_positions, slots_for_positions
+from .kv_cache import KVCache, keep_last_per_row, position_range
+from .paged_kv_cache import PagedKVCache, SequenceBlockTable, ensure_positions, keep_last, slots_for_positions
 
 _tables: dict[tuple, tuple[Tensor, Tensor]] = {}
 
@@ -170,7 +170,7 @@ def rope_write_paged_kv(
         raise IndexError("block table block_size exceeds the cache block size")
     slots = np.full(seq, -1, dtype=np.int64)
     if n_ok:
-        slots[:n_ok] = slots_for_positions(block_table, host_pos[:n_ok])
+        slots[:n_ok] = keep_last(slots_for_positions(block_table, host_pos[:n_ok]))
     q, key, value = (_last_dim_contiguous(t.to(device)) for t in (q, key, value))
     q_out = torch.empty_like(q)
     kc, vc = cache.keys[layer_idx], cache.values[layer_idx]
@@ -223,8 +223,8 @@ def rope_write_kv(
     if key.device != cache.keys.device or value.device != cache.values.device:
         raise ValueError("key/value tensors must be on the same device as the cache")
     _ops.require_cuda("rope_write_kv", cache.keys, cache.values, q)
-    max_position = int(position_ids.max().item())
-    if int(position_ids.min().item()) < 0:
+    max_position, min_position, repeats = position_range(position_ids)
+    if min_position < 0:
         raise ValueError("cache positions must be non-negative")
     if max_position >= cache.max_seq_len:
         raise ValueError("position_ids exceeds cache capacity")
@@ -236,6 +236,8 @@ def rope_write_kv(
     q, key, value = (_last_dim_contiguous(t) for t in (q, key, value))
     q_out = torch.empty_like(q)
     pos = _positions_i64(position_ids, device)
+    # a repeated position keeps the later token (write_kv's rule); every q is still rotated
+    idx = _positions_i64(keep_last_per_row(position_ids), device) if repeats else pos
     kc, vc = cache.keys[layer_idx], cache.values[layer_idx]
     if seq and batch:
         rope_scatter(
@@ -245,7 +247,7 @@ def rope_write_kv(
             value_strides=(0, value.stride(0), value.stride(2), value.stride(1)), tokens_per_row=seq,
             dst_k=kc, dst_v=vc, dst_strides=(0, kc.stride(0), kc.stride(2), kc.stride(1)),
             rows_per_major=kc.shape[2], num_majors=kc.shape[0],
-            index=pos, index_strides=(pos.stride(0), pos.stride(1)), index_row_base=kc.shape[2],
+            index=idx, index_strides=(idx.stride(0), idx.stride(1)), index_row_base=kc.shape[2],
             positions=pos, position_strides=(pos.stride(0), pos.stride(1)),
             rope_theta=rope_theta, max_position=max_position, n_tokens=batch * seq, n_layers=1,
             n_heads=num_heads, head_dim=head_dim)

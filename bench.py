@@ -661,6 +661,31 @@ def bench_decode_step(device, pool, tables) -> dict:
         times.append(a.elapsed_time(b))
     graph.reset()
     dev_ms = statistics.median(times[2:])
+    # the same step's attention alone (same tables and lengths, q already rotated): the
+    # difference is what the RoPE append costs inside the fused launch
+    from augur_b200.attention import paged_decode_attention
+
+    qr = q[:, :, :, 0].contiguous()
+    outs = torch.empty_like(qr)
+    agraph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(cs):
+        for layer in range(L):
+            paged_decode_attention(qr[layer], pool, layer, step.tables, out=outs[layer])
+    torch.cuda.synchronize(device)
+    with torch.cuda.graph(agraph, stream=cs):
+        for layer in range(L):
+            paged_decode_attention(qr[layer], pool, layer, step.tables, out=outs[layer])
+    atimes = []
+    for _ in range(7):
+        flush.fill_(1)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        agraph.replay()
+        b.record()
+        torch.cuda.synchronize(device)
+        atimes.append(a.elapsed_time(b))
+    agraph.reset()
+    att_ms = statistics.median(atimes[2:])
     host = []
     for _ in range(5):  # real steps: every table grows by one token per step
         torch.cuda.synchronize(device)
@@ -693,6 +718,8 @@ def bench_decode_step(device, pool, tables) -> dict:
     tokens = int(sum(t.seq_len for t in tabs))
     return {"seqs": B, "cached_tokens_after": tokens, "launches_per_step": launches_per_step,
             "us_per_step_device": round(dev_ms * 1e3, 1), "us_per_layer_device": round(dev_ms * 1e3 / L, 2),
+            "us_per_layer_attention_alone": round(att_ms * 1e3 / L, 2),
+            "append_in_fused_us_per_layer": round((dev_ms - att_ms) * 1e3 / L, 2),
             "us_per_step_with_host": round(statistics.median(host) * 1e6, 1),
             "us_per_step_graph_with_host": round(statistics.median(replay) * 1e6, 1),
             "timed": "per layer: decode attention with the RoPE append fused into it; device: CUDA graph, L2 flushed; "
@@ -782,6 +809,50 @@ def bench_offload(device, pool, tables, n_seqs: int = 16) -> dict:
     return out
 
 
+def bench_cow_device(device, pool, parent, forks, prefix_len: int, flush) -> dict:
+    """The copy-on-write launch alone: the parent's partial block copied into every fork's
+    private block (all layers, K and V), replayed from a CUDA graph with L2 flushed before
+    each replay. Algorithmic bytes: every copied row read once and written once (the
+    copies all read the same source block, so DRAM reads are far fewer)."""
+    from augur_b200 import batched
+
+    j, r = prefix_len // BS, prefix_len % BS
+    runs = np.zeros((len(forks), 5), dtype=np.int64)
+    runs[:, 0] = parent.block_ids[j]
+    runs[:, 2] = [f.block_ids[j] for f in forks]
+    runs[:, 4] = r
+    max_rows = batched._run_max_rows(pool.keys, BS)
+    runs_t = batched._to_device_runs(batched.split_runs(runs, max_rows), device)
+
+    def cow() -> None:
+        batched.copy_runs_between(pool.keys, pool.values, "paged", pool.keys, pool.values, "paged", runs_t,
+                                  max_rows)
+
+    cow()
+    graph = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream(device)
+    cs.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.graph(graph, stream=cs):
+        cow()
+    times = []
+    for _ in range(9):
+        flush.fill_(1)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        graph.replay()
+        b.record()
+        torch.cuda.synchronize(device)
+        times.append(a.elapsed_time(b))
+    graph.reset()
+    ms = statistics.median(times[2:])
+    nbytes = 2 * len(forks) * r * L * TOKEN_LAYER_BYTES + runs_t.numel() * 4
+    peak, kind = load_peaks()
+    gbs = nbytes / (ms / 1e3) / 1e9
+    return {"cow_us_device": round(ms * 1e3, 2), "cow_bytes": nbytes, "cow_GBps_device": round(gbs, 1),
+            "cow_frac_of_hbm_peak": round(gbs / peak, 4), "cow_kernel": "copy_runs_vec_kernel<16>",
+            "cow_timed": "CUDA graph of the one copy launch, L2 flushed before each replay"}
+
+
 def run_extras(device, handoff_only: bool = False, attention_only: bool = False, rope_only: bool = False,
                offload_only: bool = False) -> dict:
     """Config 3 handoff + decode append and config 4 fork/COW, timed with CUDA events."""
@@ -853,9 +924,12 @@ def run_extras(device, handoff_only: bool = False, attention_only: bool = False,
     torch.cuda.synchronize(device)
     ms = a.elapsed_time(b)
     abytes = scatter_bytes(B)
+    peak, _ = load_peaks()
     out["decode_append"] = {"us_per_step": round(ms * 1e3 / steps, 3), "steps": steps, "seqs": B,
                             "GBps": round(abytes * steps / (ms / 1e3) / 1e9, 1),
-                            "timed": "one CUDA graph of 256 append launches"}
+                            "frac_of_hbm_peak": round(abytes * steps / (ms / 1e3) / 1e9 / peak, 4),
+                            "hbm_floor_us": round(abytes / peak / 1e3, 3),
+                            "timed": "one CUDA graph of 256 append launches (one launch per step, all layers)"}
     graph.reset()
     del src, nk, nv
 
@@ -901,9 +975,11 @@ def run_extras(device, handoff_only: bool = False, attention_only: bool = False,
         batched.write_paged_kv_batch(pool4, sk, sk, sm_t)
         c.record()
         torch.cuda.synchronize(device)
-        out[f"prefix_fork_{prefix_len}"] = {
-            "forks": 256, "cow_blocks": copied, "cow_ms_incl_host": round(a.elapsed_time(b), 4),
-            "suffix_GBps": round(scatter_bytes(256 * 128) / (c0.elapsed_time(c) / 1e3) / 1e9, 1)}
+        entry = {"forks": 256, "cow_blocks": copied, "cow_ms_incl_host": round(a.elapsed_time(b), 4),
+                 "suffix_GBps": round(scatter_bytes(256 * 128) / (c0.elapsed_time(c) / 1e3) / 1e9, 1)}
+        if copied:
+            entry.update(bench_cow_device(device, pool4, parent, forks, prefix_len, flush))
+        out[f"prefix_fork_{prefix_len}"] = entry
         del sk, pk
     if _ops.read_status(device) != _lib.OK:
         raise RuntimeError("device status error in the extra workloads")
@@ -953,8 +1029,10 @@ def oracle_check_sequences(pool, samples: list[dict]) -> tuple[bool, int]:
     tokens = 0
     for x in samples:
         kv_oracle.scatter_slots(x["k"], x["v"], remap(x["pre"]), hk, hv, BS)
-        kv_oracle.scatter_slots(x["ak"], x["av"], remap(x["app"]), hk, hv, BS)
-        tokens += x["pre"].size + x["app"].size
+        tokens += x["pre"].size
+        if "app" in x:  # appended tokens, written after the prefill
+            kv_oracle.scatter_slots(x["ak"], x["av"], remap(x["app"]), hk, hv, BS)
+            tokens += x["app"].size
     idx = torch.from_numpy(ids).to(pool.keys.device)
     dk = pool.keys.index_select(1, idx).cpu()
     dv = pool.values.index_select(1, idx).cpu()

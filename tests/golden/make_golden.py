@@ -12,8 +12,8 @@ rows and every row that must stay untouched.
 Outputs:
   reference_cases.pt  small seeded cases of write_kv, write_paged_kv,
                       read_paged_kv, copy_prefix_into_cache, the handoff and
-                      fork compositions, allocator / block table / prefix-hash
-                      scripts;
+                      fork compositions, duplicate positions in one call,
+                      allocator / block table / prefix-hash scripts;
   config1_writes.pt   the full Qwen2.5-0.5B-shaped random-init model (fp32,
                       CPU): 128-token prefill into new_kv_cache(max_seq_len=512)
                       plus 32 greedy decode forwards, with every write_kv call
@@ -359,6 +359,40 @@ def rope_cases(ref, g):
     return cases
 
 
+def duplicate_cases(ref, g):
+    """Duplicate positions in one call: write_kv (per-row index_put) and write_paged_kv
+    (per-token loop), from poisoned caches; the reference keeps the last token written."""
+    cfg = ref.config.QwenConfig(vocab_size=16, hidden_size=16, intermediate_size=16,
+                                num_hidden_layers=2, num_attention_heads=2, num_key_value_heads=2)
+    cases = {}
+    for name, dtype in (("f32", torch.float32), ("bf16", torch.bfloat16)):
+        cache = ref.kv_cache.new_kv_cache(cfg, batch_size=3, max_seq_len=12, device=torch.device("cpu"),
+                                          dtype=dtype)
+        poison(cache.keys)
+        poison(cache.values)
+        pos = torch.tensor([[2, 4, 2, 9, 4], [0, 0, 0, 1, 0], [5, 6, 7, 5, 11]])
+        k = strided_kv(g, 3, 2, 5, 8, dtype)
+        v = strided_kv(g, 3, 2, 5, 8, dtype)
+        ref.kv_cache.write_kv(cache, 1, pos, k, v)
+        cases[f"write_kv_{name}"] = {"layer": 1, "positions": pos, "key": k.contiguous(), "value": v.contiguous(),
+                                     "keys": cache.keys.clone(), "values": cache.values.clone(),
+                                     "seq_len": cache.seq_len, "cfg": [2, 3, 2, 12, 8]}
+        pool = ref.paged_kv_cache.new_paged_kv_cache(cfg, num_blocks=6, block_size=4,
+                                                     device=torch.device("cpu"), dtype=dtype)
+        poison(pool.keys)
+        poison(pool.values)
+        table = ref.paged_kv_cache.SequenceBlockTable.empty(4)
+        ppos = torch.tensor([[3, 5, 3, 7, 5, 9, 3]])
+        pk = strided_kv(g, 1, 2, 7, 8, dtype)
+        pv = strided_kv(g, 1, 2, 7, 8, dtype)
+        ref.paged_kv_cache.write_paged_kv(pool, 0, table, ppos, pk, pv)
+        cases[f"write_paged_kv_{name}"] = {"layer": 0, "positions": ppos, "key": pk.contiguous(),
+                                           "value": pv.contiguous(), "keys": pool.keys.clone(),
+                                           "values": pool.values.clone(), "block_ids": list(table.block_ids),
+                                           "seq_len": table.seq_len, "num_blocks": 6, "block_size": 4}
+    return cases
+
+
 def bookkeeping_scripts(ref):
     P = ref.paged_kv_cache
     alloc = P.BlockAllocator(num_blocks=12)
@@ -495,6 +529,7 @@ def main() -> None:
     }
     cases["attention"] = attention_cases(Ref, torch.Generator().manual_seed(4321))
     cases["rope"] = rope_cases(Ref, torch.Generator().manual_seed(777))
+    cases["duplicates"] = duplicate_cases(Ref, torch.Generator().manual_seed(99))
     torch.save(cases, os.path.join(HERE, "reference_cases.pt"))
     if not args.skip_config1:
         torch.save(config1(Ref), os.path.join(HERE, "config1_writes.pt"))

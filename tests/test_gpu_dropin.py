@@ -266,3 +266,30 @@ def test_ref_copy_prefix(cuda):
     assert cache.seq_len == 3
     assert torch.equal(cache.keys[:, 0, :, :3, :].cpu(), entry.keys)
     assert torch.equal(cache.values[:, 0, :, :3, :].cpu(), entry.values)
+
+
+@pytest.mark.parametrize("case", ["f32", "bf16"])
+@pytest.mark.parametrize("positions_on_host", [False, True])
+def test_duplicate_positions_golden(cuda, golden, case, positions_on_host):
+    """A position repeated in one call keeps the later token, as in the reference's
+    write_kv (index_put per row) and write_paged_kv (per-token loop)."""
+    c = golden["duplicates"][f"write_kv_{case}"]
+    L, B, H, S, D = c["cfg"]
+    cache = ab.KVCache(keys=_poisoned((L, B, H, S, D), c["keys"].dtype, cuda),
+                       values=_poisoned((L, B, H, S, D), c["keys"].dtype, cuda))
+    pos = c["positions"] if positions_on_host else c["positions"].to(cuda)
+    ab.write_kv(cache, c["layer"], pos, _strided(c["key"], cuda), _strided(c["value"], cuda))
+    assert cache.seq_len == c["seq_len"]
+    assert_bits_equal(cache.keys, c["keys"], "write_kv keys")
+    assert_bits_equal(cache.values, c["values"], "write_kv values")
+    p = golden["duplicates"][f"write_paged_kv_{case}"]
+    pool = ab.PagedKVCache(keys=_poisoned(p["keys"].shape, p["keys"].dtype, cuda),
+                           values=_poisoned(p["keys"].shape, p["keys"].dtype, cuda),
+                           block_size=p["block_size"], allocator=ab.BlockAllocator(p["num_blocks"]))
+    table = ab.SequenceBlockTable.empty(p["block_size"])
+    ppos = p["positions"] if positions_on_host else p["positions"].to(cuda)
+    ab.write_paged_kv(pool, p["layer"], table, ppos, _strided(p["key"], cuda), _strided(p["value"], cuda))
+    assert table.block_ids == p["block_ids"] and table.seq_len == p["seq_len"]
+    assert_bits_equal(pool.keys, p["keys"], "write_paged_kv keys")
+    assert_bits_equal(pool.values, p["values"], "write_paged_kv values")
+    assert _ops.read_status(cuda) == _lib.OK

@@ -176,3 +176,42 @@ def test_position_outside_table_is_reported(cuda):
                               torch.tensor([3, 5000], device=cuda), 12345.0, 0, max_position=10)
     assert _ops.read_status(cuda) == _lib.EBOUNDS
     assert _is_poison(pool.keys[0, 0, :, 1]) and not _is_poison(pool.keys[0, 0, :, 0])
+
+
+@pytest.mark.parametrize("positions_on", ["device", "host"])
+def test_rope_writes_keep_the_last_duplicate(cuda, oracle, positions_on):
+    """Repeated positions in one call: every q is rotated; the cache keeps the later token
+    (apply_rope then write_kv / write_paged_kv, as the reference runs them)."""
+    g = torch.Generator().manual_seed(21)
+    B, H, Hq, S, D, M = 2, 2, 4, 6, 64, 16
+    pos = torch.tensor([[4, 1, 4, 2, 1, 9], [0, 0, 3, 3, 5, 0]])
+    q = torch.randn(B, Hq, S, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, H, S, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, H, S, D, generator=g).to(torch.bfloat16)
+    qe, ke = oracle.apply_rope(q, k, pos, THETA)
+    p_arg = pos if positions_on == "host" else pos.to(cuda)
+    # contiguous cache
+    cache = ab.KVCache(keys=poison_(torch.empty(2, B, H, M, D, dtype=torch.bfloat16, device=cuda)),
+                       values=poison_(torch.empty(2, B, H, M, D, dtype=torch.bfloat16, device=cuda)))
+    ck = poison_(torch.empty(2, B, H, M, D, dtype=torch.bfloat16))
+    cv = poison_(torch.empty(2, B, H, M, D, dtype=torch.bfloat16))
+    q_out, _, _ = rope_write_kv(cache, 1, p_arg, q.to(cuda), k.to(cuda), v.to(cuda), THETA)
+    oracle.write_kv(ck, cv, 1, pos, ke, v)
+    assert_bits_equal(q_out, qe, "rotated q")
+    assert_bits_equal(cache.keys, ck, "keys")
+    assert_bits_equal(cache.values, cv, "values")
+    # paged cache, batch 1
+    pool = ab.PagedKVCache(keys=poison_(torch.empty(1, 4, H, 4, D, dtype=torch.bfloat16, device=cuda)),
+                           values=poison_(torch.empty(1, 4, H, 4, D, dtype=torch.bfloat16, device=cuda)),
+                           block_size=4, allocator=ab.BlockAllocator(4))
+    table = ab.SequenceBlockTable.empty(4)
+    rk = poison_(torch.empty(1, 4, H, 4, D, dtype=torch.bfloat16))
+    rv = poison_(torch.empty(1, 4, H, 4, D, dtype=torch.bfloat16))
+    q_out = rope_write_paged_kv(pool, 0, table, p_arg[:1], q[:1].to(cuda), k[:1].to(cuda), v[:1].to(cuda), THETA)
+    rt = oracle.RefBlockTable([], 4)
+    oracle.write_paged_kv(rk, rv, oracle.RefBlockAllocator(4), 0, rt, pos[0].tolist(), ke[:1], v[:1])
+    assert table.block_ids == rt.block_ids
+    assert_bits_equal(q_out, qe[:1], "paged rotated q")
+    assert_bits_equal(pool.keys, rk, "paged keys")
+    assert_bits_equal(pool.values, rv, "paged values")
+    assert _ops.read_status(cuda) == _lib.OK

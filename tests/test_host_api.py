@@ -373,3 +373,23 @@ def test_decode_graph_step_refuses_a_cpu_cache():
                           block_size=16, allocator=ab.BlockAllocator(4))
     with pytest.raises(ValueError, match="needs CUDA tensors"):
         DecodeGraphStep(cpu, batch=2, max_blocks=2, n_q_heads=14, rope_theta=1e6)
+
+
+def test_keep_last_marks_earlier_repeats():
+    from augur_b200.paged_kv_cache import keep_last
+
+    x = np.array([3, 5, 3, 7, 5, 9, 3], dtype=np.int64)
+    assert keep_last(x).tolist() == [-1, -1, -1, 7, 5, 9, 3]
+    y = np.array([4, 1, 2], dtype=np.int64)
+    assert keep_last(y) is y  # no repeats: unchanged, no copy
+    assert keep_last(np.array([6], dtype=np.int64)).tolist() == [6]
+
+
+def test_position_range_reads_repeats_per_row():
+    from augur_b200.kv_cache import keep_last_per_row, position_range
+
+    pos = torch.tensor([[2, 4, 2, 9], [0, 1, 2, 3]])
+    assert position_range(pos) == (9, 0, True)
+    assert position_range(torch.tensor([[2, 4], [2, 4]])) == (4, 2, False)  # repeats across rows are fine
+    assert position_range(torch.tensor([[7], [3]])) == (7, 3, False)
+    assert keep_last_per_row(pos).tolist() == [[-1, 4, 2, 9], [0, 1, 2, 3]]

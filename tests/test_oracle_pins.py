@@ -314,3 +314,26 @@ def test_golden_rope_then_write_paged_kv(oracle, golden, case):
     assert table.block_ids == c["block_ids"]
     assert_bits_equal(pk[:, c["touched_blocks"]], c["keys"], "keys")
     assert_bits_equal(pv[:, c["touched_blocks"]], c["values"], "values")
+
+
+@pytest.mark.parametrize("case", ["f32", "bf16"])
+def test_golden_duplicate_positions(oracle, golden, case):
+    """A position given twice in one call: the reference keeps the later token's K/V, in
+    write_kv (per-row index_put) and in write_paged_kv (per-token loop); so does the oracle."""
+    c = golden["duplicates"][f"write_kv_{case}"]
+    L, B, H, S, D = c["cfg"]
+    ck, cv = _pool((L, B, H, S, D), c["keys"].dtype), _pool((L, B, H, S, D), c["keys"].dtype)
+    oracle.write_kv(ck, cv, c["layer"], c["positions"], c["key"], c["value"])
+    assert_bits_equal(ck, c["keys"], "write_kv keys")
+    assert_bits_equal(cv, c["values"], "write_kv values")
+    # the later duplicate is the one the reference kept
+    b, s_late = 1, 4  # row 1 writes position 0 at tokens 0, 1, 2 and 4
+    assert_bits_equal(c["keys"][c["layer"], b, :, 0], c["key"][b, :, s_late], "last duplicate kept")
+    p = golden["duplicates"][f"write_paged_kv_{case}"]
+    pk, pv = _pool(p["keys"].shape, p["keys"].dtype), _pool(p["keys"].shape, p["keys"].dtype)
+    a = oracle.RefBlockAllocator(p["num_blocks"])
+    t = oracle.RefBlockTable([], p["block_size"])
+    oracle.write_paged_kv(pk, pv, a, p["layer"], t, p["positions"][0].tolist(), p["key"], p["value"])
+    assert t.block_ids == p["block_ids"] and t.seq_len == p["seq_len"]
+    assert_bits_equal(pk, p["keys"], "write_paged_kv keys")
+    assert_bits_equal(pv, p["values"], "write_paged_kv values")
