@@ -126,12 +126,42 @@ def copy_prefix_into_cache(entry: PrefixCacheEntry, cache: KVCache, batch_idx: i
     cache.seq_len = max(cache.seq_len, entry.seq_len)
 
 
+def _entry_kv(cache: KVCache) -> tuple[Tensor, Tensor]:
+    """Rows [0, seq_len) of batch row 0, every layer and head, copied out of the cache into
+    fresh ``[layers, kv_heads, seq_len, head_dim]`` tensors by the run-copy kernel (one launch)."""
+    kc, vc = cache.keys, cache.values
+    L, B, H, S, D = kc.shape
+    P = cache.seq_len
+    keys = torch.empty(L, H, P, D, dtype=kc.dtype, device=kc.device)
+    values = torch.empty(L, H, P, D, dtype=vc.dtype, device=vc.device)
+    if P > 0:
+        max_rows = _ops.max_rows_for(D, kc.element_size())
+        runs = torch.from_numpy(prefix_runs(P, 0, max_rows)).to(kc.device)
+        src = lambda t: (t.stride(0), t.stride(1), t.stride(3), t.stride(2))  # noqa: E731
+        dst = lambda t: (t.stride(0), 0, t.stride(2), t.stride(1))  # noqa: E731
+        if kc.stride() == vc.stride() and kc.dtype == vc.dtype:
+            pairs = [(kc, vc, keys, values)]
+        else:
+            pairs = [(kc, None, keys, None), (vc, None, values, None)]
+        for sk, sv, dk, dv in pairs:
+            _ops.copy_runs(src_k=sk, src_v=sv, src_strides=src(sk), src_majors=B, src_rows_per_major=S,
+                           dst_k=dk, dst_v=dv, dst_strides=dst(dk), dst_majors=1, dst_rows_per_major=P,
+                           runs=runs, max_rows=max_rows, n_layers=L, n_heads=H, head_dim=D)
+    return keys, values
+
+
 def cache_prefix(input_ids: Tensor, w, cfg) -> PrefixCacheEntry:
-    """Prefill ``input_ids`` with augur's model and keep its K/V (prefix_cache.py:78-98)."""
+    """Prefill ``input_ids`` with augur's model and keep its K/V (prefix_cache.py:78-98).
+
+    The model's forward pass is augur's; the cache it fills is copied into the
+    entry by the library's run-copy kernel, so input_ids must be on a CUDA
+    device (CPU tensors raise ValueError, as every cache entry point here does).
+    """
     if input_ids.ndim != 2 or input_ids.shape[0] != 1:
         raise ValueError("prefix caching currently supports batch size 1")
     if input_ids.shape[1] == 0:
         raise ValueError("prefix must contain at least one token")
+    _ops.require_cuda("cache_prefix", input_ids)
     forward = model
     if forward is None:
         try:
@@ -150,9 +180,10 @@ def cache_prefix(input_ids: Tensor, w, cfg) -> PrefixCacheEntry:
     )
     position_ids = torch.arange(input_ids.shape[1], device=input_ids.device).unsqueeze(0)
     logits = forward(input_ids, w, cfg, cache=cache, position_ids=position_ids)
+    keys, values = _entry_kv(cache)
     return PrefixCacheEntry(
         token_ids=input_ids[0].detach().clone(),
-        keys=cache.keys[:, 0, :, : cache.seq_len, :].detach().clone(),
-        values=cache.values[:, 0, :, : cache.seq_len, :].detach().clone(),
+        keys=keys,
+        values=values,
         logits=logits[:, -1:, :].detach().clone(),
     )

@@ -307,6 +307,38 @@ def cpu_scatter_passes(seconds: float, min_passes: int = 2, threads: int | None 
     return scatter_bytes(int(lens.sum())) * n / el / 1e9, n, threads, el / n
 
 
+def cpu_reference_torch_loop(n_seqs: int = 8, threads: int | None = None) -> dict:
+    """The reference's own CPU path for the prefill scatter, timed on this host: its
+    per-token torch loop (augur/paged_kv_cache.py:188-192, restated in the oracle because
+    the reference package is not installed here) over the first `n_seqs` sequences of the
+    config-2 batch, every layer, one write_paged_kv call per (sequence, layer)."""
+    from oracle import kv_oracle
+
+    threads = threads or (os.cpu_count() or 1)
+    torch.set_num_threads(threads)
+    lens, _, k, v, _ = config2_batch(seed=0)
+    lens = lens[:n_seqs]
+    pk = torch.zeros(L, 4096, H, BS, D, dtype=torch.bfloat16)
+    pv = torch.zeros_like(pk)
+    alloc = kv_oracle.RefBlockAllocator(4096)
+    t0, pos0 = time.perf_counter(), 0
+    for n in lens:
+        n = int(n)
+        table = kv_oracle.RefBlockTable([], BS)
+        pos = torch.arange(n).unsqueeze(0)
+        for layer in range(L):
+            key = k[layer, pos0 : pos0 + n].permute(1, 0, 2).unsqueeze(0)  # [1, H, n, D] view, as attention passes it
+            val = v[layer, pos0 : pos0 + n].permute(1, 0, 2).unsqueeze(0)
+            kv_oracle.write_paged_kv_torch_loop(pk, pv, alloc, layer, table, pos, key, val)
+        pos0 += n
+    el = time.perf_counter() - t0
+    tl = int(lens.sum()) * L
+    return {"token_layers_per_s": round(tl / el, 1), "us_per_token_layer": round(el / tl * 1e6, 3),
+            "GBps": round(tl * 2 * TOKEN_LAYER_BYTES / el / 1e9, 5), "threads": threads,
+            "sample": f"first {n_seqs} config-2 sequences ({int(lens.sum())} tokens) x {L} layers, one "
+                      "write_paged_kv per (sequence, layer): the reference's per-token torch loop"}
+
+
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
@@ -493,6 +525,7 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
         line["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                                 "sample": f"{passes} full config-2 scatters (8192 tokens x 24 layers), "
                                           f"{per * 1e3:.1f} ms each, C oracle with {threads} threads"}
+        line["extra"]["cpu_reference_torch_loop"] = cpu_reference_torch_loop()
     return line
 
 
@@ -1414,6 +1447,7 @@ def run_reference(args, world: int, rank: int) -> dict | None:
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "reference_torch_loop": cpu_reference_torch_loop(),
     }
 
 

@@ -9,7 +9,9 @@ It restates semioz/augur's cache algorithm:
     order of effects: RefBlockAllocator (augur/paged_kv_cache.py:10-22),
     RefBlockTable (:88-139), ref_block_hash (:84-85);
   * data movement through liboracle_kv.so (kv_oracle.c), one C function per
-    reference loop, on torch CPU tensors.
+    reference loop, on torch CPU tensors;
+  * write_paged_kv_torch_loop: the reference's per-token torch loop itself,
+    restated only so the CPU baseline can time the reference's own path.
 
 Parity pin: tests/test_oracle_pins.py checks every function here against the
 known-answer cases of the reference's own tests (tests/test_kv_cache.py,
@@ -202,6 +204,19 @@ def write_paged_kv(pool_k, pool_v, allocator: RefBlockAllocator, layer: int, tab
                                             layer, _i64_ptr(b), _i64_ptr(o), n, heads, head_dim)
     if err is not None:
         raise err
+
+
+def write_paged_kv_torch_loop(pool_k, pool_v, allocator: RefBlockAllocator, layer: int, table: RefBlockTable,
+                              position_ids: torch.Tensor, key: torch.Tensor, value: torch.Tensor) -> None:
+    """augur/paged_kv_cache.py:188-192 as the reference runs it: a Python loop over the tokens
+    with one torch row assignment per token for K and one for V. Used to time the reference's
+    own CPU path on hosts where the reference package is not installed; the C restatement
+    (write_paged_kv above) is the checker."""
+    for token_idx, position in enumerate(position_ids[0].tolist()):
+        table.ensure_position(position, allocator)
+        physical_block, offset = table.position_to_block_offset(position)
+        pool_k[layer, physical_block, :, offset, :] = key[0, :, token_idx, :]
+        pool_v[layer, physical_block, :, offset, :] = value[0, :, token_idx, :]
 
 
 def read_paged_kv(pool_k, pool_v, layer: int, table: RefBlockTable, seq_len: int | None = None):

@@ -293,3 +293,36 @@ def test_duplicate_positions_golden(cuda, golden, case, positions_on_host):
     assert_bits_equal(pool.keys, p["keys"], "write_paged_kv keys")
     assert_bits_equal(pool.values, p["values"], "write_paged_kv values")
     assert _ops.read_status(cuda) == _lib.OK
+
+
+def test_cache_prefix_copies_the_cache_through_the_library(cuda, monkeypatch):
+    """cache_prefix runs augur's forward (a stand-in here) into a fresh cache and keeps its
+    K/V as [layers, kv_heads, prefix, head_dim]; the copy out of the cache is one run-copy
+    launch, bit-exact with the rows the forward wrote."""
+    from types import SimpleNamespace
+
+    from augur_b200 import prefix_cache
+
+    cfg = _tiny_cfg(3, 16, 2, 2)  # head_dim 8
+    g = torch.Generator(device=cuda).manual_seed(8)
+    wrote = {}
+
+    def fake_model(input_ids, w, cfg, cache=None, position_ids=None):
+        n = input_ids.shape[1]
+        assert position_ids.tolist() == [list(range(n))]
+        wrote["k"] = torch.randn(cache.keys[:, 0, :, :n].shape, generator=g, device=cuda).to(cache.keys.dtype)
+        wrote["v"] = torch.randn(cache.keys[:, 0, :, :n].shape, generator=g, device=cuda).to(cache.keys.dtype)
+        cache.keys[:, 0, :, :n] = wrote["k"]
+        cache.values[:, 0, :, :n] = wrote["v"]
+        cache.seq_len = n
+        return torch.zeros(1, n, cfg.vocab_size, device=cuda)
+
+    monkeypatch.setattr(prefix_cache, "model", fake_model)
+    launches = _ops.launch_count
+    entry = ab.cache_prefix(torch.tensor([[4, 5, 6, 7, 8]], device=cuda),
+                            SimpleNamespace(embed_tokens=torch.empty(0, dtype=torch.bfloat16)), cfg)
+    assert _ops.launch_count == launches + 1
+    assert entry.keys.shape == (3, 2, 5, 8) and entry.keys.device == cuda
+    assert_bits_equal(entry.keys, wrote["k"], "entry keys")
+    assert_bits_equal(entry.values, wrote["v"], "entry values")
+    assert entry.token_ids.tolist() == [4, 5, 6, 7, 8] and entry.logits.shape == (1, 1, cfg.vocab_size)

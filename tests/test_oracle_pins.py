@@ -337,3 +337,17 @@ def test_golden_duplicate_positions(oracle, golden, case):
     assert t.block_ids == p["block_ids"] and t.seq_len == p["seq_len"]
     assert_bits_equal(pk, p["keys"], "write_paged_kv keys")
     assert_bits_equal(pv, p["values"], "write_paged_kv values")
+
+
+def test_torch_loop_write_paged_kv_matches_golden(oracle, golden):
+    """The torch-loop restatement (timed as the reference's own CPU path) writes what the
+    reference wrote, including the duplicate-position case."""
+    for name in ("bf16", "f32"):
+        p = golden["duplicates"][f"write_paged_kv_{name}"]
+        pk, pv = _pool(p["keys"].shape, p["keys"].dtype), _pool(p["keys"].shape, p["keys"].dtype)
+        a = oracle.RefBlockAllocator(p["num_blocks"])
+        t = oracle.RefBlockTable([], p["block_size"])
+        oracle.write_paged_kv_torch_loop(pk, pv, a, p["layer"], t, p["positions"], p["key"], p["value"])
+        assert t.block_ids == p["block_ids"]
+        assert_bits_equal(pk, p["keys"], f"{name} keys")
+        assert_bits_equal(pv, p["values"], f"{name} values")
