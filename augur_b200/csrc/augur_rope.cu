@@ -258,6 +258,116 @@ __global__ void __launch_bounds__(256) rope_scatter_kernel(RopeArgs a) {
   }
 }
 
+// Resident 128-thread CTAs per SM the token-grouped kernel is compiled for
+// (8: at most 64 registers, so a config-2-sized prefill is one wave).
+#ifndef AUGUR_KV_ROPE_TOKEN
+#define AUGUR_KV_ROPE_TOKEN 1
+#endif
+#ifndef AUGUR_KV_ROPE_MIN_CTAS
+#define AUGUR_KV_ROPE_MIN_CTAS 8
+#endif
+
+// Token-grouped form for 16-bit rows whose halves are whole 16-byte pieces
+// (head_dim 64: PH = 4 pieces per half; head_dim 128: PH = 8). LT = 4 PH
+// lanes serve one token: lane l owns column piece c = l % PH of the rotated
+// rows rg, rg + 4, rg + 8, rg + 12 (rg = l / PH; q heads first, then k
+// heads), and v piece l of the token. The token's position and slot are
+// loaded once per lane (one request per group), every source load of a
+// 16-row block goes out before the first rotation, and the cos / sin pieces
+// are loaded once per lane for all of its rows. At augur's shape (14 + 2
+// rotated rows, 2 v rows, head_dim 64) a lane moves 9 pieces, and a
+// config-2-sized prefill (8,192 tokens) is one resident wave with no tail.
+template <typename T, int PH>
+__global__ void __launch_bounds__(128, AUGUR_KV_ROPE_MIN_CTAS) rope_token_kernel(RopeArgs a) {
+  constexpr int LT = 4 * PH;
+  using P = Piece<T, 8>;
+  const int layer = blockIdx.y;
+  const int l = int(threadIdx.x) % LT;
+  const int c = l % PH, rg = l / PH;
+  const int R = a.hq + a.hkv;
+  const int nv = a.has_v ? a.hkv * a.cc : 0;
+  constexpr int kHalfBytes = PH * 16;  // the second half of a row is a fixed offset from the first
+  const int e0 = c * 16;
+  const uint32_t groups = (gridDim.x * blockDim.x) / LT;
+  for (uint32_t t = (blockIdx.x * blockDim.x + threadIdx.x) / LT; t < uint32_t(a.n_tokens); t += groups) {
+    int64_t row, col;
+    if (a.tokens_per_row == a.n_tokens) {
+      row = 0;
+      col = t;
+    } else {
+      const uint32_t tr = t / uint32_t(a.tokens_per_row);
+      row = tr;
+      col = int64_t(t) - int64_t(tr) * a.tokens_per_row;
+    }
+    const int64_t p = a.pos[row * a.pos_stride[0] + col * a.pos_stride[1]];
+    const int64_t idx = a.index[row * a.index_stride[0] + col * a.index_stride[1]];
+    const char* qbase = a.q + layer * a.q_stride[0] + row * a.q_stride[1] + col * a.q_stride[2];
+    const char* kbase = a.src[0] + layer * a.src_stride[0][0] + row * a.src_stride[0][1] + col * a.src_stride[0][2];
+    auto src_of = [&](int r) -> const char* {
+      return r < a.hq ? qbase + r * a.q_stride[3] : kbase + (r - a.hq) * a.src_stride[0][3];
+    };
+    // the token's v piece l, loaded with the first block of rotated rows
+    P xv;
+    int vh = 0, vc = 0;
+    if (l < nv) {
+      vh = l / (2 * PH);  // v rows are 2 PH pieces
+      vc = l % (2 * PH);
+      xv = load_piece<T, 8>(a.src[1] + layer * a.src_stride[1][0] + row * a.src_stride[1][1] +
+                            col * a.src_stride[1][2] + vh * a.src_stride[1][3] + vc * 16);
+    }
+    P x1[4], x2[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int r = rg + 4 * j;
+      if (r < R) {
+        const char* src = src_of(r);
+        x1[j] = load_piece<T, 8>(src + e0);
+        x2[j] = load_piece<T, 8>(src + e0 + kHalfBytes);
+      }
+    }
+    int64_t major = 0, off = 0;
+    const bool slot_ok = rope_slot(a, row, idx, major, off);
+    const int64_t dofs = layer * a.dst_stride[0] + major * a.dst_stride[1] + off * a.dst_stride[2];
+    if (slot_ok && l < nv) store_piece<T, 8>(a.dst[1] + dofs + vh * a.dst_stride[3] + vc * 16, xv);
+    char* kdst = a.dst[0] + dofs;
+    const bool p_ok = p >= 0 && p < a.n_pos;
+    if (!p_ok && l == 0) record_status(a.status, AUGUR_KV_EBOUNDS);
+    P cs, sn;
+    if (p_ok) {
+      const int64_t tab = p * a.half * int64_t(sizeof(T)) + e0;
+      cs = load_piece<T, 8>(a.cos_t + tab);
+      sn = load_piece<T, 8>(a.sin_t + tab);
+    }
+    char* qdst = a.q_out + layer * a.q_out_stride[0] + row * a.q_out_stride[1] + col * a.q_out_stride[2];
+    auto rotate_store = [&](int r, const P& y1, const P& y2) {
+      char* dst;
+      if (r < a.hq) dst = qdst + r * a.q_out_stride[3];
+      else if (slot_ok) dst = kdst + (r - a.hq) * a.dst_stride[3];
+      else return;
+      P o1, o2;
+      Rotate<T, 8>::run(y1, y2, cs, sn, o1, o2);
+      store_piece<T, 8>(dst + e0, o1);
+      store_piece<T, 8>(dst + e0 + kHalfBytes, o2);
+    };
+    if (p_ok) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int r = rg + 4 * j;
+        if (r < R) rotate_store(r, x1[j], x2[j]);
+      }
+    }
+    if (slot_ok) {
+      char* vdst = a.dst[1] + dofs;
+      for (int pv = l + LT; pv < nv; pv += LT) {  // more v pieces than lanes (more KV heads)
+        split_task(pv, a.cc, a.sh_cc, vh, vc);
+        const P x = load_piece<T, 8>(a.src[1] + layer * a.src_stride[1][0] + row * a.src_stride[1][1] +
+                                     col * a.src_stride[1][2] + vh * a.src_stride[1][3] + vc * 16);
+        store_piece<T, 8>(vdst + vh * a.dst_stride[3] + vc * 16, x);
+      }
+    }
+  }
+}
+
 }  // namespace augur_kv_dev
 
 using namespace augur_kv_dev;
@@ -297,9 +407,35 @@ int launch_rope(RopeArgs a, int n_layers, cudaStream_t st) {
   return check_launch("rope_scatter_kernel");
 }
 
+// The token-grouped kernel: lanes of a token = 4 x pieces per half; one
+// resident wave of CTAs at most, groups loop over the remaining tokens.
+template <typename T, int PH>
+int launch_rope_token(RopeArgs a, int n_layers, cudaStream_t st) {
+  a.rc = PH;
+  a.cc = 2 * PH;
+  a.sh_rc = pow2_log(a.rc);
+  a.sh_cc = pow2_log(a.cc);
+  a.tasks = 0;
+  constexpr uint64_t kThreads = 128;
+  const uint64_t lanes = uint64_t(a.n_tokens) * 4 * PH;
+  uint64_t blocks = (lanes + kThreads - 1) / kThreads;
+  const uint64_t wave =
+      uint64_t(sm_count()) * uint64_t(resident_ctas(reinterpret_cast<const void*>(rope_token_kernel<T, PH>), kThreads));
+  if (blocks > wave) blocks = wave;
+  if (blocks < 1) blocks = 1;
+  rope_token_kernel<T, PH><<<dim3(unsigned(blocks), unsigned(n_layers)), unsigned(kThreads), 0, st>>>(a);
+  return check_launch("rope_token_kernel");
+}
+
 template <typename T>
 int launch_rope_t(const RopeArgs& a, int n_layers, bool vec, cudaStream_t st) {
   constexpr int V = 16 / int(sizeof(T));
+  if constexpr (sizeof(T) == 2) {
+    const int half_bytes = a.half * 2;
+    const bool token_ok = vec && a.hq + a.hkv <= 16 && AUGUR_KV_ROPE_TOKEN;
+    if (token_ok && half_bytes == 64) return launch_rope_token<T, 4>(a, n_layers, st);
+    if (token_ok && half_bytes == 128) return launch_rope_token<T, 8>(a, n_layers, st);
+  }
   return vec ? launch_rope<T, V>(a, n_layers, st) : launch_rope<T, 1>(a, n_layers, st);
 }
 
