@@ -258,13 +258,17 @@ __global__ void __launch_bounds__(256) rope_scatter_kernel(RopeArgs a) {
   }
 }
 
-// Resident 128-thread CTAs per SM the token-grouped kernel is compiled for
-// (8: at most 64 registers, so a config-2-sized prefill is one wave).
+// Resident 128-thread CTAs per SM the token-grouped kernel is compiled for.
+// 7 (at most 72 registers, no spills) makes a config-2-sized prefill, 8,192
+// tokens x 16 lanes = 1,024 CTAs, one wave of 7 x 148 = 1,036 slots. Measured
+// per layer on B200: 8.14-8.18 us with 7, 8.66-8.73 us with 8 (64 registers,
+// spills), 8.85-8.91 us with 6 (a partial second wave), 9.45 us for the
+// thread-per-piece kernel.
 #ifndef AUGUR_KV_ROPE_TOKEN
 #define AUGUR_KV_ROPE_TOKEN 1
 #endif
 #ifndef AUGUR_KV_ROPE_MIN_CTAS
-#define AUGUR_KV_ROPE_MIN_CTAS 8
+#define AUGUR_KV_ROPE_MIN_CTAS 7
 #endif
 
 // Token-grouped form for 16-bit rows whose halves are whole 16-byte pieces
@@ -277,6 +281,9 @@ __global__ void __launch_bounds__(256) rope_scatter_kernel(RopeArgs a) {
 // are loaded once per lane for all of its rows. At augur's shape (14 + 2
 // rotated rows, 2 v rows, head_dim 64) a lane moves 9 pieces, and a
 // config-2-sized prefill (8,192 tokens) is one resident wave with no tail.
+// The host uses it for at most 16 rotated rows per token (q heads + k heads);
+// more rows, fp32 and rows that are not 16-byte aligned take
+// rope_scatter_kernel.
 template <typename T, int PH>
 __global__ void __launch_bounds__(128, AUGUR_KV_ROPE_MIN_CTAS) rope_token_kernel(RopeArgs a) {
   constexpr int LT = 4 * PH;

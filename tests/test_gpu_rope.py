@@ -113,7 +113,7 @@ def _batch_case(cuda, oracle, dtype, T, Hq, Hkv, D, seed, head_stride_pad=0):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
-@pytest.mark.parametrize("Hq, Hkv, D", [(14, 2, 64), (8, 2, 128)])
+@pytest.mark.parametrize("Hq, Hkv, D", [(14, 2, 64), (8, 2, 128), (4, 4, 64), (12, 4, 128), (28, 4, 64)])
 def test_batch_matches_oracle(cuda, oracle, dtype, Hq, Hkv, D):
     _batch_case(cuda, oracle, dtype, 300, Hq, Hkv, D, 5)
 
