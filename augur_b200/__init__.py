@@ -8,8 +8,11 @@ error messages):
   augur_b200.prefix_cache    <- augur/prefix_cache.py
 
 plus batched all-layer entry points in augur_b200.batched and sequence
-sharding / peer push in augur_b200.sharding. Every byte of cache data is
-moved by libaugur_kv.so (include/augur_kv.h); there is no CPU fallback.
+sharding / peer push in augur_b200.sharding and augur_b200.peer, and the
+cache's consumers that read the pool in place in augur_b200.attention
+(decode and prefill attention) and augur_b200.decode. Every byte of cache
+data the device moves goes through libaugur_kv.so (include/augur_kv.h);
+there is no CPU fallback.
 """
 
 from ._lib import KVLibraryError

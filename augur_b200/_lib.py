@@ -72,6 +72,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _I64P, _P, _P, _I64P, _I64, _I32, _P, _I64, _I64, _P, _I32, _I32, _I32, _I32, _I32, _I32,
          _P, _I64P, _I32, _P, _I64, _P, _I64, _P, _P],
     ),
+    "augur_kv_paged_prefill_attention": (
+        ctypes.c_int,
+        [_P, _I64P, _P, _P, _I64P, _I64, _I32, _P, _I64, _I64, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
+         _I32, _P, _I64P, _I32, _P, _P],
+    ),
     "augur_kv_paged_decode_attention_workspace": (
         ctypes.c_int, [_I32, _I32, _I32, _I32, _I32, _I32, _I32, _I64P, _I64P]),
     "augur_kv_rope_scatter": (

@@ -166,3 +166,114 @@ def paged_decode_attention(
     if out is not None:
         return out
     return out3.unsqueeze(2) if squeeze else out3
+
+
+class PrefillQueries:
+    """Device copy of a batch's query-token counts, reusable across layers (and inside a
+    CUDA graph, where no host data may be uploaded): starts int32 [batch + 1], sequence b's
+    query tokens being rows [starts[b], starts[b + 1]) of q."""
+
+    def __init__(self, q_lens: Sequence[int], device: torch.device) -> None:
+        lens = np.asarray(q_lens, dtype=np.int64)
+        if lens.size and lens.min() < 0:
+            raise ValueError("q_lens must be non-negative")
+        starts = np.zeros(lens.size + 1, dtype=np.int32)
+        np.cumsum(lens, out=starts[1:])
+        self.lens = lens
+        self.total = int(starts[-1])
+        self.max_len = int(lens.max(initial=0))
+        self.starts = torch.from_numpy(starts).to(device)
+
+
+def paged_prefill_attention(
+    q: Tensor,
+    cache: PagedKVCache,
+    layer_idx: int,
+    tables: Sequence[SequenceBlockTable] | DecodeTables,
+    q_lens: Sequence[int] | PrefillQueries,
+    out: Tensor | None = None,
+    generic: bool = False,
+    stream: torch.cuda.Stream | None = None,
+) -> Tensor:
+    """Attention of a batch's new tokens over the pool (one layer, one launch).
+
+    q: ``[tokens, n_q_heads, head_dim]`` after RoPE, the sequences' new tokens
+    concatenated in table order (q_lens[b] of them for sequence b; pass a
+    PrefillQueries, with a DecodeTables, to reuse both across layers). Each
+    table's seq_len counts its cached positions with the new tokens included,
+    so write them first (write_paged_kv_batch, or its RoPE form). New token i
+    of sequence b sits at position seq_len - q_lens[b] + i and attends to
+    positions [0, that position]: a plain prefill when q_lens[b] == seq_len, the
+    suffix of a prompt whose prefix blocks were shared from the prefix index
+    otherwise. Returns ``[tokens, n_q_heads, head_dim]`` (heads not yet
+    concatenated). generic=True forces the CUDA-core kernel.
+    """
+    if q.dim() != 3:
+        raise ValueError("q must be [tokens, n_q_heads, head_dim]")
+    _ops.require_cuda("paged_prefill_attention", q, cache.keys, cache.values)
+    if not 0 <= layer_idx < cache.keys.shape[0]:
+        raise ValueError("layer_idx is outside the cache layer range")
+    L, NB, Hkv, bs, D = cache.keys.shape
+    T, Hq, Dq = q.shape
+    if Dq != D or Hq % Hkv != 0:
+        raise ValueError("query shape does not match the cache (head_dim, or heads not a multiple of KV heads)")
+    if q.dtype != cache.keys.dtype:
+        raise ValueError("query and cache dtypes differ")
+    pq = q_lens if isinstance(q_lens, PrefillQueries) else PrefillQueries(q_lens, cache.keys.device)
+    lens = pq.lens
+    if pq.total != T:
+        raise ValueError("q_lens must add up to the number of query tokens")
+    dt = tables if isinstance(tables, DecodeTables) else DecodeTables(tables, cache.keys.device)
+    if dt.batch != lens.size:
+        raise ValueError("one block table per sequence is required")
+    if dt.block_size != bs:
+        raise ValueError("block table block_size must equal the cache block size")
+    if not isinstance(tables, DecodeTables) and any(int(n) > t.seq_len for n, t in zip(lens, tables)):
+        raise ValueError("a sequence has more query tokens than cached positions (write them first)")
+    if q.stride(-1) != 1:
+        q = q.contiguous()
+    out3 = torch.empty(T, Hq, D, dtype=q.dtype, device=q.device) if out is None else out
+    if tuple(out3.shape) != (T, Hq, D) or out3.stride(-1) != 1 or out3.dtype != q.dtype:
+        raise ValueError("out must be a [tokens, n_q_heads, head_dim] tensor of q's dtype, head_dim contiguous")
+    if T == 0:
+        return out3
+    kc, vc = cache.keys[layer_idx], cache.values[layer_idx]
+    if kc.stride() != vc.stride():
+        raise ValueError("keys and values must share one layout")
+    lib = _lib.load()
+    device = kc.device
+    st = stream if stream is not None else torch.cuda.current_stream(device)
+    q_starts = pq.starts
+    flags = _lib.ATTN_GENERIC if generic else _lib.ATTN_AUTO
+    with _ops._DeviceGuard(device):
+        code = lib.augur_kv_paged_prefill_attention(
+            q.data_ptr(), _lib.i64_array((q.stride(0), q.stride(1))),
+            kc.data_ptr(), vc.data_ptr(), _lib.i64_array((kc.stride(0), kc.stride(1), kc.stride(2))),
+            NB, bs, dt.blocks.data_ptr(), dt.blocks.stride(0), dt.blocks.shape[1],
+            dt.lens.data_ptr(), q_starts.data_ptr(), lens.size, pq.max_len,
+            max(dt.max_seq_len, 1), Hq, Hkv, D, _ops.dtype_code(q),
+            out3.data_ptr(), _lib.i64_array((out3.stride(0), out3.stride(1))), flags,
+            _ops.status_word(device).data_ptr(), st.cuda_stream)
+    _lib.check(code, "augur_kv_paged_prefill_attention")
+    _ops.launch_count += 1
+    _ops.keep_until_done(st, q, dt.blocks, dt.lens, q_starts)
+    return out3
+
+
+def paged_attention(
+    q: Tensor,
+    cache: PagedKVCache,
+    layer_idx: int,
+    block_table: SequenceBlockTable,
+    generic: bool = False,
+) -> Tensor:
+    """The attention core of augur's paged branch for one sequence (augur/attention.py:72-86)
+    after its write: q ``[1, n_q_heads, seq, head_dim]`` (after RoPE) attends over the
+    table's seq_len cached positions with the reference's causal mask (its seq query
+    tokens are the last seq positions). Returns ``[1, n_q_heads, seq, head_dim]``; the
+    pool is read in place (no read_paged_kv gather, no repeated KV heads)."""
+    if q.dim() != 4 or q.shape[0] != 1:
+        raise ValueError("paged KV cache currently supports batch size 1")
+    out = paged_prefill_attention(q[0].transpose(0, 1), cache, layer_idx, [block_table], [q.shape[2]],
+                                  generic=generic)
+    return out.transpose(0, 1).unsqueeze(0)

@@ -17,7 +17,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.dirname(HERE)
 ROOT = os.path.dirname(PKG)
-SOURCES = [os.path.join(HERE, f) for f in ("augur_kv.cu", "augur_attn.cu", "augur_rope.cu", "augur_decode.cu")]
+SOURCES = [os.path.join(HERE, f) for f in ("augur_kv.cu", "augur_attn.cu", "augur_rope.cu", "augur_decode.cu", "augur_prefill.cu")]
 HEADERS = [os.path.join(ROOT, "include", "augur_kv.h"), os.path.join(HERE, "common.cuh")]
 OUTPUT = os.path.join(PKG, "libaugur_kv.so")
 

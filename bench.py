@@ -842,6 +842,87 @@ def bench_offload(device, pool, tables, n_seqs: int = 16) -> dict:
     return out
 
 
+def bench_prefill_attention(device, pool, tables, suffix: int, flush) -> dict:
+    """Suffix prefill attention over shared prefixes (config 4: 256 forks of one prefix, each
+    with its own suffix already written): every layer, the suffix queries of all forks attend
+    to their prefix and causally to their suffix, one paged_prefill_attention launch per layer,
+    replayed from a CUDA graph with L2 flushed before each replay.
+
+    Algorithmic bytes: each sequence's cached K/V read once (seq_len x 512 B per layer) plus q
+    and the output; FLOPs: 4 x head_dim per (query head, query token, visible key)."""
+    from augur_b200.attention import DecodeTables, PrefillQueries, paged_prefill_attention
+
+    Hq = 14
+    B = len(tables)
+    dt = DecodeTables(tables, device)
+    lens = PrefillQueries([suffix] * B, device)
+    g = torch.Generator(device=device).manual_seed(41)
+    q = torch.randn(B * suffix, Hq, D, generator=g, device=device).to(torch.bfloat16)
+    out = torch.empty_like(q)
+
+    def step() -> None:
+        for layer in range(L):
+            paged_prefill_attention(q, pool, layer, dt, lens, out=out)
+
+    cs = torch.cuda.Stream(device)
+    cs.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(cs):
+        step()
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=cs):
+        step()
+    times = []
+    for _ in range(5):
+        flush.fill_(1)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        graph.replay()
+        b.record()
+        torch.cuda.synchronize(device)
+        times.append(a.elapsed_time(b))
+    graph.reset()
+    ms = statistics.median(times[1:]) / L
+    seq = [t.seq_len for t in tables]
+    kv_bytes = sum(seq) * TOKEN_LAYER_BYTES + 2 * q.numel() * 2
+    flops = sum(4 * D * Hq * sum(n - suffix + i + 1 for i in range(suffix)) for n in seq)
+    peak, kind = load_peaks()
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            tf_peak, tf_kind = float(json.load(f)["bf16_tflops"]), "bf16_tflops (burst) of measured"
+    except Exception:
+        tf_peak, tf_kind = 1590.0, "fallback"
+    tflops = flops / (ms / 1e3) / 1e12
+    return {"seqs": B, "suffix_tokens": suffix, "cached_tokens_per_seq": seq[0], "us_per_layer": round(ms * 1e3, 2),
+            "kv_GBps": round(kv_bytes / (ms / 1e3) / 1e9, 1), "kv_frac_of_hbm_peak": round(kv_bytes / (ms / 1e3) / 1e9 / peak, 4),
+            "TFLOPs": round(tflops, 1), "tensor_frac": round(tflops / tf_peak, 4), "tensor_peak_source": tf_kind,
+            "kernel": "attn_prefill_mma_kernel<bf16,64> (mma.sync)",
+            "timed": "CUDA graph of 24 per-layer launches, L2 flushed; the forks share the prefix's blocks"}
+
+
+def run_prefill_attention_only(device) -> dict:
+    """Profiling case: config 4's 1,024-token prefix forked 256 ways with 128-token
+    suffixes (a 8,192-block pool, 1.6 GB), then the suffix prefill attention."""
+    import augur_b200 as ab
+    from augur_b200 import batched
+
+    NB = 8192
+    pool = ab.PagedKVCache(keys=torch.empty(L, NB, H, BS, D, dtype=torch.bfloat16, device=device),
+                           values=torch.empty(L, NB, H, BS, D, dtype=torch.bfloat16, device=device),
+                           block_size=BS, allocator=ab.BlockAllocator(NB))
+    g = torch.Generator(device=device).manual_seed(4)
+    parent = ab.SequenceBlockTable.empty(BS)
+    sm = batched.prefill_slot_mapping([parent], [1024], pool.allocator)[0]
+    pk = torch.randn(L, 1024, H, D, generator=g, device=device).to(torch.bfloat16)
+    batched.write_paged_kv_batch(pool, pk, pk, torch.from_numpy(sm).to(device))
+    forks = batched.fork_prefix(pool, parent, 256)
+    suffix = batched.prefill_slot_mapping(forks, [128] * 256, pool.allocator, start_positions=[1024] * 256)
+    sk = torch.randn(L, 256 * 128, H, D, generator=g, device=device).to(torch.bfloat16)
+    batched.write_paged_kv_batch(pool, sk, sk, torch.from_numpy(suffix.reshape(-1)).to(device))
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    return {"suffix_prefill_attention": bench_prefill_attention(device, pool, forks, 128, flush)}
+
+
 def bench_cow_device(device, pool, parent, forks, prefix_len: int, flush) -> dict:
     """The copy-on-write launch alone: the parent's partial block copied into every fork's
     private block (all layers, K and V), replayed from a CUDA graph with L2 flushed before
@@ -1012,6 +1093,8 @@ def run_extras(device, handoff_only: bool = False, attention_only: bool = False,
                  "suffix_GBps": round(scatter_bytes(256 * 128) / (c0.elapsed_time(c) / 1e3) / 1e9, 1)}
         if copied:
             entry.update(bench_cow_device(device, pool4, parent, forks, prefix_len, flush))
+        else:
+            out["suffix_prefill_attention"] = bench_prefill_attention(device, pool4, forks, 128, flush)
         out[f"prefix_fork_{prefix_len}"] = entry
         del sk, pk
     if _ops.read_status(device) != _lib.OK:
@@ -1487,6 +1570,8 @@ def main() -> None:
                     help="profiling case: decode attention over 128 box-length sequences (about 2.2 GB)")
     ap.add_argument("--offload-only", action="store_true",
                     help="config-3 cache, then offload to pinned host memory and restore")
+    ap.add_argument("--prefill-attention-only", action="store_true",
+                    help="profiling case: config-4 forks, then the suffix prefill attention")
     ap.add_argument("--rope-only", action="store_true",
                     help="profiling case: config-3 cache, then RoPE fused with the paged write")
     ap.add_argument("--workload", choices=["scatter", "disagg", "box"], default="scatter",
@@ -1511,6 +1596,10 @@ def main() -> None:
     if args.offload_only:  # config-3 pool, then offload to pinned host memory and restore
         torch.cuda.set_device(0)
         emit(run_extras(torch.device("cuda", 0), offload_only=True))
+        return
+    if args.prefill_attention_only:  # profiling case: config-4 forks, then the suffix prefill attention
+        torch.cuda.set_device(0)
+        emit(run_prefill_attention_only(torch.device("cuda", 0)))
         return
     if args.rope_only:  # profiling case: config-3 pool, then the fused RoPE + write
         torch.cuda.set_device(0)

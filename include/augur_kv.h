@@ -230,6 +230,47 @@ int augur_kv_paged_decode_attention(const void* q, const int64_t* q_strides, /* 
                                     void* scratch, int64_t scratch_bytes, int32_t* status, void* stream);
 
 /*
+ * augur_kv_paged_prefill_attention — attention of a batch's new tokens (a
+ * prefill, or the suffix of a prompt whose prefix blocks are already in the
+ * pool) over the paged pool, one layer, reading every cached K/V row in place.
+ * Replaces, for a whole batch, augur's paged branch after the write
+ * (augur/attention.py:72-86: read_paged_kv, the GQA repeat, q k^T / sqrt(d),
+ * the causal mask of _causal_mask (:15-19) with past_len = key_len -
+ * query_len, the float32 softmax and P V), which the reference runs for a
+ * batch of one (augur/paged_kv_cache.py:179-180).
+ *
+ *   q        query token j (after RoPE), head h: element d at
+ *            q + j*q_strides[0] + h*q_strides[1] + d
+ *   q_starts device int32 [batch + 1]: sequence b's query tokens are
+ *            j in [q_starts[b], q_starts[b + 1]) (n_b of them, n_b <= max_q_len)
+ *   seq_lens device int32 [batch]: cached positions of sequence b, its query
+ *            tokens included (write them first); max_seq_len bounds them
+ *   pool, block tables: as augur_kv_paged_decode_attention
+ *   out      element (j, h, d) at out + j*out_strides[0] + h*out_strides[1] + d
+ * Query token q_starts[b] + i sits at position seq_lens[b] - n_b + i and
+ * attends to positions [0, seq_lens[b] - n_b + i]. Query head h reads KV head
+ * h / (n_q_heads / n_kv_heads). The result equals the reference's within
+ * floating-point tolerance (same rounding points, another summation order).
+ * Lengths that disagree (n_b < 0, n_b > seq_lens[b], seq_lens[b] >
+ * max_seq_len, n_b > max_q_len) record AUGUR_KV_EBOUNDS and skip that
+ * sequence; a block id outside [0, num_blocks) records it and reads as zeros.
+ * flags: AUGUR_KV_ATTN_AUTO takes the tensor-core kernel for bf16/fp16,
+ * head_dim 64 or 128, <= 8 query heads per KV head, 16-byte aligned pool rows
+ * and 4-byte aligned q / out; AUGUR_KV_ATTN_GENERIC forces the CUDA-core
+ * kernel (any dtype; max_seq_len <= ~51,000). Needs no workspace.
+ */
+int augur_kv_paged_prefill_attention(const void* q, const int64_t* q_strides, /* [2] token, head */
+                                     const void* k_pool, const void* v_pool,
+                                     const int64_t* pool_strides, /* [3] block, head, row */
+                                     int64_t num_blocks, int32_t block_size,
+                                     const int32_t* block_tables, int64_t tables_stride, int64_t max_blocks,
+                                     const int32_t* seq_lens, const int32_t* q_starts, int32_t batch,
+                                     int32_t max_q_len, int32_t max_seq_len, int32_t n_q_heads,
+                                     int32_t n_kv_heads, int32_t head_dim, int32_t dtype,
+                                     void* out, const int64_t* out_strides, /* [2] token, head */
+                                     int32_t flags, int32_t* status, void* stream);
+
+/*
  * augur_kv_paged_decode_attention_workspace — bytes of counters and scratch
  * that augur_kv_paged_decode_attention uses for these sizes on the current
  * device (0 and 0: none). No reference counterpart (the reference's eager

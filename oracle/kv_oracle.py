@@ -312,6 +312,27 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch
     return torch.matmul(probs, v)
 
 
+def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    """Attention of a call's n query tokens over the whole cached sequence, restating
+    augur/attention.py:74-86 with _causal_mask (:15-19).
+
+    q [B, Hq, n, D] (after RoPE), k / v [B, Hkv, S, D] (read_paged_kv: the cache
+    in logical order, the n new tokens last). Query i sits at position
+    S - n + i (past_len = key_len - query_len) and key positions above it are
+    masked with -inf before the float32 softmax; otherwise as decode_attention.
+    """
+    groups = q.shape[1] // k.shape[1]
+    k = k.repeat_interleave(groups, dim=1)
+    v = v.repeat_interleave(groups, dim=1)
+    scores = torch.matmul(q, k.transpose(-2, -1)) / math.sqrt(q.shape[-1])
+    n, S = q.shape[2], k.shape[2]
+    query_positions = torch.arange(n).unsqueeze(-1) + (S - n)
+    key_positions = torch.arange(S).unsqueeze(0)
+    scores = scores.masked_fill(key_positions > query_positions, float("-inf"))
+    probs = torch.softmax(scores, dim=-1, dtype=torch.float32).to(q.dtype)
+    return torch.matmul(probs, v)
+
+
 def rope_inv_freq(head_dim: int, rope_theta: float) -> torch.Tensor:
     """augur/rope.py:29-32: 1 / theta^(arange(0, D, 2) / D), float32."""
     return 1.0 / (rope_theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim))

@@ -13,6 +13,7 @@ Outputs:
   reference_cases.pt  small seeded cases of write_kv, write_paged_kv,
                       read_paged_kv, copy_prefix_into_cache, the handoff and
                       fork compositions, duplicate positions in one call,
+                      decode and prefill attention over a paged cache,
                       allocator / block table / prefix-hash scripts;
   config1_writes.pt   the full Qwen2.5-0.5B-shaped random-init model (fp32,
                       CPU): 128-token prefill into new_kv_cache(max_seq_len=512)
@@ -298,6 +299,62 @@ def attention_cases(ref, g):
     return cases
 
 
+def prefill_attention_cases(ref, g):
+    """Prefill attention over a paged cache through the reference's own attention()
+    (augur/attention.py:22-92): a prefix of P tokens is prefilled first (P = 0: none),
+    then a call with the n suffix tokens (seq = n > 1), whose queries attend to the
+    prefix and causally to each other. augur's GQA shape, one layer, block size 16,
+    o-projection the identity. Stored: the suffix's rotated queries, the pool, the
+    block table and the reference output of the suffix call."""
+    import torch.nn.functional as F
+    from einops import rearrange
+
+    from augur.attention import attention
+    from augur.rope import apply_rope
+
+    P = ref.paged_kv_cache
+    W = ref.weights
+    cases = {}
+    for name, dtype, prefix, n in (("f32_prefix", torch.float32, 21, 16), ("bf16_prefix", torch.bfloat16, 200, 45),
+                                   ("bf16_plain", torch.bfloat16, 0, 37)):
+        cfg = ref.config.QwenConfig(vocab_size=16, hidden_size=896, intermediate_size=16,
+                                    num_hidden_layers=1, num_attention_heads=14, num_key_value_heads=2)
+        D, Hq, Hkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
+        w = W.Attention(
+            q=W.Linear((torch.randn(Hq * D, 896, generator=g) * 0.06).to(dtype),
+                       (torch.randn(Hq * D, generator=g) * 0.1).to(dtype)),
+            k=W.Linear((torch.randn(Hkv * D, 896, generator=g) * 0.06).to(dtype),
+                       (torch.randn(Hkv * D, generator=g) * 0.1).to(dtype)),
+            v=W.Linear((torch.randn(Hkv * D, 896, generator=g) * 0.06).to(dtype)),
+            o=W.Linear(torch.eye(896, dtype=dtype)),
+        )
+        seq = prefix + n
+        x = torch.randn(1, seq, 896, generator=g).to(dtype)
+        state = P.PagedKVCacheState(
+            cache=P.new_paged_kv_cache(cfg, num_blocks=-(-seq // 16) + 3, block_size=16,
+                                       device=torch.device("cpu"), dtype=dtype),
+            block_table=P.SequenceBlockTable.empty(block_size=16),
+        )
+        poison(state.cache.keys)
+        poison(state.cache.values)
+        state.cache.allocator.allocate()  # the pool already holds another block
+        pos = torch.arange(seq).unsqueeze(0)
+        if prefix:
+            attention(x[:, :prefix], w, cfg, pos[:, :prefix], paged_cache=state, layer_idx=0)
+        out = attention(x[:, prefix:], w, cfg, pos[:, prefix:], paged_cache=state, layer_idx=0)
+        q = rearrange(F.linear(x[:, prefix:], w.q.weight, w.q.bias),
+                      "batch seq (heads head_dim) -> batch heads seq head_dim", heads=Hq, head_dim=D)
+        k_new = rearrange(F.linear(x[:, prefix:], w.k.weight, w.k.bias),
+                          "batch seq (heads head_dim) -> batch heads seq head_dim", heads=Hkv, head_dim=D)
+        q, _ = apply_rope(q, k_new, pos[:, prefix:], cfg.rope_theta)
+        kk, vv = P.read_paged_kv(state.cache, 0, state.block_table)
+        cases[name] = {"q": q.contiguous(), "keys": state.cache.keys.clone(), "values": state.cache.values.clone(),
+                       "block_ids": list(state.block_table.block_ids), "seq_len": state.block_table.seq_len,
+                       "k": kk.clone(), "v": vv.clone(), "prefix_len": prefix, "n": n,
+                       "out": out.view(1, n, Hq, D).permute(0, 2, 1, 3).contiguous(), "n_kv_heads": Hkv}
+    return cases
+
+
 def rope_cases(ref, g):
     """apply_rope (augur/rope.py:12-40) followed by the cache write, as augur/attention.py:53-71 runs it.
 
@@ -530,6 +587,7 @@ def main() -> None:
     cases["attention"] = attention_cases(Ref, torch.Generator().manual_seed(4321))
     cases["rope"] = rope_cases(Ref, torch.Generator().manual_seed(777))
     cases["duplicates"] = duplicate_cases(Ref, torch.Generator().manual_seed(99))
+    cases["prefill_attention"] = prefill_attention_cases(Ref, torch.Generator().manual_seed(2024))
     torch.save(cases, os.path.join(HERE, "reference_cases.pt"))
     if not args.skip_config1:
         torch.save(config1(Ref), os.path.join(HERE, "config1_writes.pt"))

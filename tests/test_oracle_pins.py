@@ -351,3 +351,17 @@ def test_torch_loop_write_paged_kv_matches_golden(oracle, golden):
         assert t.block_ids == p["block_ids"]
         assert_bits_equal(pk, p["keys"], f"{name} keys")
         assert_bits_equal(pv, p["values"], f"{name} values")
+
+
+@pytest.mark.parametrize("case", ["f32_prefix", "bf16_prefix", "bf16_plain"])
+def test_golden_prefill_attention(oracle, golden, case):
+    """The oracle's prefill attention (causal mask with past_len = key_len - query_len)
+    equals the reference's own attention() for a call of several new tokens on a paged
+    cache, with and without a cached prefix; its gather equals read_paged_kv's."""
+    c = golden["prefill_attention"][case]
+    t = oracle.RefBlockTable(c["block_ids"], 16, c["seq_len"])
+    kk, vv = oracle.read_paged_kv(c["keys"], c["values"], 0, t)
+    assert_bits_equal(kk, c["k"], "gathered keys")
+    assert_bits_equal(vv, c["v"], "gathered values")
+    got = oracle.prefill_attention(c["q"], kk, vv)
+    assert_bits_equal(got, c["out"], "attention output")
