@@ -17,7 +17,7 @@
 //  * attn_prefill_mma_kernel (bf16 / fp16, head_dim 64 or 128, at most 8 query
 //    heads per KV head): one CTA per (sequence, KV head, tile of 16 query
 //    tokens), one warp per query head of the group. K and V stream through
-//    shared memory 32 keys at a time (cp.async, three stage buffers, the
+//    shared memory 64 keys at a time (cp.async, three stage buffers, the
 //    block-table entry looked up per row); S = Q K^T and O += P V run on
 //    mma.sync m16n8k16 around an online softmax in base 2. Tiles are issued
 //    longest first (the last tile of a sequence reads the most keys).
@@ -69,9 +69,21 @@ struct PrefillArgs {
 constexpr float kNegInf = -INFINITY;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kQT = 16;     // query tokens per CTA (one mma row tile)
-constexpr int kKT = 32;     // keys per stage
 constexpr int kStages = 3;  // stage buffers
 constexpr int kMaxGroups = 8;
+// Keys per stage and the resident CTAs per SM the kernel is compiled for.
+// Measured on B200 (config-4 suffix prefill: 256 x 128 query tokens over
+// 1,152 cached positions, bf16, head_dim 64, per layer): 64 keys with 2 CTAs
+// 840 us (152 TFLOP/s); 32 keys with 3 CTAs (80 registers, spills) 895 us;
+// 64 keys unbounded (165 registers, 1 CTA) 1,098 us; 32 keys unbounded
+// (139 registers) 1,366 us.
+#ifndef AUGUR_KV_PREFILL_KT
+#define AUGUR_KV_PREFILL_KT 64
+#endif
+#ifndef AUGUR_KV_PREFILL_MIN_CTAS
+#define AUGUR_KV_PREFILL_MIN_CTAS 2
+#endif
+constexpr int kKT = AUGUR_KV_PREFILL_KT;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -177,7 +189,7 @@ struct PfCfg {
 };
 
 template <typename T, int D>
-__global__ void __launch_bounds__(kMaxGroups * 32) attn_prefill_mma_kernel(PrefillArgs a) {
+__global__ void __launch_bounds__(kMaxGroups * 32, AUGUR_KV_PREFILL_MIN_CTAS) attn_prefill_mma_kernel(PrefillArgs a) {
   using CF = PfCfg<D>;
   using M = Mma<T>;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -256,24 +268,27 @@ __global__ void __launch_bounds__(kMaxGroups * 32) attn_prefill_mma_kernel(Prefi
     }
     const unsigned char* Ks = smem + (s % kStages) * CF::kStageBytes;
     const unsigned char* Vs = Ks + CF::kTileBytes;
-    // S = Q K^T: 16 tokens x 32 keys, four 8-key n-tiles
-    float sc[4][4];
+    // S = Q K^T: 16 tokens x kKT keys, 8-key n-tiles
+    constexpr int NJ = kKT / 8;
+    float sc[NJ][4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+    for (int j = 0; j < NJ; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
 #pragma unroll
     for (int ks = 0; ks < D / 16; ++ks) {
 #pragma unroll
-      for (int np = 0; np < 2; ++np) {
+      for (int np = 0; np < NJ / 2; ++np) {
         uint32_t kb[4];
         ldsm_x4(kb, Ks + (np * 16 + (mat >> 1) * 8 + r8) * CF::kRowBytes + (ks * 16 + (mat & 1) * 8) * 2);
         M::run(sc[2 * np], qa[ks], kb[0], kb[1]);
         M::run(sc[2 * np + 1], qa[ks], kb[2], kb[3]);
       }
     }
-    // round as the reference's dtype matmul and division do, to base 2, causal mask
+    // round as the reference's dtype matmul and division do, to base 2; the causal
+    // mask only where the stage's last key is past the tile's first query
+    const bool need_mask = (s + 1) * kKT - 1 > past + i0;
     float rmax[2] = {kNegInf, kNegInf};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < NJ; ++j) {
 #pragma unroll
       for (int hp = 0; hp < 2; ++hp) {
         float2 r = M::round2(sc[j][2 * hp], sc[j][2 * hp + 1]);
@@ -293,10 +308,12 @@ __global__ void __launch_bounds__(kMaxGroups * 32) attn_prefill_mma_kernel(Prefi
           x0 = r.x * scale1;
           x1 = r.y * scale1;
         }
-        const int key = s * kKT + j * 8 + 2 * t;
-        const int qp = hp ? qp1 : qp0;
-        x0 = key > qp ? kNegInf : x0;
-        x1 = key + 1 > qp ? kNegInf : x1;
+        if (need_mask) {
+          const int key = s * kKT + j * 8 + 2 * t;
+          const int qp = hp ? qp1 : qp0;
+          x0 = key > qp ? kNegInf : x0;
+          x1 = key + 1 > qp ? kNegInf : x1;
+        }
         sc[j][2 * hp] = x0;
         sc[j][2 * hp + 1] = x1;
         rmax[hp] = fmaxf(rmax[hp], fmaxf(x0, x1));
@@ -320,10 +337,10 @@ __global__ void __launch_bounds__(kMaxGroups * 32) attn_prefill_mma_kernel(Prefi
       o[j][2] *= alpha[1];
       o[j][3] *= alpha[1];
     }
-    // probabilities, rounded to the dtype, as A fragments of P (two 16-key k-steps)
-    uint32_t pa[2][4];
+    // probabilities, rounded to the dtype, as A fragments of P (16-key k-steps)
+    uint32_t pa[NJ / 2][4];
 #pragma unroll
-    for (int kk = 0; kk < 2; ++kk) {
+    for (int kk = 0; kk < NJ / 2; ++kk) {
 #pragma unroll
       for (int h2 = 0; h2 < 2; ++h2) {
         const int j = 2 * kk + h2;
@@ -337,7 +354,7 @@ __global__ void __launch_bounds__(kMaxGroups * 32) attn_prefill_mma_kernel(Prefi
     }
     // O += P V: V^T fragments by transposing loads, two 8-dim n-tiles per load
 #pragma unroll
-    for (int kk = 0; kk < 2; ++kk) {
+    for (int kk = 0; kk < NJ / 2; ++kk) {
 #pragma unroll
       for (int dn = 0; dn < D / 8; dn += 2) {
         uint32_t vb[4];
