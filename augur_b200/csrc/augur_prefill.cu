@@ -71,7 +71,9 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kQT = 16;     // query tokens per CTA (one mma row tile)
 constexpr int kStages = 3;  // stage buffers
 constexpr int kMaxGroups = 8;
-// Keys per stage and the resident CTAs per SM the kernel is compiled for.
+// Keys per stage and the resident CTAs per SM the head_dim-64 kernel is
+// compiled for (head_dim 128 is compiled for one: its accumulators need more
+// than 128 registers).
 // Measured on B200 (config-4 suffix prefill: 256 x 128 query tokens over
 // 1,152 cached positions, bf16, head_dim 64, per layer): 64 keys with 2 CTAs
 // 840 us (152 TFLOP/s); 32 keys with 3 CTAs (80 registers, spills) 895 us;
@@ -189,7 +191,8 @@ struct PfCfg {
 };
 
 template <typename T, int D>
-__global__ void __launch_bounds__(kMaxGroups * 32, AUGUR_KV_PREFILL_MIN_CTAS) attn_prefill_mma_kernel(PrefillArgs a) {
+__global__ void __launch_bounds__(kMaxGroups * 32, D == 64 ? AUGUR_KV_PREFILL_MIN_CTAS : 1)
+    attn_prefill_mma_kernel(PrefillArgs a) {
   using CF = PfCfg<D>;
   using M = Mma<T>;
   extern __shared__ __align__(128) unsigned char smem[];
