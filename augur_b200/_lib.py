@@ -31,6 +31,7 @@ COPY_FENCE_SYSTEM = 4
 
 ATTN_AUTO = 0
 ATTN_GENERIC = 1
+ATTN_MMA_SYNC = 2  # paged prefill attention: the mma.sync kernel instead of tcgen05
 
 STATUS_NAMES = {
     OK: "ok",

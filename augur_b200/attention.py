@@ -194,6 +194,7 @@ def paged_prefill_attention(
     out: Tensor | None = None,
     generic: bool = False,
     stream: torch.cuda.Stream | None = None,
+    kernel: str = "auto",
 ) -> Tensor:
     """Attention of a batch's new tokens over the pool (one layer, one launch).
 
@@ -206,8 +207,13 @@ def paged_prefill_attention(
     positions [0, that position]: a plain prefill when q_lens[b] == seq_len, the
     suffix of a prompt whose prefix blocks were shared from the prefix index
     otherwise. Returns ``[tokens, n_q_heads, head_dim]`` (heads not yet
-    concatenated). generic=True forces the CUDA-core kernel.
+    concatenated). kernel: "auto" (tcgen05 for bf16/fp16 at head_dim 64 or
+    128 with 16-byte aligned rows), "mma_sync" (the legacy tensor-core
+    kernel, same shapes) or "generic" (CUDA cores, any dtype); generic=True
+    is kernel="generic".
     """
+    if kernel not in ("auto", "mma_sync", "generic"):
+        raise ValueError("kernel must be 'auto', 'mma_sync' or 'generic'")
     if q.dim() != 3:
         raise ValueError("q must be [tokens, n_q_heads, head_dim]")
     _ops.require_cuda("paged_prefill_attention", q, cache.keys, cache.values)
@@ -244,7 +250,8 @@ def paged_prefill_attention(
     device = kc.device
     st = stream if stream is not None else torch.cuda.current_stream(device)
     q_starts = pq.starts
-    flags = _lib.ATTN_GENERIC if generic else _lib.ATTN_AUTO
+    flags = _lib.ATTN_GENERIC if generic or kernel == "generic" else (
+        _lib.ATTN_MMA_SYNC if kernel == "mma_sync" else _lib.ATTN_AUTO)
     with _ops._DeviceGuard(device):
         code = lib.augur_kv_paged_prefill_attention(
             q.data_ptr(), _lib.i64_array((q.stride(0), q.stride(1))),
@@ -266,6 +273,7 @@ def paged_attention(
     layer_idx: int,
     block_table: SequenceBlockTable,
     generic: bool = False,
+    kernel: str = "auto",
 ) -> Tensor:
     """The attention core of augur's paged branch for one sequence (augur/attention.py:72-86)
     after its write: q ``[1, n_q_heads, seq, head_dim]`` (after RoPE) attends over the
@@ -274,6 +282,6 @@ def paged_attention(
     pool is read in place (no read_paged_kv gather, no repeated KV heads)."""
     if q.dim() != 4 or q.shape[0] != 1:
         raise ValueError("paged KV cache currently supports batch size 1")
-    out = paged_prefill_attention(q[0].transpose(0, 1), cache, layer_idx, [block_table], [q.shape[2]],
-                                  generic=generic)
+    out = paged_prefill_attention(q[0].transpose(0, 1).contiguous(), cache, layer_idx, [block_table], [q.shape[2]],
+                                  generic=generic, kernel=kernel)
     return out.transpose(0, 1).unsqueeze(0)

@@ -386,6 +386,350 @@ __global__ void __launch_bounds__(kMaxGroups * 32, D == 64 ? AUGUR_KV_PREFILL_MI
 }
 
 // ---------------------------------------------------------------------------
+// tcgen05 path: the products on the 5th-generation tensor cores, accumulators
+// in tensor memory
+// ---------------------------------------------------------------------------
+//
+// One CTA (4 warps) per (sequence, KV head, tile of 16 query tokens). The MMA
+// rows are 8 head slots x 16 tokens (row = slot * 16 + token; slots past the
+// group and tokens past the sequence are zero rows, never stored), so warp w
+// owns rows (tensor-memory lanes) 32w .. 32w + 31 and each thread one row.
+// Per 64-key stage: one thread issues S = Q K^T into tensor memory (kind::f16,
+// M = 128, N = 64, four K = 16 steps) and commits it to an mbarrier; every
+// thread loads its row of S (tcgen05.ld), applies the reference's rounding,
+// the causal mask and an online softmax in base 2 with no shuffles, and
+// writes its row of P (the dtype) to shared memory; then one thread issues the
+// stage's O = P V into a second tensor-memory region, which every thread
+// loads and folds into its row of the output held in registers. Operands sit
+// in shared memory in the no-swizzle core-matrix layout (8 rows x 16 bytes per
+// core matrix): Q, K and P K-major, V MN-major as the pool stores it (its rows
+// copy in as they are). K and V are staged with cp.async, two stage buffers.
+// Every mbarrier wait is bounded (%globaltimer, 2 s); on expiry the CTA records
+// AUGUR_KV_ETIMEOUT, frees its tensor memory and returns.
+
+constexpr int kUKeys = 64;   // keys per stage
+constexpr int kURows = 128;  // MMA rows: 8 head slots x 16 tokens
+
+template <int D>
+struct UCfg {
+  static constexpr int kChunks = D / 8;  // 16-byte chunks per row of Q or K
+  static constexpr int kQBytes = kURows * D * 2;
+  static constexpr int kKVBytes = kUKeys * D * 2;  // one K or V stage
+  static constexpr int kPBytes = kURows * kUKeys * 2;
+  static constexpr int kQ = 0;
+  static constexpr int kK = kQ + kQBytes;
+  static constexpr int kV = kK + 2 * kKVBytes;
+  static constexpr int kP = kV + 2 * kKVBytes;
+  static constexpr int kBar = kP + kPBytes;  // two mbarriers, then the tensor-memory address
+  static constexpr int kBytes = kBar + 64;
+  static constexpr int kRowGroup = kChunks * 128;  // K-major Q / K: bytes between 8-row groups
+  static constexpr int kVChunk = (kUKeys / 8) * 128;  // MN-major V: bytes between 8-dim chunks
+  static constexpr uint32_t kCols = D == 64 ? 128 : 256;  // S (64 columns) + O (D columns)
+  static constexpr int kMinCtas = D == 64 ? 3 : 2;
+};
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+// Shared-memory matrix descriptor, no swizzle: start address, leading byte
+// offset (between the two K chunks of a K-major step, or between K groups of
+// an MN-major operand), stride byte offset (between 8-row groups, or between
+// MN chunks), descriptor version 1.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return uint64_t((addr & 0x3FFFFu) >> 4) | (uint64_t(lbo >> 4) << 16) | (uint64_t(sbo >> 4) << 32) |
+         (uint64_t(1) << 46);
+}
+// Instruction descriptor for kind::f16: f32 accumulator, A and B of the
+// cache dtype (bf16 = 1, f16 = 0), A K-major, B K-major or MN-major, N, M.
+template <typename T>
+__host__ __device__ constexpr uint32_t umma_idesc(int n, bool b_mn_major) {
+  return (1u << 4) | ((Mma<T>::dtype == AUGUR_KV_BF16 ? 1u : 0u) << 7) |
+         ((Mma<T>::dtype == AUGUR_KV_BF16 ? 1u : 0u) << 10) | (uint32_t(b_mn_major) << 16) |
+         (uint32_t(n >> 3) << 17) | (uint32_t(kURows >> 4) << 24);
+}
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, int count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P1;\n\tmbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, P1;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Wait for the phase with this parity to complete; false after 2 s.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (!mbar_try(bar, parity)) {
+    if (global_ns() - t0 > 2000000000ull) return false;
+  }
+  return true;
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// 32 consecutive 32-bit columns of this thread's tensor-memory lane
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(128, UCfg<D>::kMinCtas) attn_prefill_umma_kernel(PrefillArgs a) {
+  using U = UCfg<D>;
+  using M = Mma<T>;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tile = int(gridDim.x) - 1 - int(blockIdx.x);  // longest tiles first
+  const int b = blockIdx.y / a.hkv, hk = blockIdx.y - b * a.hkv;
+  int q0, n, past;
+  if (!seq_bounds(a, b, q0, n, past)) return;
+  const int i0 = tile * kQT;
+  if (i0 >= n) return;
+  const int i1 = min(n, i0 + kQT);
+  const int key_end = past + i1;
+  const int n_st = (key_end + kUKeys - 1) / kUKeys;
+  uint64_t* bar_s = reinterpret_cast<uint64_t*>(smem + U::kBar);
+  uint64_t* bar_o = bar_s + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + U::kBar + 16);
+  const uint32_t sb = smem_u32(smem);
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(U::kCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (tid == 0) {
+    mbar_init(bar_s, 1);
+    mbar_init(bar_o, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  // Q: row r = slot * 16 + token, K-major core matrices
+  for (int p = tid; p < kURows * U::kChunks; p += 128) {
+    const int r = p / U::kChunks, c = p - (p / U::kChunks) * U::kChunks;
+    const int slot = r >> 4, tok = r & 15;
+    const bool ok = slot < a.groups && i0 + tok < n;
+    const char* src = ok ? a.q + int64_t(q0 + i0 + tok) * a.q_stride_t + int64_t(hk * a.groups + slot) * a.q_stride_h +
+                               c * 16
+                         : a.q;
+    cp_async16(smem + U::kQ + (r >> 3) * U::kRowGroup + c * 128 + (r & 7) * 16, src, ok ? 16 : 0);
+  }
+  auto load_kv = [&](int s, int buf) {
+    unsigned char* kd = smem + U::kK + buf * U::kKVBytes;
+    unsigned char* vd = smem + U::kV + buf * U::kKVBytes;
+    constexpr int kPieces = kUKeys * U::kChunks;
+    for (int p = tid; p < 2 * kPieces; p += 128) {
+      const int kv = p >= kPieces;
+      const int rest = p - kv * kPieces;
+      const int row = rest / U::kChunks, c = rest - (rest / U::kChunks) * U::kChunks;
+      const int key = s * kUKeys + row;
+      const char* src = kv ? a.v : a.k;
+      int bytes = 0;
+      if (key < key_end) {
+        const char* rp = pool_row(a, src, b, hk, key);
+        if (rp != nullptr) {
+          src = rp + c * 16;
+          bytes = 16;
+        }
+      }
+      unsigned char* dst = kv ? vd + c * U::kVChunk + (row >> 3) * 128 + (row & 7) * 16
+                              : kd + (row >> 3) * U::kRowGroup + c * 128 + (row & 7) * 16;
+      cp_async16(dst, src, bytes);
+    }
+  };
+  load_kv(0, 0);
+  cp_async_commit();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_s = tmem, t_o = tmem + uint32_t(kUKeys);
+  const uint32_t my_lanes = uint32_t(warp * 32) << 16;
+  const int row = tid, slot = row >> 4, tok = row & 15;
+  const int qp = past + i0 + tok;
+  constexpr uint32_t idesc_s = umma_idesc<T>(kUKeys, false);
+  constexpr uint32_t idesc_o = umma_idesc<T>(D, true);
+  const bool round_twice = M::dtype == AUGUR_KV_F16 || !a.scale_exact;
+  const float scale1 = round_twice ? (a.scale_exact ? a.inv_sqrt_d : 1.f) : a.inv_sqrt_d * kLog2e;
+  float o[D];
+#pragma unroll
+  for (int d = 0; d < D; ++d) o[d] = 0.f;
+  float mrow = kNegInf, lrow = 0.f;
+  bool ok = true;
+  for (int s = 0; s < n_st && ok; ++s) {
+    const int buf = s & 1;
+    if (s + 1 < n_st) load_kv(s + 1, buf ^ 1);  // that buffer's last reader (stage s - 1's P V) is done
+    cp_async_commit();
+    cp_async_wait<1>();
+    fence_async_smem();  // this thread's staged rows (and P of the last stage) -> the tensor core's view
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0) {
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks)
+        umma_f16(t_s, umma_desc(sb + U::kQ + ks * 256, 128, U::kRowGroup),
+                 umma_desc(sb + U::kK + buf * U::kKVBytes + ks * 256, 128, U::kRowGroup), idesc_s, ks > 0);
+      umma_commit(bar_s);
+    }
+    ok = __syncthreads_and(mbar_wait(bar_s, uint32_t(s) & 1u));
+    if (!ok) break;
+    tc_fence_after();
+    // this row's scores: round as the reference's dtype matmul and division do,
+    // base 2, causal mask where the stage reaches past the tile's first query
+    const bool need_mask = (s + 1) * kUKeys - 1 > past + i0;
+    float sv[kUKeys];
+    {
+      float h[32];
+      tmem_ld32(t_s + my_lanes, h);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) sv[j] = h[j];
+      tmem_ld32(t_s + my_lanes + 32, h);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) sv[32 + j] = h[j];
+    }
+    float mx = kNegInf;
+#pragma unroll
+    for (int j = 0; j < kUKeys; j += 2) {
+      float2 r = M::round2(sv[j], sv[j + 1]);
+      float x0, x1;
+      if (round_twice) {
+        if (!a.scale_exact) {
+          r.x /= a.sqrt_d;
+          r.y /= a.sqrt_d;
+        } else {
+          r.x *= scale1;
+          r.y *= scale1;
+        }
+        r = M::round2(r.x, r.y);
+        x0 = r.x * kLog2e;
+        x1 = r.y * kLog2e;
+      } else {
+        x0 = r.x * scale1;
+        x1 = r.y * scale1;
+      }
+      if (need_mask) {
+        const int key = s * kUKeys + j;
+        x0 = key > qp ? kNegInf : x0;
+        x1 = key + 1 > qp ? kNegInf : x1;
+      }
+      sv[j] = x0;
+      sv[j + 1] = x1;
+      mx = fmaxf(mx, fmaxf(x0, x1));
+    }
+    const float mnew = fmaxf(mrow, mx);  // finite: stage 0 holds key 0, which every row sees
+    const float alpha = ex2(mrow - mnew);
+    mrow = mnew;
+    lrow *= alpha;
+    // P (the dtype) -> shared memory, this row's 8 K-major chunks of 8 keys
+    unsigned char* prow = smem + U::kP + (row >> 3) * 1024 + (row & 7) * 16;
+#pragma unroll
+    for (int c = 0; c < kUKeys / 8; ++c) {
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float p0 = ex2(sv[c * 8 + 2 * e] - mnew), p1 = ex2(sv[c * 8 + 2 * e + 1] - mnew);
+        lrow += p0 + p1;
+        w[e] = M::pack(p0, p1);
+      }
+      *reinterpret_cast<uint4*>(prow + c * 128) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0) {
+#pragma unroll
+      for (int kk = 0; kk < kUKeys / 16; ++kk)
+        umma_f16(t_o, umma_desc(sb + U::kP + kk * 256, 128, 1024),
+                 umma_desc(sb + U::kV + buf * U::kKVBytes + kk * 256, 128, U::kVChunk), idesc_o, kk > 0);
+      umma_commit(bar_o);
+    }
+    ok = __syncthreads_and(mbar_wait(bar_o, uint32_t(s) & 1u));
+    if (!ok) break;
+    tc_fence_after();
+#pragma unroll
+    for (int d0 = 0; d0 < D; d0 += 32) {
+      float h[32];
+      tmem_ld32(t_o + my_lanes + d0, h);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) o[d0 + j] = o[d0 + j] * alpha + h[j];
+    }
+  }
+  cp_async_wait<0>();
+  if (!ok && tid == 0) record_status(a.status, AUGUR_KV_ETIMEOUT);
+  if (ok && slot < a.groups && i0 + tok < n) {
+    const float inv = lrow > 0.f ? 1.f / lrow : 0.f;
+    char* orow = a.out + int64_t(q0 + i0 + tok) * a.out_stride_t + int64_t(hk * a.groups + slot) * a.out_stride_h;
+#pragma unroll
+    for (int c = 0; c < D / 8; ++c) {
+      uint4 w;
+      w.x = M::pack(o[c * 8 + 0] * inv, o[c * 8 + 1] * inv);
+      w.y = M::pack(o[c * 8 + 2] * inv, o[c * 8 + 3] * inv);
+      w.z = M::pack(o[c * 8 + 4] * inv, o[c * 8 + 5] * inv);
+      w.w = M::pack(o[c * 8 + 6] * inv, o[c * 8 + 7] * inv);
+      *reinterpret_cast<uint4*>(orow + c * 16) = w;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(U::kCols) : "memory");
+}
+
+template <typename T, int D>
+int launch_umma(const PrefillArgs& a, cudaStream_t st) {
+  using augur_kv_dev::fail;
+  constexpr int smem = UCfg<D>::kBytes;
+  static int attr_done[augur_kv_dev::kMaxDevices] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= augur_kv_dev::kMaxDevices)
+    return fail(AUGUR_KV_ECUDA, "paged_prefill_attention: cannot query the current device");
+  {
+    std::lock_guard<std::recursive_mutex> lock(augur_kv_dev::g_cache_mutex);
+    if (!attr_done[dev]) {
+      if (cudaFuncSetAttribute(attn_prefill_umma_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+          cudaSuccess)
+        return augur_kv_dev::check_launch("cudaFuncSetAttribute(attn_prefill_umma_kernel)");
+      attr_done[dev] = 1;
+    }
+  }
+  const dim3 grid{unsigned((a.max_q_len + kQT - 1) / kQT), unsigned(a.batch * a.hkv), 1u};
+  attn_prefill_umma_kernel<T, D><<<grid, 128u, smem, st>>>(a);
+  return augur_kv_dev::check_launch("attn_prefill_umma_kernel");
+}
+
+// ---------------------------------------------------------------------------
 // Generic path: one CTA per (query token, query head), the reference's order
 // ---------------------------------------------------------------------------
 
@@ -518,7 +862,7 @@ AUGUR_KV_EXPORT int augur_kv_paged_prefill_attention(
       num_blocks <= 0 || max_blocks <= 0 || max_q_len > max_seq_len || n_q_heads > 65535 ||
       int64_t(batch) * n_kv_heads > 65535 || max_q_len > 65535)
     return fail(AUGUR_KV_EINVAL, "paged_prefill_attention: bad sizes");
-  if (flags != AUGUR_KV_ATTN_AUTO && flags != AUGUR_KV_ATTN_GENERIC)
+  if (flags != AUGUR_KV_ATTN_AUTO && flags != AUGUR_KV_ATTN_GENERIC && flags != AUGUR_KV_ATTN_MMA_SYNC)
     return fail(AUGUR_KV_EINVAL, "paged_prefill_attention: unknown flags %d", flags);
 
   PrefillArgs a;
@@ -569,6 +913,13 @@ AUGUR_KV_EXPORT int augur_kv_paged_prefill_attention(
   const bool mma_ok = (dtype == AUGUR_KV_BF16 || dtype == AUGUR_KV_F16) && (head_dim == 64 || head_dim == 128) &&
                       a.groups <= kMaxGroups && (align & 15u) == 0 && (align4 & 3u) == 0 &&
                       a.row_stride == int64_t(head_dim) * es;
+  // tcgen05: the same shapes with q and out rows 16-byte aligned
+  const bool umma_ok = mma_ok && (align4 & 15u) == 0;
+  if (flags == AUGUR_KV_ATTN_AUTO && umma_ok) {
+    if (dtype == AUGUR_KV_BF16)
+      return head_dim == 64 ? launch_umma<__nv_bfloat16, 64>(a, st) : launch_umma<__nv_bfloat16, 128>(a, st);
+    return head_dim == 64 ? launch_umma<__half, 64>(a, st) : launch_umma<__half, 128>(a, st);
+  }
   if (flags != AUGUR_KV_ATTN_GENERIC && mma_ok) {
     if (dtype == AUGUR_KV_BF16)
       return head_dim == 64 ? launch_mma<__nv_bfloat16, 64>(a, st) : launch_mma<__nv_bfloat16, 128>(a, st);

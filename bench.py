@@ -896,7 +896,7 @@ def bench_prefill_attention(device, pool, tables, suffix: int, flush) -> dict:
     return {"seqs": B, "suffix_tokens": suffix, "cached_tokens_per_seq": seq[0], "us_per_layer": round(ms * 1e3, 2),
             "kv_GBps": round(kv_bytes / (ms / 1e3) / 1e9, 1), "kv_frac_of_hbm_peak": round(kv_bytes / (ms / 1e3) / 1e9 / peak, 4),
             "TFLOPs": round(tflops, 1), "tensor_frac": round(tflops / tf_peak, 4), "tensor_peak_source": tf_kind,
-            "kernel": "attn_prefill_mma_kernel<bf16,64> (mma.sync)",
+            "kernel": "attn_prefill_umma_kernel<bf16,64> (tcgen05, TMEM accumulators)",
             "timed": "CUDA graph of 24 per-layer launches, L2 flushed; the forks share the prefix's blocks"}
 
 

@@ -10,7 +10,7 @@ place. Checked against:
     goldens) on seeded batches: several sequences per launch, prefixes that
     end inside a block, suffixes of one token (a decode step) up to several
     16-token tiles, both head dims, GQA groups of 1 to 8 heads, bf16 / fp16
-    on the tensor-core kernel and float32 on the CUDA-core kernel;
+    on the tcgen05 and mma.sync kernels and float32 on the CUDA-core kernel;
   * a prompt admitted through PagedSequences with its prefix shared from the
     prefix index: its suffix attends to the shared blocks in place.
 Tolerance: 1e-2 for bf16 / fp16 (the reference's bf16-kernel tolerance),
@@ -37,21 +37,21 @@ def _tol(dtype):
 
 
 @pytest.mark.parametrize("case", ["f32_prefix", "bf16_prefix", "bf16_plain"])
-@pytest.mark.parametrize("generic", [False, True])
-def test_golden_prefill_attention(cuda, golden, case, generic):
+@pytest.mark.parametrize("kernel", ["auto", "mma_sync", "generic"])
+def test_golden_prefill_attention(cuda, golden, case, kernel):
     """The reference's own attention() output for a call of several tokens on a paged cache
     (its pool as the reference left it: rows never written stay 0xFF and are never read)."""
     c = golden["prefill_attention"][case]
     pool = ab.PagedKVCache(keys=c["keys"].to(cuda), values=c["values"].to(cuda), block_size=16,
                            allocator=ab.BlockAllocator(c["keys"].shape[1]))
     table = ab.SequenceBlockTable(block_ids=list(c["block_ids"]), block_size=16, seq_len=c["seq_len"])
-    out = paged_attention(c["q"].to(cuda), pool, 0, table, generic=generic)
+    out = paged_attention(c["q"].to(cuda), pool, 0, table, kernel=kernel)
     assert out.shape == c["out"].shape
     torch.testing.assert_close(out.float().cpu(), c["out"].float(), **_tol(c["q"].dtype))
     assert _ops.read_status(cuda) == _lib.OK
 
 
-def _batch(cuda, oracle, dtype, D, Hq, Hkv, prefixes, suffixes, seed, generic=False):
+def _batch(cuda, oracle, dtype, D, Hq, Hkv, prefixes, suffixes, seed, kernel="auto"):
     """Sequences with the given cached prefixes and new suffixes in one pool; the suffix
     tokens' attention from one launch against the oracle, sequence by sequence."""
     g = torch.Generator().manual_seed(seed)
@@ -72,7 +72,7 @@ def _batch(cuda, oracle, dtype, D, Hq, Hkv, prefixes, suffixes, seed, generic=Fa
     batched.write_paged_kv_batch(pool, k.to(cuda), v.to(cuda), torch.from_numpy(flat).to(cuda))
     q = torch.randn(sum(suffixes), Hq, D, generator=g).to(dtype)
     layer = 1
-    out = paged_prefill_attention(q.to(cuda), pool, layer, tables, suffixes, generic=generic)
+    out = paged_prefill_attention(q.to(cuda), pool, layer, tables, suffixes, kernel=kernel)
     assert _ops.read_status(cuda) == _lib.OK
     hk, hv = pool.keys.cpu(), pool.values.cpu()
     q0 = 0
@@ -91,20 +91,23 @@ PREFIXES = [0, 21, 200, 700, 16, 5]
 SUFFIXES = [37, 16, 45, 1, 64, 3]
 
 
+@pytest.mark.parametrize("kernel", ["auto", "mma_sync"])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("D, Hq, Hkv", [(64, 14, 2), (128, 8, 2), (64, 8, 8), (64, 16, 2)])
-def test_batch_matches_oracle(cuda, oracle, dtype, D, Hq, Hkv):
-    _batch(cuda, oracle, dtype, D, Hq, Hkv, PREFIXES, SUFFIXES, seed=D + Hq)
+def test_batch_matches_oracle(cuda, oracle, dtype, D, Hq, Hkv, kernel):
+    _batch(cuda, oracle, dtype, D, Hq, Hkv, PREFIXES, SUFFIXES, seed=D + Hq, kernel=kernel)
 
 
 def test_float32_takes_the_generic_kernel(cuda, oracle):
     _batch(cuda, oracle, torch.float32, 64, 14, 2, PREFIXES[:4], SUFFIXES[:4], seed=3)
 
 
-def test_generic_kernel_matches_the_tensor_core_kernel(cuda, oracle):
+def test_the_three_kernels_agree(cuda, oracle):
     a = _batch(cuda, oracle, torch.bfloat16, 64, 14, 2, PREFIXES, SUFFIXES, seed=9)
-    b = _batch(cuda, oracle, torch.bfloat16, 64, 14, 2, PREFIXES, SUFFIXES, seed=9, generic=True)
+    b = _batch(cuda, oracle, torch.bfloat16, 64, 14, 2, PREFIXES, SUFFIXES, seed=9, kernel="generic")
+    c = _batch(cuda, oracle, torch.bfloat16, 64, 14, 2, PREFIXES, SUFFIXES, seed=9, kernel="mma_sync")
     torch.testing.assert_close(a.float(), b.float(), rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(c.float(), b.float(), rtol=1e-2, atol=1e-2)
 
 
 def test_a_long_prefix_and_a_sequence_with_no_new_tokens(cuda, oracle):
