@@ -31,7 +31,7 @@ COPY_FENCE_SYSTEM = 4
 
 ATTN_AUTO = 0
 ATTN_GENERIC = 1
-ATTN_MMA_SYNC = 2  # paged prefill attention: the mma.sync kernel instead of tcgen05
+ATTN_TCGEN05 = 2  # paged prefill attention: the tcgen05 kernel instead of mma.sync
 
 STATUS_NAMES = {
     OK: "ok",

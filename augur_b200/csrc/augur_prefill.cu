@@ -14,6 +14,9 @@
 // cached positions (its own included) sits at position seq_len - n + i and
 // attends to positions [0, seq_len - n + i].
 //
+//  * attn_prefill_umma_kernel (on request, AUGUR_KV_ATTN_TCGEN05): the same
+//    work on the 5th-generation tensor cores, accumulators in tensor memory
+//    (described at the kernel).
 //  * attn_prefill_mma_kernel (bf16 / fp16, head_dim 64 or 128, at most 8 query
 //    heads per KV head): one CTA per (sequence, KV head, tile of 16 query
 //    tokens), one warp per query head of the group. K and V stream through
@@ -409,6 +412,8 @@ __global__ void __launch_bounds__(kMaxGroups * 32, D == 64 ? AUGUR_KV_PREFILL_MI
 
 constexpr int kUKeys = 64;   // keys per stage
 constexpr int kURows = 128;  // MMA rows: 8 head slots x 16 tokens
+constexpr int kUKV = 3;      // K/V stage buffers
+constexpr int kUP = 2;       // P buffers
 
 template <int D>
 struct UCfg {
@@ -418,14 +423,15 @@ struct UCfg {
   static constexpr int kPBytes = kURows * kUKeys * 2;
   static constexpr int kQ = 0;
   static constexpr int kK = kQ + kQBytes;
-  static constexpr int kV = kK + 2 * kKVBytes;
-  static constexpr int kP = kV + 2 * kKVBytes;
-  static constexpr int kBar = kP + kPBytes;  // two mbarriers, then the tensor-memory address
+  static constexpr int kV = kK + kUKV * kKVBytes;
+  static constexpr int kP = kV + kUKV * kKVBytes;
+  static constexpr int kRed = kP + kUP * kPBytes;  // [2][128] row maxima of the two halves, then [2][128] sums
+  static constexpr int kBar = kRed + 4 * kURows * 4;  // mbarriers (S x 2, O), then the tensor-memory address
   static constexpr int kBytes = kBar + 64;
   static constexpr int kRowGroup = kChunks * 128;  // K-major Q / K: bytes between 8-row groups
   static constexpr int kVChunk = (kUKeys / 8) * 128;  // MN-major V: bytes between 8-dim chunks
-  static constexpr uint32_t kCols = D == 64 ? 128 : 256;  // S (64 columns) + O (D columns)
-  static constexpr int kMinCtas = D == 64 ? 3 : 2;
+  static constexpr uint32_t kCols = 256;  // S x 2 (64 columns each), then O (D columns)
+  static constexpr int kMinCtas = D == 64 ? 2 : 1;  // shared memory: 96 KB / 160 KB per CTA
 };
 
 __device__ __forceinline__ uint64_t global_ns() {
@@ -502,8 +508,10 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+constexpr int kUThreads = 256;  // two threads per row: warps w and w + 4 share tensor-memory lanes 32 (w % 4) ..
+
 template <typename T, int D>
-__global__ void __launch_bounds__(128, UCfg<D>::kMinCtas) attn_prefill_umma_kernel(PrefillArgs a) {
+__global__ void __launch_bounds__(kUThreads, UCfg<D>::kMinCtas) attn_prefill_umma_kernel(PrefillArgs a) {
   using U = UCfg<D>;
   using M = Mma<T>;
   extern __shared__ __align__(1024) unsigned char smem[];
@@ -517,9 +525,9 @@ __global__ void __launch_bounds__(128, UCfg<D>::kMinCtas) attn_prefill_umma_kern
   const int i1 = min(n, i0 + kQT);
   const int key_end = past + i1;
   const int n_st = (key_end + kUKeys - 1) / kUKeys;
-  uint64_t* bar_s = reinterpret_cast<uint64_t*>(smem + U::kBar);
-  uint64_t* bar_o = bar_s + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + U::kBar + 16);
+  uint64_t* bar_s = reinterpret_cast<uint64_t*>(smem + U::kBar);  // [2]: S buffers
+  uint64_t* bar_o = bar_s + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + U::kBar + 32);
   const uint32_t sb = smem_u32(smem);
 
   if (warp == 0) {
@@ -530,11 +538,12 @@ __global__ void __launch_bounds__(128, UCfg<D>::kMinCtas) attn_prefill_umma_kern
   }
   if (tid == 0) {
     mbar_init(bar_s, 1);
+    mbar_init(bar_s + 1, 1);
     mbar_init(bar_o, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   // Q: row r = slot * 16 + token, K-major core matrices
-  for (int p = tid; p < kURows * U::kChunks; p += 128) {
+  for (int p = tid; p < kURows * U::kChunks; p += kUThreads) {
     const int r = p / U::kChunks, c = p - (p / U::kChunks) * U::kChunks;
     const int slot = r >> 4, tok = r & 15;
     const bool ok = slot < a.groups && i0 + tok < n;
@@ -547,7 +556,7 @@ __global__ void __launch_bounds__(128, UCfg<D>::kMinCtas) attn_prefill_umma_kern
     unsigned char* kd = smem + U::kK + buf * U::kKVBytes;
     unsigned char* vd = smem + U::kV + buf * U::kKVBytes;
     constexpr int kPieces = kUKeys * U::kChunks;
-    for (int p = tid; p < 2 * kPieces; p += 128) {
+    for (int p = tid; p < 2 * kPieces; p += kUThreads) {
       const int kv = p >= kPieces;
       const int rest = p - kv * kPieces;
       const int row = rest / U::kChunks, c = rest - (rest / U::kChunks) * U::kChunks;
@@ -566,60 +575,75 @@ __global__ void __launch_bounds__(128, UCfg<D>::kMinCtas) attn_prefill_umma_kern
       cp_async16(dst, src, bytes);
     }
   };
+  constexpr uint32_t idesc_s = umma_idesc<T>(kUKeys, false);
+  constexpr uint32_t idesc_o = umma_idesc<T>(D, true);
+  auto issue_s = [&](int s, uint32_t t_dst) {  // one thread: S_s = Q K_s^T, then arrive on bar_s[s & 1]
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks)
+      umma_f16(t_dst, umma_desc(sb + U::kQ + ks * 256, 128, U::kRowGroup),
+               umma_desc(sb + U::kK + (s % kUKV) * U::kKVBytes + ks * 256, 128, U::kRowGroup), idesc_s, ks > 0);
+    umma_commit(bar_s + (s & 1));
+  };
   load_kv(0, 0);
-  cp_async_commit();
+  cp_async_commit();  // Q and stage 0
+  if (n_st > 1) load_kv(1, 1);
+  cp_async_commit();  // stage 1
+  cp_async_wait<1>();
+  fence_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_s = tmem, t_o = tmem + uint32_t(kUKeys);
-  const uint32_t my_lanes = uint32_t(warp * 32) << 16;
-  const int row = tid, slot = row >> 4, tok = row & 15;
+  const uint32_t t_o = tmem + 2 * uint32_t(kUKeys);
+  const int half = warp >> 2;  // this thread's 32 keys of each stage and D / 2 output dims
+  const uint32_t my_lanes = uint32_t((warp & 3) * 32) << 16;
+  if (tid == 0) issue_s(0, tmem);
+  const int row = (warp & 3) * 32 + (tid & 31), slot = row >> 4, tok = row & 15;
+  float* red_m = reinterpret_cast<float*>(smem + U::kRed);  // [2][128]
+  float* red_l = red_m + 2 * kURows;                        // [2][128]
   const int qp = past + i0 + tok;
-  constexpr uint32_t idesc_s = umma_idesc<T>(kUKeys, false);
-  constexpr uint32_t idesc_o = umma_idesc<T>(D, true);
   const bool round_twice = M::dtype == AUGUR_KV_F16 || !a.scale_exact;
   const float scale1 = round_twice ? (a.scale_exact ? a.inv_sqrt_d : 1.f) : a.inv_sqrt_d * kLog2e;
-  float o[D];
+  constexpr int DH = D / 2;  // output dims of this thread
+  float o[DH];
 #pragma unroll
-  for (int d = 0; d < D; ++d) o[d] = 0.f;
-  float mrow = kNegInf, lrow = 0.f;
+  for (int d = 0; d < DH; ++d) o[d] = 0.f;
+  float mrow = kNegInf, lrow = 0.f, alpha_prev = 0.f;
   bool ok = true;
-  for (int s = 0; s < n_st && ok; ++s) {
-    const int buf = s & 1;
-    if (s + 1 < n_st) load_kv(s + 1, buf ^ 1);  // that buffer's last reader (stage s - 1's P V) is done
-    cp_async_commit();
-    cp_async_wait<1>();
-    fence_async_smem();  // this thread's staged rows (and P of the last stage) -> the tensor core's view
+  // fold the previous stage's P V (in tensor memory) into the output row
+  auto fold = [&](int s_done) -> bool {
+    if (!__syncthreads_and(mbar_wait(bar_o, uint32_t(s_done) & 1u))) return false;
+    tc_fence_after();
+#pragma unroll
+    for (int d0 = 0; d0 < DH; d0 += 32) {
+      float h[32];
+      tmem_ld32(t_o + my_lanes + half * DH + d0, h);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) o[d0 + j] = o[d0 + j] * alpha_prev + h[j];
+    }
+    return true;
+  };
+  for (int s = 0; s < n_st; ++s) {
+    // stage s + 1's rows have landed: its S goes to the tensor core while this
+    // stage's softmax runs
+    if (s + 1 < n_st) cp_async_wait<0>();
+    fence_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (tid == 0) {
-#pragma unroll
-      for (int ks = 0; ks < D / 16; ++ks)
-        umma_f16(t_s, umma_desc(sb + U::kQ + ks * 256, 128, U::kRowGroup),
-                 umma_desc(sb + U::kK + buf * U::kKVBytes + ks * 256, 128, U::kRowGroup), idesc_s, ks > 0);
-      umma_commit(bar_s);
-    }
-    ok = __syncthreads_and(mbar_wait(bar_s, uint32_t(s) & 1u));
+    if (tid == 0 && s + 1 < n_st) issue_s(s + 1, tmem + uint32_t((s + 1) & 1) * kUKeys);
+    ok = __syncthreads_and(mbar_wait(bar_s + (s & 1), uint32_t(s >> 1) & 1u));
     if (!ok) break;
     tc_fence_after();
     // this row's scores: round as the reference's dtype matmul and division do,
     // base 2, causal mask where the stage reaches past the tile's first query
     const bool need_mask = (s + 1) * kUKeys - 1 > past + i0;
-    float sv[kUKeys];
-    {
-      float h[32];
-      tmem_ld32(t_s + my_lanes, h);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) sv[j] = h[j];
-      tmem_ld32(t_s + my_lanes + 32, h);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) sv[32 + j] = h[j];
-    }
+    constexpr int KH = kUKeys / 2;  // this thread's keys of the stage
+    float sv[KH];
+    tmem_ld32(tmem + uint32_t(s & 1) * kUKeys + my_lanes + half * KH, sv);
     float mx = kNegInf;
 #pragma unroll
-    for (int j = 0; j < kUKeys; j += 2) {
+    for (int j = 0; j < KH; j += 2) {
       float2 r = M::round2(sv[j], sv[j + 1]);
       float x0, x1;
       if (round_twice) {
@@ -638,7 +662,7 @@ __global__ void __launch_bounds__(128, UCfg<D>::kMinCtas) attn_prefill_umma_kern
         x1 = r.y * scale1;
       }
       if (need_mask) {
-        const int key = s * kUKeys + j;
+        const int key = s * kUKeys + half * KH + j;
         x0 = key > qp ? kNegInf : x0;
         x1 = key + 1 > qp ? kNegInf : x1;
       }
@@ -646,14 +670,19 @@ __global__ void __launch_bounds__(128, UCfg<D>::kMinCtas) attn_prefill_umma_kern
       sv[j + 1] = x1;
       mx = fmaxf(mx, fmaxf(x0, x1));
     }
+    // the row's maximum over both halves (red_m is rewritten only after the
+    // next stage's first barrier, when both halves have read it)
+    red_m[half * kURows + row] = mx;
+    __syncthreads();
+    mx = fmaxf(red_m[row], red_m[kURows + row]);
     const float mnew = fmaxf(mrow, mx);  // finite: stage 0 holds key 0, which every row sees
     const float alpha = ex2(mrow - mnew);
     mrow = mnew;
     lrow *= alpha;
-    // P (the dtype) -> shared memory, this row's 8 K-major chunks of 8 keys
-    unsigned char* prow = smem + U::kP + (row >> 3) * 1024 + (row & 7) * 16;
+    // P (the dtype) -> P buffer s & 1 (its last reader, P V of stage s - 2, is done)
+    unsigned char* prow = smem + U::kP + (s & 1) * U::kPBytes + (row >> 3) * 1024 + (row & 7) * 16 + half * 4 * 128;
 #pragma unroll
-    for (int c = 0; c < kUKeys / 8; ++c) {
+    for (int c = 0; c < KH / 8; ++c) {
       uint32_t w[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -663,6 +692,9 @@ __global__ void __launch_bounds__(128, UCfg<D>::kMinCtas) attn_prefill_umma_kern
       }
       *reinterpret_cast<uint4*>(prow + c * 128) = make_uint4(w[0], w[1], w[2], w[3]);
     }
+    // the previous stage's P V is folded before this stage's overwrites its accumulator
+    if (s > 0 && !(ok = fold(s - 1))) break;
+    alpha_prev = alpha;
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
@@ -670,28 +702,26 @@ __global__ void __launch_bounds__(128, UCfg<D>::kMinCtas) attn_prefill_umma_kern
     if (tid == 0) {
 #pragma unroll
       for (int kk = 0; kk < kUKeys / 16; ++kk)
-        umma_f16(t_o, umma_desc(sb + U::kP + kk * 256, 128, 1024),
-                 umma_desc(sb + U::kV + buf * U::kKVBytes + kk * 256, 128, U::kVChunk), idesc_o, kk > 0);
+        umma_f16(t_o, umma_desc(sb + U::kP + (s & 1) * U::kPBytes + kk * 256, 128, 1024),
+                 umma_desc(sb + U::kV + (s % kUKV) * U::kKVBytes + kk * 256, 128, U::kVChunk), idesc_o, kk > 0);
       umma_commit(bar_o);
     }
-    ok = __syncthreads_and(mbar_wait(bar_o, uint32_t(s) & 1u));
-    if (!ok) break;
-    tc_fence_after();
-#pragma unroll
-    for (int d0 = 0; d0 < D; d0 += 32) {
-      float h[32];
-      tmem_ld32(t_o + my_lanes + d0, h);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) o[d0 + j] = o[d0 + j] * alpha + h[j];
-    }
+    // stage s + 2 into the buffer of stage s - 1 (its S and P V are done)
+    if (s + 2 < n_st) load_kv(s + 2, (s + 2) % kUKV);
+    cp_async_commit();
   }
+  if (ok) ok = fold(n_st - 1);
   cp_async_wait<0>();
   if (!ok && tid == 0) record_status(a.status, AUGUR_KV_ETIMEOUT);
+  red_l[half * kURows + row] = lrow;  // both halves' sums share one maximum per stage
+  __syncthreads();
+  lrow = red_l[row] + red_l[kURows + row];
   if (ok && slot < a.groups && i0 + tok < n) {
     const float inv = lrow > 0.f ? 1.f / lrow : 0.f;
-    char* orow = a.out + int64_t(q0 + i0 + tok) * a.out_stride_t + int64_t(hk * a.groups + slot) * a.out_stride_h;
+    char* orow = a.out + int64_t(q0 + i0 + tok) * a.out_stride_t + int64_t(hk * a.groups + slot) * a.out_stride_h +
+                 half * DH * 2;
 #pragma unroll
-    for (int c = 0; c < D / 8; ++c) {
+    for (int c = 0; c < DH / 8; ++c) {
       uint4 w;
       w.x = M::pack(o[c * 8 + 0] * inv, o[c * 8 + 1] * inv);
       w.y = M::pack(o[c * 8 + 2] * inv, o[c * 8 + 3] * inv);
@@ -725,7 +755,7 @@ int launch_umma(const PrefillArgs& a, cudaStream_t st) {
     }
   }
   const dim3 grid{unsigned((a.max_q_len + kQT - 1) / kQT), unsigned(a.batch * a.hkv), 1u};
-  attn_prefill_umma_kernel<T, D><<<grid, 128u, smem, st>>>(a);
+  attn_prefill_umma_kernel<T, D><<<grid, unsigned(kUThreads), smem, st>>>(a);
   return augur_kv_dev::check_launch("attn_prefill_umma_kernel");
 }
 
@@ -862,7 +892,7 @@ AUGUR_KV_EXPORT int augur_kv_paged_prefill_attention(
       num_blocks <= 0 || max_blocks <= 0 || max_q_len > max_seq_len || n_q_heads > 65535 ||
       int64_t(batch) * n_kv_heads > 65535 || max_q_len > 65535)
     return fail(AUGUR_KV_EINVAL, "paged_prefill_attention: bad sizes");
-  if (flags != AUGUR_KV_ATTN_AUTO && flags != AUGUR_KV_ATTN_GENERIC && flags != AUGUR_KV_ATTN_MMA_SYNC)
+  if (flags != AUGUR_KV_ATTN_AUTO && flags != AUGUR_KV_ATTN_GENERIC && flags != AUGUR_KV_ATTN_TCGEN05)
     return fail(AUGUR_KV_EINVAL, "paged_prefill_attention: unknown flags %d", flags);
 
   PrefillArgs a;
@@ -913,14 +943,20 @@ AUGUR_KV_EXPORT int augur_kv_paged_prefill_attention(
   const bool mma_ok = (dtype == AUGUR_KV_BF16 || dtype == AUGUR_KV_F16) && (head_dim == 64 || head_dim == 128) &&
                       a.groups <= kMaxGroups && (align & 15u) == 0 && (align4 & 3u) == 0 &&
                       a.row_stride == int64_t(head_dim) * es;
-  // tcgen05: the same shapes with q and out rows 16-byte aligned
+  // tcgen05 (on request): the same shapes with q and out rows 16-byte aligned.
+  // AUTO takes the mma.sync kernel, measured faster on the config-4 suffix
+  // prefill (840 against 961 us per layer).
   const bool umma_ok = mma_ok && (align4 & 15u) == 0;
-  if (flags == AUGUR_KV_ATTN_AUTO && umma_ok) {
+  if (flags == AUGUR_KV_ATTN_TCGEN05) {
+    if (!umma_ok)
+      return fail(AUGUR_KV_EINVAL,
+                  "paged_prefill_attention: the tcgen05 kernel needs bf16/fp16, head_dim 64 or 128, <= 8 query "
+                  "heads per KV head and 16-byte aligned rows");
     if (dtype == AUGUR_KV_BF16)
       return head_dim == 64 ? launch_umma<__nv_bfloat16, 64>(a, st) : launch_umma<__nv_bfloat16, 128>(a, st);
     return head_dim == 64 ? launch_umma<__half, 64>(a, st) : launch_umma<__half, 128>(a, st);
   }
-  if (flags != AUGUR_KV_ATTN_GENERIC && mma_ok) {
+  if (flags == AUGUR_KV_ATTN_AUTO && mma_ok) {
     if (dtype == AUGUR_KV_BF16)
       return head_dim == 64 ? launch_mma<__nv_bfloat16, 64>(a, st) : launch_mma<__nv_bfloat16, 128>(a, st);
     return head_dim == 64 ? launch_mma<__half, 64>(a, st) : launch_mma<__half, 128>(a, st);
