@@ -926,6 +926,27 @@ def run_prefill_attention_only(device) -> dict:
                                                                         kernel="tcgen05")}
 
 
+def run_cow_only(device) -> dict:
+    """Profiling case: config 4's 1,000-token prefix (62 full blocks + 8 rows) forked 256
+    ways, the copy-on-write of its partial last block, then the COW launch timed alone."""
+    import augur_b200 as ab
+    from augur_b200 import batched
+
+    NB = 8192
+    pool = ab.PagedKVCache(keys=torch.empty(L, NB, H, BS, D, dtype=torch.bfloat16, device=device),
+                           values=torch.empty(L, NB, H, BS, D, dtype=torch.bfloat16, device=device),
+                           block_size=BS, allocator=ab.BlockAllocator(NB))
+    g = torch.Generator(device=device).manual_seed(4)
+    parent = ab.SequenceBlockTable.empty(BS)
+    sm = batched.prefill_slot_mapping([parent], [1000], pool.allocator)[0]
+    pk = torch.randn(L, 1000, H, D, generator=g, device=device).to(torch.bfloat16)
+    batched.write_paged_kv_batch(pool, pk, pk, torch.from_numpy(sm).to(device))
+    forks = batched.fork_prefix(pool, parent, 256)
+    copied = batched.cow_partial_blocks(pool, forks)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    return {"cow_blocks": copied, **bench_cow_device(device, pool, parent, forks, 1000, flush)}
+
+
 def bench_cow_device(device, pool, parent, forks, prefix_len: int, flush) -> dict:
     """The copy-on-write launch alone: the parent's partial block copied into every fork's
     private block (all layers, K and V), replayed from a CUDA graph with L2 flushed before
@@ -1575,6 +1596,8 @@ def main() -> None:
                     help="profiling case: decode attention over 128 box-length sequences (about 2.2 GB)")
     ap.add_argument("--offload-only", action="store_true",
                     help="config-3 cache, then offload to pinned host memory and restore")
+    ap.add_argument("--cow-only", action="store_true",
+                    help="profiling case: config-4 fork of a 1000-token prefix, then the copy-on-write launch")
     ap.add_argument("--prefill-attention-only", action="store_true",
                     help="profiling case: config-4 forks, then the suffix prefill attention")
     ap.add_argument("--rope-only", action="store_true",
@@ -1601,6 +1624,10 @@ def main() -> None:
     if args.offload_only:  # config-3 pool, then offload to pinned host memory and restore
         torch.cuda.set_device(0)
         emit(run_extras(torch.device("cuda", 0), offload_only=True))
+        return
+    if args.cow_only:  # profiling case: config-4 fork, then the copy-on-write launch
+        torch.cuda.set_device(0)
+        emit(run_cow_only(torch.device("cuda", 0)))
         return
     if args.prefill_attention_only:  # profiling case: config-4 forks, then the suffix prefill attention
         torch.cuda.set_device(0)
