@@ -362,7 +362,9 @@ def copy_blocks(
     runs[:, 0] = np.asarray(src_blocks, np.int64)
     runs[:, 2] = np.asarray(dst_blocks, np.int64)
     runs[:, 4] = rows
-    max_rows = _run_max_rows(cache.keys, bs)
+    # the longest run bounds the copy's rows (short copy-on-write runs let the
+    # kernel give each warp several planes)
+    max_rows = min(_run_max_rows(cache.keys, bs), max(1, int(rows.max())))
     runs_t = _to_device_runs(split_runs(runs, max_rows), cache.keys.device)
     copy_runs_between(cache.keys, cache.values, "paged", cache.keys, cache.values, "paged", runs_t,
                       max_rows, flags=flags, stream=stream)

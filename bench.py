@@ -959,7 +959,7 @@ def bench_cow_device(device, pool, parent, forks, prefix_len: int, flush) -> dic
     runs[:, 0] = parent.block_ids[j]
     runs[:, 2] = [f.block_ids[j] for f in forks]
     runs[:, 4] = r
-    max_rows = batched._run_max_rows(pool.keys, BS)
+    max_rows = min(batched._run_max_rows(pool.keys, BS), r)  # as copy_blocks bounds them
     runs_t = batched._to_device_runs(batched.split_runs(runs, max_rows), device)
 
     def cow() -> None:

@@ -197,6 +197,31 @@ def test_copy_blocks_vs_oracle(cuda, oracle, flags):
     assert_bits_equal(pool.values, ev, "values")
 
 
+@pytest.mark.parametrize("L, H, D, dtype", [(3, 2, 64, torch.bfloat16), (3, 1, 64, torch.bfloat16),
+                                           (5, 2, 128, torch.float32)])
+def test_short_runs_take_several_planes_per_warp(cuda, oracle, L, H, D, dtype):
+    """Runs of at most 1 KB per plane (copy-on-write of partly filled blocks): each warp
+    copies its run for several (layer, K/V, head) planes; plane counts that do and do not
+    divide by four."""
+    g = torch.Generator().manual_seed(7)
+    NB, bs = 48, 16
+    pool = _pool(L, NB, H, bs, D, dtype, cuda)
+    init_k, init_v = _rand((L, NB, H, bs, D), dtype, g), _rand((L, NB, H, bs, D), dtype, g)
+    pool.keys.copy_(init_k)
+    pool.values.copy_(init_v)
+    max_rows = 1024 // (D * init_k.element_size())
+    rng = np.random.default_rng(7)
+    src = rng.choice(NB // 2, size=20, replace=False).tolist()
+    dst = (NB // 2 + rng.choice(NB // 2, size=20, replace=False)).tolist()
+    rows = rng.integers(1, max_rows + 1, size=20).tolist()
+    batched.copy_blocks(pool, src, dst, rows)
+    ek, ev = init_k.clone(), init_v.clone()
+    oracle.copy_runs(init_k, init_v, ek, ev, np.array([[s, 0, d, 0, r] for s, d, r in zip(src, dst, rows)]))
+    assert_bits_equal(pool.keys, ek, "keys")
+    assert_bits_equal(pool.values, ev, "values")
+    assert _ops.read_status(cuda) == _lib.OK
+
+
 def test_conversion_special_values_vs_oracle(cuda, oracle):
     """f32 -> bf16 / f16 through write_paged_kv: RNE rounding, signed zero, inf, subnormals, ties."""
     vals = torch.tensor([0.0, -0.0, 1.0, -1.0, float("inf"), -float("inf"), 1e-40, -3e-39, 65504.0,
