@@ -31,7 +31,8 @@ COPY_FENCE_SYSTEM = 4
 
 ATTN_AUTO = 0
 ATTN_GENERIC = 1
-ATTN_TCGEN05 = 2  # paged prefill attention: the tcgen05 kernel instead of mma.sync
+ATTN_TCGEN05 = 2  # paged prefill attention: force the tcgen05 kernel
+ATTN_MMA_SYNC = 3  # paged prefill attention: force the mma.sync kernel
 
 STATUS_NAMES = {
     OK: "ok",

@@ -207,14 +207,15 @@ def paged_prefill_attention(
     positions [0, that position]: a plain prefill when q_lens[b] == seq_len, the
     suffix of a prompt whose prefix blocks were shared from the prefix index
     otherwise. Returns ``[tokens, n_q_heads, head_dim]`` (heads not yet
-    concatenated). kernel: "auto" (the mma.sync tensor-core kernel for
-    bf16/fp16 at head_dim 64 or 128, CUDA cores otherwise), "tcgen05" (the
-    5th-generation tensor cores with accumulators in tensor memory; same
-    shapes, 16-byte aligned rows) or "generic" (CUDA cores, any dtype);
-    generic=True is kernel="generic".
+    concatenated). kernel: "auto" (the 5th-generation tensor cores with
+    accumulators in tensor memory for bf16/fp16 at head_dim 64 or 128 with
+    16-byte aligned rows, the mma.sync kernel for those shapes otherwise, CUDA
+    cores for the rest), "tcgen05" or "mma_sync" (force one tensor-core
+    kernel) or "generic" (CUDA cores, any dtype); generic=True is
+    kernel="generic".
     """
-    if kernel not in ("auto", "tcgen05", "generic"):
-        raise ValueError("kernel must be 'auto', 'tcgen05' or 'generic'")
+    if kernel not in ("auto", "tcgen05", "mma_sync", "generic"):
+        raise ValueError("kernel must be 'auto', 'tcgen05', 'mma_sync' or 'generic'")
     if q.dim() != 3:
         raise ValueError("q must be [tokens, n_q_heads, head_dim]")
     _ops.require_cuda("paged_prefill_attention", q, cache.keys, cache.values)
@@ -251,8 +252,8 @@ def paged_prefill_attention(
     device = kc.device
     st = stream if stream is not None else torch.cuda.current_stream(device)
     q_starts = pq.starts
-    flags = _lib.ATTN_GENERIC if generic or kernel == "generic" else (
-        _lib.ATTN_TCGEN05 if kernel == "tcgen05" else _lib.ATTN_AUTO)
+    flags = _lib.ATTN_GENERIC if generic or kernel == "generic" else {
+        "tcgen05": _lib.ATTN_TCGEN05, "mma_sync": _lib.ATTN_MMA_SYNC}.get(kernel, _lib.ATTN_AUTO)
     with _ops._DeviceGuard(device):
         code = lib.augur_kv_paged_prefill_attention(
             q.data_ptr(), _lib.i64_array((q.stride(0), q.stride(1))),

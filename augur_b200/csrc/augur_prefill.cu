@@ -14,10 +14,12 @@
 // cached positions (its own included) sits at position seq_len - n + i and
 // attends to positions [0, seq_len - n + i].
 //
-//  * attn_prefill_umma_kernel (on request, AUGUR_KV_ATTN_TCGEN05): the same
-//    work on the 5th-generation tensor cores, accumulators in tensor memory
-//    (described at the kernel).
-//  * attn_prefill_mma_kernel (bf16 / fp16, head_dim 64 or 128, at most 8 query
+//  * attn_prefill_umma_kernel (bf16 / fp16, head_dim 64 or 128, at most 8
+//    query heads per KV head, 16-byte aligned rows): the work on the
+//    5th-generation tensor cores, accumulators in tensor memory (described at
+//    the kernel).
+//  * attn_prefill_mma_kernel (the same shapes when q / out rows are only
+//    4-byte aligned, or on request; bf16 / fp16, head_dim 64 or 128, at most 8 query
 //    heads per KV head): one CTA per (sequence, KV head, tile of 16 query
 //    tokens), one warp per query head of the group. K and V stream through
 //    shared memory 64 keys at a time (cp.async, three stage buffers, the
@@ -198,7 +200,7 @@ __global__ void __launch_bounds__(kMaxGroups * 32, D == 64 ? AUGUR_KV_PREFILL_MI
     attn_prefill_mma_kernel(PrefillArgs a) {
   using CF = PfCfg<D>;
   using M = Mma<T>;
-  extern __shared__ __align__(128) unsigned char smem[];
+  extern __shared__ __align__(1024) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int tile = int(gridDim.x) - 1 - int(blockIdx.x);  // longest tiles first
   const int b = blockIdx.y / a.hkv, hk = blockIdx.y - b * a.hkv;
@@ -555,24 +557,23 @@ __global__ void __launch_bounds__(kUThreads, UCfg<D>::kMinCtas) attn_prefill_umm
   auto load_kv = [&](int s, int buf) {
     unsigned char* kd = smem + U::kK + buf * U::kKVBytes;
     unsigned char* vd = smem + U::kV + buf * U::kKVBytes;
-    constexpr int kPieces = kUKeys * U::kChunks;
-    for (int p = tid; p < 2 * kPieces; p += kUThreads) {
-      const int kv = p >= kPieces;
-      const int rest = p - kv * kPieces;
-      const int row = rest / U::kChunks, c = rest - (rest / U::kChunks) * U::kChunks;
+    // 2 x 64 rows (K then V), each split into two halves of kChunks / 2 pieces:
+    // one block-table lookup per half row
+    constexpr int kHalfChunks = U::kChunks / 2;
+    for (int w = tid; w < 2 * kUKeys * 2; w += kUThreads) {
+      const int kv = w >= 2 * kUKeys;
+      const int rw = w - kv * 2 * kUKeys;
+      const int row = rw >> 1, c0 = (rw & 1) * kHalfChunks;
       const int key = s * kUKeys + row;
-      const char* src = kv ? a.v : a.k;
-      int bytes = 0;
-      if (key < key_end) {
-        const char* rp = pool_row(a, src, b, hk, key);
-        if (rp != nullptr) {
-          src = rp + c * 16;
-          bytes = 16;
-        }
+      const char* rp = key < key_end ? pool_row(a, kv ? a.v : a.k, b, hk, key) : nullptr;
+      const char* src = rp != nullptr ? rp : a.k;
+      const int bytes = rp != nullptr ? 16 : 0;
+#pragma unroll
+      for (int c = c0; c < c0 + kHalfChunks; ++c) {
+        unsigned char* dst = kv ? vd + c * U::kVChunk + (row >> 3) * 128 + (row & 7) * 16
+                                : kd + (row >> 3) * U::kRowGroup + c * 128 + (row & 7) * 16;
+        cp_async16(dst, src + (bytes ? c * 16 : 0), bytes);
       }
-      unsigned char* dst = kv ? vd + c * U::kVChunk + (row >> 3) * 128 + (row & 7) * 16
-                              : kd + (row >> 3) * U::kRowGroup + c * 128 + (row & 7) * 16;
-      cp_async16(dst, src, bytes);
     }
   };
   constexpr uint32_t idesc_s = umma_idesc<T>(kUKeys, false);
@@ -612,7 +613,7 @@ __global__ void __launch_bounds__(kUThreads, UCfg<D>::kMinCtas) attn_prefill_umm
   bool ok = true;
   // fold the previous stage's P V (in tensor memory) into the output row
   auto fold = [&](int s_done) -> bool {
-    if (!__syncthreads_and(mbar_wait(bar_o, uint32_t(s_done) & 1u))) return false;
+    if (!__syncthreads_and(tid != 0 || mbar_wait(bar_o, uint32_t(s_done) & 1u))) return false;
     tc_fence_after();
 #pragma unroll
     for (int d0 = 0; d0 < DH; d0 += 32) {
@@ -632,7 +633,8 @@ __global__ void __launch_bounds__(kUThreads, UCfg<D>::kMinCtas) attn_prefill_umm
     __syncthreads();
     tc_fence_after();
     if (tid == 0 && s + 1 < n_st) issue_s(s + 1, tmem + uint32_t((s + 1) & 1) * kUKeys);
-    ok = __syncthreads_and(mbar_wait(bar_s + (s & 1), uint32_t(s >> 1) & 1u));
+    // one thread waits on the mbarrier; the others sleep at the CTA barrier
+    ok = __syncthreads_and(tid != 0 || mbar_wait(bar_s + (s & 1), uint32_t(s >> 1) & 1u));
     if (!ok) break;
     tc_fence_after();
     // this row's scores: round as the reference's dtype matmul and division do,
@@ -892,7 +894,8 @@ AUGUR_KV_EXPORT int augur_kv_paged_prefill_attention(
       num_blocks <= 0 || max_blocks <= 0 || max_q_len > max_seq_len || n_q_heads > 65535 ||
       int64_t(batch) * n_kv_heads > 65535 || max_q_len > 65535)
     return fail(AUGUR_KV_EINVAL, "paged_prefill_attention: bad sizes");
-  if (flags != AUGUR_KV_ATTN_AUTO && flags != AUGUR_KV_ATTN_GENERIC && flags != AUGUR_KV_ATTN_TCGEN05)
+  if (flags != AUGUR_KV_ATTN_AUTO && flags != AUGUR_KV_ATTN_GENERIC && flags != AUGUR_KV_ATTN_TCGEN05 &&
+      flags != AUGUR_KV_ATTN_MMA_SYNC)
     return fail(AUGUR_KV_EINVAL, "paged_prefill_attention: unknown flags %d", flags);
 
   PrefillArgs a;
@@ -943,11 +946,11 @@ AUGUR_KV_EXPORT int augur_kv_paged_prefill_attention(
   const bool mma_ok = (dtype == AUGUR_KV_BF16 || dtype == AUGUR_KV_F16) && (head_dim == 64 || head_dim == 128) &&
                       a.groups <= kMaxGroups && (align & 15u) == 0 && (align4 & 3u) == 0 &&
                       a.row_stride == int64_t(head_dim) * es;
-  // tcgen05 (on request): the same shapes with q and out rows 16-byte aligned.
-  // AUTO takes the mma.sync kernel, measured faster on the config-4 suffix
-  // prefill (840 against 961 us per layer).
+  // tcgen05: the same shapes with q and out rows 16-byte aligned (AUTO takes
+  // it when it can: 805 against 840 us per layer for mma.sync on the config-4
+  // suffix prefill)
   const bool umma_ok = mma_ok && (align4 & 15u) == 0;
-  if (flags == AUGUR_KV_ATTN_TCGEN05) {
+  if (flags == AUGUR_KV_ATTN_TCGEN05 || (flags == AUGUR_KV_ATTN_AUTO && umma_ok)) {
     if (!umma_ok)
       return fail(AUGUR_KV_EINVAL,
                   "paged_prefill_attention: the tcgen05 kernel needs bf16/fp16, head_dim 64 or 128, <= 8 query "
@@ -956,7 +959,11 @@ AUGUR_KV_EXPORT int augur_kv_paged_prefill_attention(
       return head_dim == 64 ? launch_umma<__nv_bfloat16, 64>(a, st) : launch_umma<__nv_bfloat16, 128>(a, st);
     return head_dim == 64 ? launch_umma<__half, 64>(a, st) : launch_umma<__half, 128>(a, st);
   }
-  if (flags == AUGUR_KV_ATTN_AUTO && mma_ok) {
+  if (flags == AUGUR_KV_ATTN_MMA_SYNC && !mma_ok)
+    return fail(AUGUR_KV_EINVAL,
+                "paged_prefill_attention: the mma.sync kernel needs bf16/fp16, head_dim 64 or 128, <= 8 query "
+                "heads per KV head and aligned rows");
+  if ((flags == AUGUR_KV_ATTN_AUTO || flags == AUGUR_KV_ATTN_MMA_SYNC) && mma_ok) {
     if (dtype == AUGUR_KV_BF16)
       return head_dim == 64 ? launch_mma<__nv_bfloat16, 64>(a, st) : launch_mma<__nv_bfloat16, 128>(a, st);
     return head_dim == 64 ? launch_mma<__half, 64>(a, st) : launch_mma<__half, 128>(a, st);

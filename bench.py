@@ -896,8 +896,8 @@ def bench_prefill_attention(device, pool, tables, suffix: int, flush, kernel: st
     return {"seqs": B, "suffix_tokens": suffix, "cached_tokens_per_seq": seq[0], "us_per_layer": round(ms * 1e3, 2),
             "kv_GBps": round(kv_bytes / (ms / 1e3) / 1e9, 1), "kv_frac_of_hbm_peak": round(kv_bytes / (ms / 1e3) / 1e9 / peak, 4),
             "TFLOPs": round(tflops, 1), "tensor_frac": round(tflops / tf_peak, 4), "tensor_peak_source": tf_kind,
-            "kernel": ("attn_prefill_umma_kernel<bf16,64> (tcgen05, TMEM accumulators)" if kernel == "tcgen05"
-                       else "attn_prefill_mma_kernel<bf16,64> (mma.sync)"),
+            "kernel": ("attn_prefill_mma_kernel<bf16,64> (mma.sync)" if kernel == "mma_sync"
+                       else "attn_prefill_umma_kernel<bf16,64> (tcgen05, TMEM accumulators)"),
             "timed": "CUDA graph of 24 per-layer launches, L2 flushed; the forks share the prefix's blocks"}
 
 
@@ -922,8 +922,8 @@ def run_prefill_attention_only(device) -> dict:
     batched.write_paged_kv_batch(pool, sk, sk, torch.from_numpy(suffix.reshape(-1)).to(device))
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
     return {"suffix_prefill_attention": bench_prefill_attention(device, pool, forks, 128, flush),
-            "suffix_prefill_attention_tcgen05": bench_prefill_attention(device, pool, forks, 128, flush,
-                                                                        kernel="tcgen05")}
+            "suffix_prefill_attention_mma_sync": bench_prefill_attention(device, pool, forks, 128, flush,
+                                                                         kernel="mma_sync")}
 
 
 def run_cow_only(device) -> dict:
@@ -1119,8 +1119,8 @@ def run_extras(device, handoff_only: bool = False, attention_only: bool = False,
             entry.update(bench_cow_device(device, pool4, parent, forks, prefix_len, flush))
         else:
             out["suffix_prefill_attention"] = bench_prefill_attention(device, pool4, forks, 128, flush)
-            out["suffix_prefill_attention_tcgen05"] = bench_prefill_attention(device, pool4, forks, 128, flush,
-                                                                              kernel="tcgen05")
+            out["suffix_prefill_attention_mma_sync"] = bench_prefill_attention(device, pool4, forks, 128, flush,
+                                                                               kernel="mma_sync")
         out[f"prefix_fork_{prefix_len}"] = entry
         del sk, pk
     if _ops.read_status(device) != _lib.OK:

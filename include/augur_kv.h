@@ -254,16 +254,18 @@ int augur_kv_paged_decode_attention(const void* q, const int64_t* q_strides, /* 
  * Lengths that disagree (n_b < 0, n_b > seq_lens[b], seq_lens[b] >
  * max_seq_len, n_b > max_q_len) record AUGUR_KV_EBOUNDS and skip that
  * sequence; a block id outside [0, num_blocks) records it and reads as zeros.
- * flags: AUGUR_KV_ATTN_AUTO takes the tensor-core kernel (mma.sync) for
- * bf16/fp16, head_dim 64 or 128, <= 8 query heads per KV head, 16-byte aligned
- * pool rows and 4-byte aligned q / out; AUGUR_KV_ATTN_TCGEN05 takes the
- * tcgen05 kernel (5th-generation tensor cores, accumulators in tensor memory;
- * the same shapes with 16-byte aligned q / out rows, EINVAL otherwise);
- * AUGUR_KV_ATTN_GENERIC forces the CUDA-core kernel (any dtype; max_seq_len
- * <= ~51,000). Needs no workspace. A bounded wait of the tcgen05 kernel that
- * gives up records AUGUR_KV_ETIMEOUT.
+ * flags: AUGUR_KV_ATTN_AUTO takes the tcgen05 kernel (5th-generation tensor
+ * cores, accumulators in tensor memory) for bf16/fp16, head_dim 64 or 128,
+ * <= 8 query heads per KV head and 16-byte aligned rows of the pool, q and
+ * out; the mma.sync kernel for the same shapes when q / out rows are only
+ * 4-byte aligned; the CUDA-core kernel otherwise. AUGUR_KV_ATTN_TCGEN05 and
+ * AUGUR_KV_ATTN_MMA_SYNC force those kernels (EINVAL for shapes they do not
+ * take); AUGUR_KV_ATTN_GENERIC forces the CUDA-core kernel (any dtype;
+ * max_seq_len <= ~51,000). Needs no workspace. A bounded wait of the tcgen05
+ * kernel that gives up records AUGUR_KV_ETIMEOUT.
  */
 #define AUGUR_KV_ATTN_TCGEN05 2
+#define AUGUR_KV_ATTN_MMA_SYNC 3
 int augur_kv_paged_prefill_attention(const void* q, const int64_t* q_strides, /* [2] token, head */
                                      const void* k_pool, const void* v_pool,
                                      const int64_t* pool_strides, /* [3] block, head, row */

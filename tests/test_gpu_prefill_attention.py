@@ -37,7 +37,7 @@ def _tol(dtype):
 
 
 @pytest.mark.parametrize("case", ["f32_prefix", "bf16_prefix", "bf16_plain"])
-@pytest.mark.parametrize("kernel", ["auto", "tcgen05", "generic"])
+@pytest.mark.parametrize("kernel", ["auto", "tcgen05", "mma_sync", "generic"])
 def test_golden_prefill_attention(cuda, golden, case, kernel):
     """The reference's own attention() output for a call of several tokens on a paged cache
     (its pool as the reference left it: rows never written stay 0xFF and are never read)."""
@@ -45,8 +45,8 @@ def test_golden_prefill_attention(cuda, golden, case, kernel):
     pool = ab.PagedKVCache(keys=c["keys"].to(cuda), values=c["values"].to(cuda), block_size=16,
                            allocator=ab.BlockAllocator(c["keys"].shape[1]))
     table = ab.SequenceBlockTable(block_ids=list(c["block_ids"]), block_size=16, seq_len=c["seq_len"])
-    if kernel == "tcgen05" and c["q"].dtype == torch.float32:
-        with pytest.raises(ab.KVLibraryError, match="tcgen05 kernel needs bf16/fp16"):
+    if kernel in ("tcgen05", "mma_sync") and c["q"].dtype == torch.float32:
+        with pytest.raises(ab.KVLibraryError, match="needs bf16/fp16"):
             paged_attention(c["q"].to(cuda), pool, 0, table, kernel=kernel)
         return
     out = paged_attention(c["q"].to(cuda), pool, 0, table, kernel=kernel)
@@ -95,7 +95,7 @@ PREFIXES = [0, 21, 200, 700, 16, 5]
 SUFFIXES = [37, 16, 45, 1, 64, 3]
 
 
-@pytest.mark.parametrize("kernel", ["auto", "tcgen05"])
+@pytest.mark.parametrize("kernel", ["tcgen05", "mma_sync"])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("D, Hq, Hkv", [(64, 14, 2), (128, 8, 2), (64, 8, 8), (64, 16, 2)])
 def test_batch_matches_oracle(cuda, oracle, dtype, D, Hq, Hkv, kernel):
@@ -107,7 +107,7 @@ def test_float32_takes_the_generic_kernel(cuda, oracle):
 
 
 def test_the_three_kernels_agree(cuda, oracle):
-    a = _batch(cuda, oracle, torch.bfloat16, 64, 14, 2, PREFIXES, SUFFIXES, seed=9)
+    a = _batch(cuda, oracle, torch.bfloat16, 64, 14, 2, PREFIXES, SUFFIXES, seed=9, kernel="mma_sync")
     b = _batch(cuda, oracle, torch.bfloat16, 64, 14, 2, PREFIXES, SUFFIXES, seed=9, kernel="generic")
     c = _batch(cuda, oracle, torch.bfloat16, 64, 14, 2, PREFIXES, SUFFIXES, seed=9, kernel="tcgen05")
     torch.testing.assert_close(a.float(), b.float(), rtol=1e-2, atol=1e-2)
