@@ -33,6 +33,7 @@ ATTN_AUTO = 0
 ATTN_GENERIC = 1
 ATTN_TCGEN05 = 2  # paged prefill attention: force the tcgen05 kernel
 ATTN_MMA_SYNC = 3  # paged prefill attention: force the mma.sync kernel
+ATTN_EARLY_READS = 16  # decode attention: read lengths, tables and pool rows before the dependency wait
 
 STATUS_NAMES = {
     OK: "ok",

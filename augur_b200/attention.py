@@ -101,6 +101,7 @@ def paged_decode_attention(
     out: Tensor | None = None,
     generic: bool = False,
     stream: torch.cuda.Stream | None = None,
+    early_reads: bool = False,
 ) -> Tensor:
     """Attention of each sequence's decode query over its cached K/V (one layer).
 
@@ -109,6 +110,10 @@ def paged_decode_attention(
     sequence (its seq_len positions are attended) or a prepared DecodeTables.
     Returns the attention output in q's shape (before the output projection,
     heads not yet concatenated). generic=True forces the CUDA-core kernel.
+    early_reads=True lets the launch read the lengths, the block tables and
+    the pool before the kernel ahead of it on the stream has finished
+    (AUGUR_KV_ATTN_EARLY_READS): only when that kernel writes none of them,
+    e.g. when it is the previous layer's attention.
     """
     squeeze = q.dim() == 4
     if squeeze:
@@ -147,10 +152,11 @@ def paged_decode_attention(
     lib = _lib.load()
     device = kc.device
     st = stream if stream is not None else torch.cuda.current_stream(device)
-    flags = _lib.ATTN_GENERIC if generic else _lib.ATTN_AUTO
+    kind = _lib.ATTN_GENERIC if generic else _lib.ATTN_AUTO
+    flags = kind | (_lib.ATTN_EARLY_READS if early_reads else 0)
     dcode = _ops.dtype_code(q3)
     with _ops._DeviceGuard(device):
-        cnt, scr = _workspace(lib, device, st, (B, Hq, Hkv, D, dt.max_seq_len, dcode, flags))
+        cnt, scr = _workspace(lib, device, st, (B, Hq, Hkv, D, dt.max_seq_len, dcode, kind))
         code = lib.augur_kv_paged_decode_attention(
             q3.data_ptr(), _lib.i64_array((q3.stride(0), q3.stride(1))),
             kc.data_ptr(), vc.data_ptr(), _lib.i64_array((kc.stride(0), kc.stride(1), kc.stride(2))),

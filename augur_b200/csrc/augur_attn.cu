@@ -110,6 +110,9 @@ struct AttnArgs {
   // these disagree with them (the two-launch path uses them directly).
   const int64_t* chk_pos;
   const int64_t* chk_slot;
+  // AUGUR_KV_ATTN_EARLY_READS: seq_lens, the block tables and the pool rows
+  // of a CTA's first item are read before the grid-dependency wait
+  int32_t early;
 };
 
 constexpr float kNegInf = -INFINITY;
@@ -465,7 +468,11 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   // Launched as a programmatic dependent of the previous kernel on the
   // stream: wait for it to finish (its writes visible) before reading inputs.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // With early reads the plan, the first item's block-table entries and its
+  // K/V rows are read first, while the previous kernel's last CTAs drain; q,
+  // the new token's k / v, the output and the workspace only after the wait.
+  const bool early = a.early != 0;
+  if (!early) asm volatile("griddepcontrol.wait;" ::: "memory");
   // Persistent: CTA i takes items i, i + grid, i + 2 grid, ... Warp 0 plans,
   // then finds each item one item ahead (while its own loads for the current
   // item are in flight) and publishes it in a double-buffered descriptor.
@@ -513,6 +520,7 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
   __syncthreads();  // descriptor `slot` is published; the previous item is done with shared memory
   const int* d = desc + slot * 6;
   if (d[1] < 0) {
+    if (early && first_item) asm volatile("griddepcontrol.wait;" ::: "memory");  // before the workspace
     if (sched != nullptr && threadIdx.x == 0 && atomicAdd(sched + 1, 1) == int(gridDim.x) - 1) {
       sched[0] = 0;  // every CTA has taken its last id: ready for the next launch
       sched[1] = 0;
@@ -527,28 +535,8 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
   const int tok0 = chunk * plan_C, tok1 = min(S, tok0 + plan_C);
   const int G = a.groups;
 
-  // Q^T as mma B fragments: b0 = Q[head nt*8+g][dims ks*16+2t, +1], b1 the
-  // same 8 dims further (heads >= G are 0).
+  // Q^T as mma B fragments (loaded once this item's first K/V loads are issued)
   uint32_t qb[D / 16][NT][2];
-  {
-    const char* qbase = a.q + int64_t(b) * a.q_stride_b;
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const int head = nt * 8 + g;
-      const char* qrow = qbase + int64_t(hk * G + head) * a.q_stride_h;
-#pragma unroll
-      for (int ks = 0; ks < D / 16; ++ks) {
-        uint32_t v0 = 0, v1 = 0;
-        if (head < G) {
-          v0 = *reinterpret_cast<const uint32_t*>(qrow + (ks * 16 + 2 * t) * 2);
-          v1 = *reinterpret_cast<const uint32_t*>(qrow + (ks * 16 + 8 + 2 * t) * 2);
-        }
-        qb[ks][nt][0] = v0;
-        qb[ks][nt][1] = v1;
-      }
-    }
-  }
-
   // O^T accumulators: o[dm][nt] = O^T[dims dm*16 + g (+8)][heads nt*8 + 2t (+1)]
   float o[D / 16][NT][4];
 #pragma unroll
@@ -642,15 +630,53 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
   const int mat = lane >> 3, r8 = lane & 7;
   // stage i of this warp starts at token tok0 + (warp + i W) * 32; the first
   // NS stages load up front, and each buffer refills as soon as it is computed
+  auto load_first = [&]() {
 #pragma unroll
-  for (int i = 0; i < NS; ++i) {
-    if (i < n_my) load_stage(tok0 + (warp + i * W) * kStageTok, i);
-    else cp_async_commit();
+    for (int i = 0; i < NS; ++i) {
+      if (i < n_my) load_stage(tok0 + (warp + i * W) * kStageTok, i);
+      else cp_async_commit();
+    }
+  };
+  // early reads: a warp whose first stages hold the new token of a fused
+  // launch (its k / v come from the previous kernel) loads after the wait
+  bool defer = false;
+  if (FUSE && early && first_item) {
+#pragma unroll
+    for (int i = 0; i < NS; ++i) {
+      const int s0 = tok0 + (warp + i * W) * kStageTok;
+      defer = defer || (i < n_my && new_pos >= s0 && new_pos < s0 + kStageTok);
+    }
   }
-  if (first_item) {  // this CTA's first loads are issued: the next kernel may start launching
+  if (!defer) load_first();
+  if (first_item) {
+    if (early) asm volatile("griddepcontrol.wait;" ::: "memory");
+    // this CTA's first loads are issued (and the previous kernel is done):
+    // the next kernel may start launching
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     first_item = false;
   }
+  if (defer) load_first();
+  // Q^T as mma B fragments: b0 = Q[head nt*8+g][dims ks*16+2t, +1], b1 the
+  // same 8 dims further (heads >= G are 0).
+  {
+    const char* qbase = a.q + int64_t(b) * a.q_stride_b;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int head = nt * 8 + g;
+      const char* qrow = qbase + int64_t(hk * G + head) * a.q_stride_h;
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        uint32_t v0 = 0, v1 = 0;
+        if (head < G) {
+          v0 = *reinterpret_cast<const uint32_t*>(qrow + (ks * 16 + 2 * t) * 2);
+          v1 = *reinterpret_cast<const uint32_t*>(qrow + (ks * 16 + 8 + 2 * t) * 2);
+        }
+        qb[ks][nt][0] = v0;
+        qb[ks][nt][1] = v1;
+      }
+    }
+  }
+
   if (warp == 0) publish(slot ^ 1, next_id());  // overlaps this warp's loads
   if (FUSE && n_my > 0 && S > 0) {
     // fused launches: q arrives before RoPE. Dims d and d + D/2 of a head sit
@@ -1194,7 +1220,8 @@ AUGUR_KV_EXPORT int augur_kv_paged_decode_attention_workspace(int32_t batch, int
       n_q_heads % n_kv_heads != 0 || head_dim <= 0)
     return fail(AUGUR_KV_EINVAL, "paged_decode_attention_workspace: bad sizes");
   const int G = n_q_heads / n_kv_heads;
-  if (batch == 0 || flags == AUGUR_KV_ATTN_GENERIC || !mma_shape_ok(dtype, head_dim, G)) return AUGUR_KV_OK;
+  if (batch == 0 || (flags & ~AUGUR_KV_ATTN_EARLY_READS) == AUGUR_KV_ATTN_GENERIC || !mma_shape_ok(dtype, head_dim, G))
+    return AUGUR_KV_OK;
   if (max_seq_len > kMaxSeq)
     return fail(AUGUR_KV_EINVAL, "paged_decode_attention_workspace: max_seq_len above %d", kMaxSeq);
   if (dtype == AUGUR_KV_BF16)
@@ -1228,7 +1255,8 @@ int paged_decode_attention_impl(
   if (n_q_heads <= 0 || n_kv_heads <= 0 || n_q_heads % n_kv_heads != 0 || head_dim <= 0 || block_size <= 0 ||
       num_blocks <= 0 || max_blocks <= 0 || batch > 65535 || n_kv_heads > 65535)
     return fail(AUGUR_KV_EINVAL, "paged_decode_attention: bad sizes");
-  if (flags < AUGUR_KV_ATTN_AUTO || flags > AUGUR_KV_ATTN_GENERIC)
+  const int32_t kind = flags & ~AUGUR_KV_ATTN_EARLY_READS;
+  if (kind < AUGUR_KV_ATTN_AUTO || kind > AUGUR_KV_ATTN_GENERIC)
     return fail(AUGUR_KV_EINVAL, "paged_decode_attention: unknown flags %d", flags);
 
   AttnArgs a;
@@ -1263,6 +1291,7 @@ int paged_decode_attention_impl(
   a.out_stride_h = out_strides[1] * es;
   a.dtype = dtype;
   a.status = status;
+  a.early = (flags & AUGUR_KV_ATTN_EARLY_READS) != 0 ? 1 : 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
   a.max_seq = max_seq_len;
@@ -1284,7 +1313,7 @@ int paged_decode_attention_impl(
     const uintptr_t falign = reinterpret_cast<uintptr_t>(fuse->new_k) | reinterpret_cast<uintptr_t>(fuse->new_v) |
                              uintptr_t(fuse->new_stride_b * es) | uintptr_t(fuse->new_stride_h * es) |
                              reinterpret_cast<uintptr_t>(fuse->cos) | reinterpret_cast<uintptr_t>(fuse->sin);
-    if (flags == AUGUR_KV_ATTN_GENERIC || !mma_ok || (falign & 15u) != 0 || fuse->new_k == nullptr ||
+    if (kind == AUGUR_KV_ATTN_GENERIC || !mma_ok || (falign & 15u) != 0 || fuse->new_k == nullptr ||
         fuse->new_v == nullptr || fuse->cos == nullptr || fuse->sin == nullptr || fuse->n_pos <= 0 ||
         max_seq_len > kMaxSeq)
       return AUGUR_KV_OK;
@@ -1305,7 +1334,7 @@ int paged_decode_attention_impl(
     a.v_w = static_cast<char*>(const_cast<void*>(v_pool));
     if (fused != nullptr) *fused = true;
   }
-  if (flags != AUGUR_KV_ATTN_GENERIC && mma_ok) {
+  if (kind != AUGUR_KV_ATTN_GENERIC && mma_ok) {
     if (max_seq_len > kMaxSeq)
       return fail(AUGUR_KV_EINVAL, "paged_decode_attention: max_seq_len above %d", kMaxSeq);
     if (dtype == AUGUR_KV_BF16)

@@ -64,9 +64,10 @@ AUGUR_KV_EXPORT int augur_kv_decode_layer(augur_kv_decode_args* A, int32_t layer
                                  A->rope_positions, q, q_src, A->q_rot, q_rot, Hq, A->batch, 1, A->n_kv_heads, D,
                                  A->status, stream);
   if (rc != AUGUR_KV_OK) return rc;
+  // the RoPE write just ahead of it writes the new tokens' pool rows: no early reads
   return augur_kv_paged_decode_attention(A->q_rot, dense, kl, vl, pool, A->num_blocks, A->block_size,
                                          A->block_tables, A->tables_stride, A->max_blocks, A->seq_lens,
                                          A->max_seq_len, A->batch, Hq, A->n_kv_heads, D, A->dtype, out, dense,
-                                         A->flags, A->counters, A->counters_bytes, A->scratch, A->scratch_bytes,
+                                         A->flags & ~AUGUR_KV_ATTN_EARLY_READS, A->counters, A->counters_bytes, A->scratch, A->scratch_bytes,
                                          A->status, stream);
 }

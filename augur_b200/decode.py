@@ -41,8 +41,14 @@ class DecodeStep:
     it crosses a boundary, as ensure_position does), and the step's slots, positions and
     device block tables are built once for all layers."""
 
-    def __init__(self, cache: PagedKVCache, tables: Sequence[SequenceBlockTable]) -> None:
+    def __init__(self, cache: PagedKVCache, tables: Sequence[SequenceBlockTable], early_reads: bool = False) -> None:
+        """early_reads: the one-launch layers read the lengths, block tables and pool before the
+        kernel ahead of them on the stream has finished (AUGUR_KV_ATTN_EARLY_READS). Valid
+        when no kernel that may still run at a layer's launch writes them: the model's
+        projections and the previous layer's launch do not; a prefill write or copy-on-write
+        of the pool issued just before the first layer does."""
         device = cache.keys.device
+        self.flags = _lib.ATTN_AUTO | (_lib.ATTN_EARLY_READS if early_reads else 0)
         positions = np.asarray([t.seq_len for t in tables], dtype=np.int64)
         slots = decode_slot_mapping(tables, cache.allocator)  # seq_len += 1 for every table
         self.batch = len(tables)
@@ -82,7 +88,7 @@ class DecodeStep:
         a.k_pool, a.v_pool = kc.data_ptr(), cache.values.data_ptr()
         a.pool_strides[:] = kc.stride()[:4]  # layer, block, kv head, row
         a.num_blocks, a.block_size, a.n_layers = NB, bs, L
-        a.n_q_heads, a.n_kv_heads, a.head_dim, a.dtype, a.batch, a.flags = Hq, Hkv, D, dcode, B, _lib.ATTN_AUTO
+        a.n_q_heads, a.n_kv_heads, a.head_dim, a.dtype, a.batch, a.flags = Hq, Hkv, D, dcode, B, self.flags
         a.slots, a.positions = self.slots.data_ptr(), self.positions.data_ptr()
         a.rope_cos, a.rope_sin, a.rope_positions = cos.data_ptr(), sin.data_ptr(), cos.shape[0]
         a.q_strides[:] = q.stride()[:2]
@@ -146,7 +152,8 @@ class DecodeGraphStep:
     """
 
     def __init__(self, cache: PagedKVCache, batch: int, max_blocks: int, n_q_heads: int,
-                 rope_theta: float) -> None:
+                 rope_theta: float, early_reads: bool = False) -> None:
+        """early_reads: as DecodeStep's."""
         _ops.require_cuda("DecodeGraphStep", cache.keys, cache.values)
         L, NB, Hkv, bs, D = cache.keys.shape
         if batch <= 0 or max_blocks <= 0 or n_q_heads <= 0 or n_q_heads % Hkv != 0:
@@ -176,7 +183,8 @@ class DecodeGraphStep:
         a.k_pool, a.v_pool = kc.data_ptr(), cache.values.data_ptr()
         a.pool_strides[:] = kc.stride()[:4]
         a.num_blocks, a.block_size, a.n_layers = NB, bs, L
-        a.n_q_heads, a.n_kv_heads, a.head_dim, a.dtype, a.batch, a.flags = n_q_heads, Hkv, D, dcode, batch, _lib.ATTN_AUTO
+        a.n_q_heads, a.n_kv_heads, a.head_dim, a.dtype, a.batch = n_q_heads, Hkv, D, dcode, batch
+        a.flags = _lib.ATTN_AUTO | (_lib.ATTN_EARLY_READS if early_reads else 0)
         a.slots, a.positions = self._d64[0].data_ptr(), self._d64[1].data_ptr()
         a.rope_cos, a.rope_sin, a.rope_positions = self._cos.data_ptr(), self._sin.data_ptr(), self._cos.shape[0]
         a.q_strides[:] = (n_q_heads * D, D)  # dense [batch, n_q_heads, 1, head_dim]

@@ -529,11 +529,14 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
     return line
 
 
-def bench_decode_attention(device, pool, tables) -> dict:
+def bench_decode_attention(device, pool, tables, early_reads: bool = True) -> dict:
     """paged_decode_attention for every layer of one decode step, graph-captured, L2 cold.
 
     Algorithmic bytes: every cached K and V row of every sequence read once
     (24 layers x sum(seq_len) x 512 B) plus the queries and outputs.
+    early_reads: each layer's launch reads lengths, tables and its K/V rows while the
+    previous layer's launch drains (the kernel ahead of it writes none of them).
+    The same graph without early reads is timed beside it.
     """
     from augur_b200.attention import DecodeTables, paged_decode_attention
 
@@ -546,7 +549,7 @@ def bench_decode_attention(device, pool, tables) -> dict:
 
     def step() -> None:
         for layer in range(L):
-            paged_decode_attention(qs[layer], pool, layer, dt, out=outs[layer])
+            paged_decode_attention(qs[layer], pool, layer, dt, out=outs[layer], early_reads=early_reads)
 
     graph = torch.cuda.CUDAGraph()
     cs = torch.cuda.Stream(device)
@@ -572,9 +575,13 @@ def bench_decode_attention(device, pool, tables) -> dict:
     kv_bytes = L * tokens * TOKEN_LAYER_BYTES + 2 * qs.numel() * 2
     peak, kind = load_peaks()
     gbs = kv_bytes / (ms / 1e3) / 1e9
-    return {"us_per_step_all_layers": round(ms * 1e3, 2), "us_per_layer": round(ms * 1e3 / L, 2),
-            "seqs": B, "cached_tokens": tokens, "GBps": round(gbs, 1), "frac_of_hbm_peak": round(gbs / peak, 4),
-            "kernel": "attn_decode_split_kernel<bf16,64>", "timed": "CUDA graph of 24 per-layer launches, L2 flushed"}
+    res = {"us_per_step_all_layers": round(ms * 1e3, 2), "us_per_layer": round(ms * 1e3 / L, 2),
+           "seqs": B, "cached_tokens": tokens, "GBps": round(gbs, 1), "frac_of_hbm_peak": round(gbs / peak, 4),
+           "early_reads": early_reads, "kernel": "attn_decode_split_kernel<bf16,64>",
+           "timed": "CUDA graph of 24 per-layer launches, L2 flushed"}
+    if early_reads:
+        res["us_per_layer_without_early_reads"] = bench_decode_attention(device, pool, tables, False)["us_per_layer"]
+    return res
 
 
 def bench_rope(device, pool, reps: int = 7) -> dict:
@@ -666,7 +673,7 @@ def bench_decode_step(device, pool, tables) -> dict:
     q = torch.randn(L, B, Hq, 1, D, generator=g, device=device).to(torch.bfloat16)
     k = torch.randn(L, B, H, 1, D, generator=g, device=device).to(torch.bfloat16)
     v = torch.randn(L, B, H, 1, D, generator=g, device=device).to(torch.bfloat16)
-    step = DecodeStep(pool, tabs)
+    step = DecodeStep(pool, tabs, early_reads=True)  # the kernel ahead of each layer is the previous layer's
 
     def layers(st) -> None:
         for layer in range(L):
@@ -703,11 +710,11 @@ def bench_decode_step(device, pool, tables) -> dict:
     agraph = torch.cuda.CUDAGraph()
     with torch.cuda.stream(cs):
         for layer in range(L):
-            paged_decode_attention(qr[layer], pool, layer, step.tables, out=outs[layer])
+            paged_decode_attention(qr[layer], pool, layer, step.tables, out=outs[layer], early_reads=True)
     torch.cuda.synchronize(device)
     with torch.cuda.graph(agraph, stream=cs):
         for layer in range(L):
-            paged_decode_attention(qr[layer], pool, layer, step.tables, out=outs[layer])
+            paged_decode_attention(qr[layer], pool, layer, step.tables, out=outs[layer], early_reads=True)
     atimes = []
     for _ in range(7):
         flush.fill_(1)
@@ -723,13 +730,13 @@ def bench_decode_step(device, pool, tables) -> dict:
     for _ in range(5):  # real steps: every table grows by one token per step
         torch.cuda.synchronize(device)
         t0 = time.perf_counter()
-        layers(DecodeStep(pool, tabs))
+        layers(DecodeStep(pool, tabs, early_reads=True))
         torch.cuda.synchronize(device)
         host.append(time.perf_counter() - t0)
     # the same steps replayed from one captured graph (DecodeGraphStep): per step the host
     # grows the tables and refreshes the step's buffers, then the 48 launches replay
     max_blocks = max(len(t.block_ids) for t in tabs) + 4
-    gstep = DecodeGraphStep(pool, B, max_blocks, Hq, theta)
+    gstep = DecodeGraphStep(pool, B, max_blocks, Hq, theta, early_reads=True)
     gs = torch.cuda.Stream(device)
     gs.wait_stream(torch.cuda.current_stream(device))
     ggraph = torch.cuda.CUDAGraph()

@@ -214,9 +214,21 @@ int augur_kv_copy_runs(const void* src_k, const void* src_v,
  * processed unsplit; without counters, work items are also assigned statically.
  * A seq_lens entry above max_seq_len records AUGUR_KV_EBOUNDS and only its
  * first max_seq_len positions are attended. max_seq_len is at most 2^30.
+ * flags | AUGUR_KV_ATTN_EARLY_READS (tensor-core kernel; ignored otherwise):
+ * the launch is a programmatic dependent of the kernel ahead of it on the
+ * stream either way; with this bit its CTAs read seq_lens, the block tables
+ * and the K/V rows of their first work item BEFORE waiting for that kernel to
+ * finish, so those reads overlap its last CTAs. Set it only when no work
+ * still running at the launch writes seq_lens, the tables or this layer's
+ * pool rows: the kernel ahead writes none of them, and everything before it
+ * has finished (it has when the kernel ahead is a launch of this entry point
+ * or of augur_kv_decode_layer, which release their dependents only after
+ * their own wait). q, the new tokens' k / v (augur_kv_decode_layer), out and
+ * the workspace are touched only after the wait, as without the bit.
  */
 #define AUGUR_KV_ATTN_AUTO 0
 #define AUGUR_KV_ATTN_GENERIC 1
+#define AUGUR_KV_ATTN_EARLY_READS 16
 
 int augur_kv_paged_decode_attention(const void* q, const int64_t* q_strides, /* [2] */
                                     const void* k_pool, const void* v_pool,
@@ -313,6 +325,10 @@ int augur_kv_paged_decode_attention_workspace(int32_t batch, int32_t n_q_heads, 
  * new k and v rows, bit for bit what the two separate launches write and
  * return. Other shapes run augur_kv_rope_scatter (the rotated q into
  * args->q_rot, otherwise unused scratch) and then the attention.
+ * args->flags: as augur_kv_paged_decode_attention's. With
+ * AUGUR_KV_ATTN_EARLY_READS the one-launch form reads the pool early (the
+ * new token's row is loaded after the wait); the two-launch form drops the
+ * bit, since its RoPE write just ahead writes the pool.
  * Returns the first failing code; AUGUR_KV_EINVAL for a null args or a layer
  * outside [0, n_layers).
  */

@@ -16,6 +16,7 @@ import torch
 import augur_b200 as ab
 from augur_b200 import _lib, _ops
 from augur_b200.attention import DecodeTables, paged_decode_attention
+from tests.conftest import assert_bits_equal
 
 pytestmark = pytest.mark.gpu
 
@@ -260,3 +261,70 @@ def test_back_to_back_launches_share_the_workspace(cuda, oracle):
     for seed in (41, 42, 43):
         lens = [int(x) for x in np.random.default_rng(seed).integers(100, 3000, size=20)]
         _case(cuda, oracle, torch.float16, len(lens), 14, 2, 64, 16, lens, seed, False)
+
+
+@pytest.mark.parametrize("nseq", [5, 40, 300])
+def test_early_reads_back_to_back_layers(cuda, oracle, nseq):
+    """AUGUR_KV_ATTN_EARLY_READS: each layer's launch reads lengths, tables and pool rows
+    before the previous layer's launch (which shares its workspace) has finished. Six
+    layers back to back, twice over, give the same outputs bit for bit both times, and the
+    outputs of launches without early reads and the oracle's within tolerance (a small
+    batch's plan may take fewer, longer chunks with early reads, so the summation order can
+    differ). Five sequences leave most CTAs without an item (they exit through the
+    scheduler's counters); 300 take several items per CTA."""
+    L, Hq, Hkv, D, bs = 6, 14, 2, 64, 16
+    rng = np.random.default_rng(nseq)
+    lens = [int(x) for x in rng.integers(1, 2500 if nseq < 100 else 900, size=nseq)]
+    nblk = [-(-n // bs) for n in lens]
+    NB = sum(nblk) + 3
+    g = torch.Generator().manual_seed(nseq)
+    kp = torch.randn(L, NB, Hkv, bs, D, generator=g).to(torch.bfloat16)
+    vp = torch.randn(L, NB, Hkv, bs, D, generator=g).to(torch.bfloat16)
+    perm = rng.permutation(NB).tolist()
+    tables, cur = [], 0
+    for n, nb in zip(lens, nblk):
+        tables.append(ab.SequenceBlockTable(block_ids=perm[cur : cur + nb], block_size=bs, seq_len=n))
+        cur += nb
+    pool = ab.PagedKVCache(keys=kp.to(cuda), values=vp.to(cuda), block_size=bs, allocator=ab.BlockAllocator(NB))
+    dt = DecodeTables(tables, cuda)
+    q = torch.randn(L, nseq, Hq, D, generator=g).to(torch.bfloat16)
+    qd = q.to(cuda)
+    plain = torch.stack([paged_decode_attention(qd[layer], pool, layer, dt) for layer in range(L)])
+    first = None
+    for _ in range(2):
+        outs = torch.full_like(qd, float("nan"))
+        for layer in range(L):
+            paged_decode_attention(qd[layer], pool, layer, dt, out=outs[layer], early_reads=True)
+        torch.cuda.synchronize(cuda)
+        if first is None:
+            first = outs
+            _close(outs, plain, torch.bfloat16, "early reads against plain launches")
+        else:
+            assert_bits_equal(outs, first, "early reads, second pass")
+    assert _ops.read_status(cuda) == _lib.OK
+    for layer in (0, L - 1):
+        for b in range(0, nseq, max(1, nseq // 10)):
+            k, v = oracle.read_paged_kv(kp, vp, layer, oracle.RefBlockTable(tables[b].block_ids, bs, lens[b]))
+            want = oracle.decode_attention(q[layer, b : b + 1].unsqueeze(2), k, v)[0, :, 0, :]
+            _close(outs[layer, b], want, torch.bfloat16, f"layer {layer} seq {b}")
+
+
+def test_early_reads_flag_is_checked(cuda):
+    """The early-reads bit combines with AUTO or GENERIC only; other values are refused."""
+    lens = [40, 3]
+    kp, vp, tables, q, pool = _long_batch(cuda, 23, lens)
+    dt = DecodeTables(tables, cuda)
+    qd = q.to(cuda)
+    out = torch.empty_like(qd)
+    lib = _lib.load()
+    for flags, ok in ((_lib.ATTN_EARLY_READS, True), (_lib.ATTN_GENERIC | _lib.ATTN_EARLY_READS, True),
+                      (_lib.ATTN_EARLY_READS | 2, False), (32, False)):
+        code = lib.augur_kv_paged_decode_attention(
+            qd.data_ptr(), _lib.i64_array((qd.stride(0), qd.stride(1))), pool.keys[0].data_ptr(),
+            pool.values[0].data_ptr(), _lib.i64_array(pool.keys[0].stride()[:3]), pool.keys.shape[1], 16,
+            dt.blocks.data_ptr(), dt.blocks.stride(0), dt.blocks.shape[1], dt.lens.data_ptr(), dt.max_seq_len,
+            2, 14, 2, 64, _lib.BF16, out.data_ptr(), _lib.i64_array((out.stride(0), out.stride(1))), flags,
+            None, 0, None, 0, _ops.status_word(cuda).data_ptr(), torch.cuda.current_stream(cuda).cuda_stream)
+        assert (code == _lib.OK) == ok, flags
+    torch.cuda.synchronize(cuda)
+    assert _ops.read_status(cuda) == _lib.OK

@@ -84,11 +84,14 @@ def test_decode_layers_match_the_reference_branch(cuda, oracle, path):
     assert _ops.read_status(cuda) == _lib.OK
 
 
-def test_graph_step_replays_match_eager_steps(cuda):
+@pytest.mark.parametrize("early", [False, True])
+def test_graph_step_replays_match_eager_steps(cuda, early):
     """A CUDA graph captured once over DecodeGraphStep.layer calls, replayed after each
     update(), gives the eager DecodeStep results: the same pool bits, the same block tables,
     attention outputs within the bf16 tolerance (the launch plan sees the step's capacity
-    instead of its longest sequence); padding rows write nothing and return zeros."""
+    instead of its longest sequence); padding rows write nothing and return zeros.
+    early: the graph's layers read lengths, tables and pool before the previous layer's
+    launch has finished."""
     from augur_b200.decode import DecodeGraphStep
 
     L, H, Hq, D, bs, NB = 2, 2, 14, 64, 16, 96
@@ -122,7 +125,7 @@ def test_graph_step_replays_match_eager_steps(cuda):
     q_in = torch.zeros(L, cap_seqs, Hq, 1, D, dtype=torch.bfloat16, device=cuda)
     k_in = torch.zeros(L, cap_seqs, H, 1, D, dtype=torch.bfloat16, device=cuda)
     v_in = torch.zeros(L, cap_seqs, H, 1, D, dtype=torch.bfloat16, device=cuda)
-    gs = DecodeGraphStep(pool_g, cap_seqs, max_blocks, Hq, THETA)
+    gs = DecodeGraphStep(pool_g, cap_seqs, max_blocks, Hq, THETA, early_reads=early)
     graph = torch.cuda.CUDAGraph()
     cs = torch.cuda.Stream(cuda)
     cs.wait_stream(torch.cuda.current_stream(cuda))
@@ -174,14 +177,18 @@ def test_graph_step_rejects_what_it_cannot_describe(cuda):
                  torch.zeros(2, 2, 1, 64, dtype=torch.bfloat16, device=cuda))
 
 
+@pytest.mark.parametrize("early", [False, True])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("head_dim", [64, 128])
-def test_fused_decode_layer_matches_separate_launches(cuda, dtype, head_dim):
+def test_fused_decode_layer_matches_separate_launches(cuda, dtype, head_dim, early):
     """augur_kv_decode_layer rotates q and the new k inside the attention launch and writes
     the new k / v rows itself (bf16 / fp16); the general path runs the RoPE write and the
     attention as two launches. Both must leave the same pool bits and return the same
-    outputs bit for bit, step after step. float32 takes the two-launch form in both."""
-    L, H, Hq, bs, NB = 2, 2, 14, 16, 96
+    outputs bit for bit, step after step. float32 takes the two-launch form in both.
+    early: the prepared layers read lengths, tables and pool rows before the previous
+    layer's launch has finished (the new token's row after it); the two-launch form drops
+    the early reads."""
+    L, H, Hq, bs, NB = 4, 2, 14, 16, 96
     prior = [1, 15, 16, 47, 300]
     g = torch.Generator().manual_seed(77)
 
@@ -207,7 +214,7 @@ def test_fused_decode_layer_matches_separate_launches(cuda, dtype, head_dim):
         v = torch.randn(L, B, H, 1, head_dim, generator=g).to(dtype).to(cuda)
         outs = []
         for i, (pool, tables) in enumerate(pools):
-            step = DecodeStep(pool, tables)
+            step = DecodeStep(pool, tables, early_reads=early and i == 0)
             stream = torch.cuda.current_stream(cuda) if i == 1 else None
             outs.append([paged_decode_layer(step, pool, layer, q[layer], k[layer], v[layer], THETA, stream=stream)
                          for layer in range(L)])
