@@ -265,7 +265,7 @@ struct SplitCfg {
 #define AUGUR_KV_ATTN_STAGES 1  // stage buffers per warp at head_dim 64
 #endif
 #ifndef AUGUR_KV_ATTN_COMBINE_REGS
-#define AUGUR_KV_ATTN_COMBINE_REGS 16  // registers per thread holding partial outputs in the combine
+#define AUGUR_KV_ATTN_COMBINE_REGS 20  // registers per thread holding partial outputs in the combine
 #endif
 
 __device__ __forceinline__ float ex2(float x) {  // 2^x; ex2(-inf) = 0

@@ -57,7 +57,11 @@ def assert_bits_equal(a: torch.Tensor, b: torch.Tensor, what: str = "") -> None:
     ab, bb = bits(a.cpu()), bits(b.cpu())
     if not torch.equal(ab, bb):
         diff = (ab != bb).nonzero()
-        raise AssertionError(f"{what}: {diff.shape[0]} elements differ, first at {diff[0].tolist()}")
+        mask = (1 << (8 * a.element_size())) - 1
+        shown = ", ".join(f"{idx}: {int(ab[tuple(idx)]) & mask:#x} vs {int(bb[tuple(idx)]) & mask:#x}"
+                          for idx in diff[:8].tolist())
+        raise AssertionError(f"{what}: {diff.shape[0]} elements differ, first at {diff[0].tolist()} "
+                             f"(got vs want bits: {shown})")
 
 
 def poison_(t: torch.Tensor) -> torch.Tensor:
