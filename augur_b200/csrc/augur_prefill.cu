@@ -554,26 +554,43 @@ __global__ void __launch_bounds__(kUThreads, UCfg<D>::kMinCtas) attn_prefill_umm
                          : a.q;
     cp_async16(smem + U::kQ + (r >> 3) * U::kRowGroup + c * 128 + (r & 7) * 16, src, ok ? 16 : 0);
   }
-  auto load_kv = [&](int s, int buf) {
+  // K/V staging: 2 x 64 rows (K then V), each split into two halves of
+  // kChunks / 2 pieces, one (K or V, row, half) per thread. A thread's
+  // block-table entry for a stage is read one stage before its rows are
+  // copied, so the copies never wait on the table.
+  static_assert(2 * kUKeys * 2 == kUThreads, "one K/V half row per thread");
+  constexpr int kHalfChunks = U::kChunks / 2;
+  const int kv_sel = tid >= 2 * kUKeys;
+  const int kv_row = (tid - kv_sel * 2 * kUKeys) >> 1, kv_c0 = (tid & 1) * kHalfChunks;
+  const int32_t* kv_table = a.tables + int64_t(b) * a.tables_stride;
+  // block id of this thread's key of stage s; -1: past the sequence; -2: past the table
+  auto table_entry = [&](int s) -> int {
+    const int key = s * kUKeys + kv_row;
+    if (key >= key_end) return -1;
+    const int lb = a.bs_shift >= 0 ? (key >> a.bs_shift) : key / a.block_size;
+    return lb < a.max_blocks ? __ldg(kv_table + lb) : -2;
+  };
+  auto load_kv = [&](int s, int buf, int blk) {
     unsigned char* kd = smem + U::kK + buf * U::kKVBytes;
     unsigned char* vd = smem + U::kV + buf * U::kKVBytes;
-    // 2 x 64 rows (K then V), each split into two halves of kChunks / 2 pieces:
-    // one block-table lookup per half row
-    constexpr int kHalfChunks = U::kChunks / 2;
-    for (int w = tid; w < 2 * kUKeys * 2; w += kUThreads) {
-      const int kv = w >= 2 * kUKeys;
-      const int rw = w - kv * 2 * kUKeys;
-      const int row = rw >> 1, c0 = (rw & 1) * kHalfChunks;
-      const int key = s * kUKeys + row;
-      const char* rp = key < key_end ? pool_row(a, kv ? a.v : a.k, b, hk, key) : nullptr;
-      const char* src = rp != nullptr ? rp : a.k;
-      const int bytes = rp != nullptr ? 16 : 0;
-#pragma unroll
-      for (int c = c0; c < c0 + kHalfChunks; ++c) {
-        unsigned char* dst = kv ? vd + c * U::kVChunk + (row >> 3) * 128 + (row & 7) * 16
-                                : kd + (row >> 3) * U::kRowGroup + c * 128 + (row & 7) * 16;
-        cp_async16(dst, src + (bytes ? c * 16 : 0), bytes);
+    const int key = s * kUKeys + kv_row;
+    const char* src = a.k;
+    int bytes = 0;
+    if (key < key_end) {
+      if (blk >= 0 && blk < a.num_blocks) {
+        const int lb = a.bs_shift >= 0 ? (key >> a.bs_shift) : key / a.block_size;
+        src = (kv_sel ? a.v : a.k) + int64_t(blk) * a.blk_stride + int64_t(hk) * a.head_stride +
+              int64_t(key - lb * a.block_size) * a.row_stride;
+        bytes = 16;
+      } else {
+        record_status(a.status, AUGUR_KV_EBOUNDS);  // reads as zeros
       }
+    }
+#pragma unroll
+    for (int c = kv_c0; c < kv_c0 + kHalfChunks; ++c) {
+      unsigned char* dst = kv_sel ? vd + c * U::kVChunk + (kv_row >> 3) * 128 + (kv_row & 7) * 16
+                                  : kd + (kv_row >> 3) * U::kRowGroup + c * 128 + (kv_row & 7) * 16;
+      cp_async16(dst, src + (bytes ? c * 16 : 0), bytes);
     }
   };
   constexpr uint32_t idesc_s = umma_idesc<T>(kUKeys, false);
@@ -585,10 +602,11 @@ __global__ void __launch_bounds__(kUThreads, UCfg<D>::kMinCtas) attn_prefill_umm
                umma_desc(sb + U::kK + (s % kUKV) * U::kKVBytes + ks * 256, 128, U::kRowGroup), idesc_s, ks > 0);
     umma_commit(bar_s + (s & 1));
   };
-  load_kv(0, 0);
+  load_kv(0, 0, table_entry(0));
   cp_async_commit();  // Q and stage 0
-  if (n_st > 1) load_kv(1, 1);
+  if (n_st > 1) load_kv(1, 1, table_entry(1));
   cp_async_commit();  // stage 1
+  int next_blk = n_st > 2 ? table_entry(2) : -1;  // for the stage loaded at the end of iteration 0
   cp_async_wait<1>();
   fence_async_smem();
   tc_fence_before();
@@ -709,8 +727,9 @@ __global__ void __launch_bounds__(kUThreads, UCfg<D>::kMinCtas) attn_prefill_umm
       umma_commit(bar_o);
     }
     // stage s + 2 into the buffer of stage s - 1 (its S and P V are done)
-    if (s + 2 < n_st) load_kv(s + 2, (s + 2) % kUKV);
+    if (s + 2 < n_st) load_kv(s + 2, (s + 2) % kUKV, next_blk);
     cp_async_commit();
+    if (s + 3 < n_st) next_blk = table_entry(s + 3);
   }
   if (ok) ok = fold(n_st - 1);
   cp_async_wait<0>();
