@@ -556,7 +556,24 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
   const int shift = a.bs_shift;
   // Stage tokens [s0, s0 + 32) into buffer buf: lane l reads the table entry
   // of the stage's l-th logical block (a stage spans at most 32 blocks).
-  auto load_stage = [&](int s0, int buf) {
+  // the new token's cos / sin rows to the tail and (lane part 0) the caller's
+  // position and slot, compared when the row is written
+  auto load_new_inputs = [&](int pos) {
+    if (part == 0 && a.chk_pos != nullptr) {
+      cp_async8(new_chk, a.chk_pos + b);
+      cp_async8(new_chk + 1, a.chk_slot + b);
+    }
+    if (part < PARTS / 2) {
+      const bool in_table = pos < a.rope_n;
+      const int64_t row = in_table ? int64_t(pos) * D : 0;  // D/2 elements of 2 bytes
+      cp_async16(new_cs + part * 16, a.rope_cos + row + part * 16, in_table ? 16 : 0);
+      cp_async16(new_sn + part * 16, a.rope_sin + row + part * 16, in_table ? 16 : 0);
+      if (!in_table && part == 0) record_status(a.status, AUGUR_KV_EBOUNDS);
+    }
+  };
+  // late: the new token's row of a fused launch is left to load_new_late
+  // (after the grid-dependency wait); its pool offset is still recorded here
+  auto load_stage = [&](int s0, int buf, bool late) {
     const int last = min(tok1, s0 + kStageTok) - 1;
     const int lb_first = shift >= 0 ? (s0 >> shift) : s0 / a.block_size;
     const int lb_last = shift >= 0 ? (last >> shift) : last / a.block_size;
@@ -591,31 +608,36 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
           record_status(a.status, AUGUR_KV_EBOUNDS);  // reads as zeros
         }
         if (FUSE && pos == new_pos) {  // the new token: its k and v from the inputs, its cos / sin rows to the tail
-          const int64_t src = int64_t(b) * a.new_stride_b + int64_t(hk) * a.new_stride_h + part * 16;
-          kp = a.new_k + src;
-          vp = a.new_v + src;
-          bytes = 16;
           if (part == 0) {
             *new_ofs = blk_ok ? int64_t(blk) * a.blk_stride + int64_t(hk) * a.head_stride +
                                     int64_t(off) * a.row_stride
                               : int64_t(-1);
             new_chk[2] = int64_t(blk) * a.block_size + off;
-            if (a.chk_pos != nullptr) {  // arrive with the stage; compared when the row is written
-              cp_async8(new_chk, a.chk_pos + b);
-              cp_async8(new_chk + 1, a.chk_slot + b);
-            }
           }
-          if (part < PARTS / 2) {
-            const bool in_table = pos < a.rope_n;
-            const int64_t row = in_table ? int64_t(pos) * D : 0;  // D/2 elements of 2 bytes
-            cp_async16(new_cs + part * 16, a.rope_cos + row + part * 16, in_table ? 16 : 0);
-            cp_async16(new_sn + part * 16, a.rope_sin + row + part * 16, in_table ? 16 : 0);
-            if (!in_table && part == 0) record_status(a.status, AUGUR_KV_EBOUNDS);
-          }
+          if (late) continue;
+          load_new_inputs(pos);
+          const int64_t src = int64_t(b) * a.new_stride_b + int64_t(hk) * a.new_stride_h + part * 16;
+          kp = a.new_k + src;
+          vp = a.new_v + src;
+          bytes = 16;
         }
       }
       cp_async16(kdst + r * CF::kRowBytes, kp, bytes);
       cp_async16(vdst + r * CF::kRowBytes, vp, bytes);
+    }
+    cp_async_commit();
+  };
+  // the new token's row of stage s0 (a fused launch's first stage loaded
+  // with late = true): its k and v, cos / sin rows and the caller's
+  // position and slot, copied by the lanes that own the row
+  auto load_new_late = [&](int s0, int buf) {
+    const int r = new_pos - s0;
+    if (r % ROW_STEP == row0) {
+      load_new_inputs(new_pos);
+      const int64_t src = int64_t(b) * a.new_stride_b + int64_t(hk) * a.new_stride_h + part * 16;
+      unsigned char* kdst = wbuf + buf * CF::kWarpStage + part * 16 + r * CF::kRowBytes;
+      cp_async16(kdst, a.new_k + src, 16);
+      cp_async16(kdst + CF::kStageBytes, a.new_v + src, 16);
     }
     cp_async_commit();
   };
@@ -630,24 +652,27 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
   const int mat = lane >> 3, r8 = lane & 7;
   // stage i of this warp starts at token tok0 + (warp + i W) * 32; the first
   // NS stages load up front, and each buffer refills as soon as it is computed
-  auto load_first = [&]() {
+  auto load_first = [&](bool late) {
 #pragma unroll
     for (int i = 0; i < NS; ++i) {
-      if (i < n_my) load_stage(tok0 + (warp + i * W) * kStageTok, i);
+      if (i < n_my) load_stage(tok0 + (warp + i * W) * kStageTok, i, late);
       else cp_async_commit();
     }
   };
-  // early reads: a warp whose first stages hold the new token of a fused
-  // launch (its k / v come from the previous kernel) loads after the wait
-  bool defer = false;
+  // early reads: the new token of a fused launch (its k / v come from the
+  // previous kernel) is copied after the wait. With one stage buffer per
+  // warp only its row waits; with more, the warp's first stages do.
+  bool defer = false, late_new = false;
   if (FUSE && early && first_item) {
 #pragma unroll
     for (int i = 0; i < NS; ++i) {
       const int s0 = tok0 + (warp + i * W) * kStageTok;
-      defer = defer || (i < n_my && new_pos >= s0 && new_pos < s0 + kStageTok);
+      const bool has = i < n_my && new_pos >= s0 && new_pos < s0 + kStageTok;
+      if (NS == 1) late_new = late_new || has;
+      else defer = defer || has;
     }
   }
-  if (!defer) load_first();
+  if (!defer) load_first(late_new);
   if (first_item) {
     if (early) asm volatile("griddepcontrol.wait;" ::: "memory");
     // this CTA's first loads are issued (and the previous kernel is done):
@@ -655,7 +680,8 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     first_item = false;
   }
-  if (defer) load_first();
+  if (defer) load_first(false);
+  if (late_new) load_new_late(tok0 + warp * kStageTok, 0);  // one stage buffer: its row 0 stage
   // Q^T as mma B fragments: b0 = Q[head nt*8+g][dims ks*16+2t, +1], b1 the
   // same 8 dims further (heads >= G are 0).
   {
@@ -843,7 +869,7 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
     }
     __syncwarp();  // every lane is done with the buffer before it is refilled
     const int nxt = it + NS;
-    if (nxt < n_my) load_stage(tok0 + (warp + nxt * W) * kStageTok, nxt % NS);
+    if (nxt < n_my) load_stage(tok0 + (warp + nxt * W) * kStageTok, nxt % NS, false);
     else cp_async_commit();
   }
   cp_async_wait<0>();
