@@ -48,11 +48,34 @@ def rope_tables(head_dim: int, rope_theta: float, dtype: torch.dtype, n_position
         size = 4096
         while size < n_positions:
             size *= 2
-        inv_freq = 1.0 / (rope_theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim))
-        freqs = torch.arange(size, dtype=torch.float32).unsqueeze(-1) * inv_freq
-        entry = (freqs.cos().to(dtype).to(device), freqs.sin().to(dtype).to(device))
+        cos, sin = _host_tables(head_dim, rope_theta, size)
+        entry = (cos.to(dtype).to(device), sin.to(dtype).to(device))
         _tables[key] = entry
     return entry
+
+
+def _host_tables(head_dim: int, rope_theta: float, size: int, attempts: int = 4) -> tuple[Tensor, Tensor]:
+    """float32 cos / sin [size, head_dim // 2] on the host, accepted only when two
+    computations agree bit for bit.
+
+    On the GPU hosts a long vectorised torch CPU loop has been seen to return, now
+    and then, a contiguous run of slightly wrong values (errors growing with the
+    angle, up to 1e-4; the same call repeated is exact). A table built from such
+    a run would put rotated keys 1 ulp off the reference's, so the table is
+    computed twice and recomputed until both agree.
+    """
+    def once() -> tuple[Tensor, Tensor]:
+        inv_freq = 1.0 / (rope_theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim))
+        freqs = torch.arange(size, dtype=torch.float32).unsqueeze(-1) * inv_freq
+        return freqs.cos(), freqs.sin()
+
+    first = once()
+    for _ in range(attempts):
+        second = once()
+        if torch.equal(first[0], second[0]) and torch.equal(first[1], second[1]):
+            return first
+        first = second
+    raise RuntimeError("rope_tables: the host's cos / sin computations disagree between attempts")
 
 
 def _positions_i64(position_ids: Tensor | np.ndarray, device: torch.device) -> Tensor:
