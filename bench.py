@@ -275,6 +275,18 @@ def max_over_ranks(x: float, world: int, device) -> float:
     return float(t.item())
 
 
+def gather_over_ranks(x: float, world: int, device) -> list[float]:
+    """Every rank's value, in rank order (an all-gather every rank takes part in)."""
+    if world == 1:
+        return [x]
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(o.item()) for o in out]
+
+
 def barrier(world: int, device) -> None:
     if world > 1:
         import torch.distributed as dist
@@ -462,15 +474,40 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
         e2e_step(i)
     e1.record(comp)
     torch.cuda.synchronize(device)
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world, device)
+    own_ms = e0.elapsed_time(e1)
+    e2e_ms = max_over_ranks(own_ms, world, device)
     if int(status_host.item()) != _lib.OK:
         raise RuntimeError("device status error in the e2e region")
     h2d = int(sets[0][0].numel() * 8 + sets[0][1].numel() * 2 * 2)
+    # the same host-to-device copies alone (no scatter), every rank at once: the
+    # rate the host link gives this rank while all ranks copy
+    barrier(world, device)
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(copy_stream):
+        c0.record(copy_stream)
+        for i in range(e2e_steps):
+            hs, hk, hv = pinned[i % n_sets]
+            ds, dk, dv = dev_bufs[i % 2]
+            ds.copy_(hs, non_blocking=True)
+            dk.copy_(hk, non_blocking=True)
+            dv.copy_(hv, non_blocking=True)
+        c1.record(copy_stream)
+    torch.cuda.synchronize(device)
+    copy_gbs = h2d * e2e_steps / (c0.elapsed_time(c1) / 1e3) / 1e9
+    e2e_h2d_gbs = gather_over_ranks(h2d * e2e_steps / (own_ms / 1e3) / 1e9, world, device)
+    copy_only_gbs = gather_over_ranks(copy_gbs, world, device)
+    frac = min(a / b for a, b in zip(e2e_h2d_gbs, copy_only_gbs))
     e2e = {"value": round(world * step_bytes * e2e_steps / (e2e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "steps": e2e_steps,
            "path": "augur_b200.batched.write_paged_kv_batch (ctypes -> augur_kv_scatter)",
            "pipeline": "pinned host -> device on a copy stream into two device buffers, overlapping the "
-                       "previous step's scatter; status read back every step"}
+                       "previous step's scatter; status read back every step",
+           "h2d_GBps_per_rank": [round(x, 1) for x in e2e_h2d_gbs],
+           "h2d_copy_only_GBps_per_rank": [round(x, 1) for x in copy_only_gbs],
+           "bound": ("host-to-device copies: each rank's e2e moves its inputs at "
+                     f"{100 * frac:.0f} % or more of the rate the same copies reach alone"
+                     if frac >= 0.85 else
+                     f"not the host link: e2e copies run at {100 * frac:.0f} % of the copy-only rate")}
     del pinned, dev_bufs
     graph.reset()
     if rem_graph is not None:
