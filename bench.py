@@ -319,6 +319,26 @@ def cpu_scatter_passes(seconds: float, min_passes: int = 2, threads: int | None 
     return scatter_bytes(int(lens.sum())) * n / el / 1e9, n, threads, el / n
 
 
+def cpu_copy_runs(src_k, src_v, dst_k, dst_v, runs, n_bytes: int, seconds: float = 1.0) -> dict:
+    """The same row runs copied on the host by the C oracle (the reference's copy as
+    per-row memcpy, all host threads), over host copies of the caches; bounded to about
+    `seconds` of work after one pass that touches the destination."""
+    from oracle import kv_oracle
+
+    threads = kv_oracle.max_threads()
+    r = runs.cpu().numpy() if isinstance(runs, torch.Tensor) else np.asarray(runs)
+    kv_oracle.copy_runs(src_k, src_v, dst_k, dst_v, r, threads)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        kv_oracle.copy_runs(src_k, src_v, dst_k, dst_v, r, threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if n >= 2 and el >= seconds:
+            break
+    return {"cpu_ms": round(el / n * 1e3, 3), "cpu_GBps": round(n_bytes * n / el / 1e9, 2), "cpu_threads": threads,
+            "cpu_kind": "port (C oracle copy_runs)"}
+
+
 def cpu_reference_torch_loop(n_seqs: int = 8, threads: int | None = None) -> dict:
     """The reference's own CPU path for the prefill scatter, timed on this host: its
     per-token torch loop (augur/paged_kv_cache.py:188-192, restated in the oracle because
@@ -516,7 +536,7 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
 
     extra = {}
     if not args.skip_extras:
-        extra = run_extras(device)
+        extra = run_extras(device, cpu=world == 1 and not args.skip_cpu)  # host legs on one GPU runs only
     del pool
     torch.cuda.empty_cache()
     if not args.skip_scaleout:
@@ -991,7 +1011,7 @@ def run_cow_only(device) -> dict:
     return {"cow_blocks": copied, **bench_cow_device(device, pool, parent, forks, 1000, flush)}
 
 
-def bench_cow_device(device, pool, parent, forks, prefix_len: int, flush) -> dict:
+def bench_cow_device(device, pool, parent, forks, prefix_len: int, flush, cpu: bool = False) -> dict:
     """The copy-on-write launch alone: the parent's partial block copied into every fork's
     private block (all layers, K and V), replayed from a CUDA graph with L2 flushed before
     each replay. Algorithmic bytes: every copied row read once and written once (the
@@ -1030,13 +1050,23 @@ def bench_cow_device(device, pool, parent, forks, prefix_len: int, flush) -> dic
     nbytes = 2 * len(forks) * r * L * TOKEN_LAYER_BYTES + runs_t.numel() * 4
     peak, kind = load_peaks()
     gbs = nbytes / (ms / 1e3) / 1e9
-    return {"cow_us_device": round(ms * 1e3, 2), "cow_bytes": nbytes, "cow_GBps_device": round(gbs, 1),
-            "cow_frac_of_hbm_peak": round(gbs / peak, 4), "cow_kernel": "copy_runs_vec_kernel<16>",
-            "cow_timed": "CUDA graph of the one copy launch, L2 flushed before each replay"}
+    res = {"cow_us_device": round(ms * 1e3, 2), "cow_bytes": nbytes, "cow_GBps_device": round(gbs, 1),
+           "cow_frac_of_hbm_peak": round(gbs / peak, 4), "cow_kernel": "copy_runs_vec_kernel<16>",
+           "cow_timed": "CUDA graph of the one copy launch, L2 flushed before each replay"}
+    if cpu:  # the same runs on a host pool of the same shape (the copied rows hold the device's values)
+        hk = torch.empty(pool.keys.shape, dtype=pool.keys.dtype)
+        hv = torch.empty_like(hk)
+        hk[:, parent.block_ids[j]] = pool.keys[:, parent.block_ids[j]].cpu()
+        hv[:, parent.block_ids[j]] = pool.values[:, parent.block_ids[j]].cpu()
+        c = cpu_copy_runs(hk, hv, hk, hv, runs_t, nbytes)
+        res.update({"cow_" + k: v for k, v in c.items()})
+        res["cow_gpu_over_cpu"] = round(c["cpu_ms"] / (ms or 1e-9), 1)
+        del hk, hv
+    return res
 
 
 def run_extras(device, handoff_only: bool = False, attention_only: bool = False, rope_only: bool = False,
-               offload_only: bool = False) -> dict:
+               offload_only: bool = False, cpu: bool = False) -> dict:
     """Config 3 handoff + decode append and config 4 fork/COW, timed with CUDA events."""
     import augur_b200 as ab
     from augur_b200 import _lib, _ops, batched
@@ -1076,6 +1106,15 @@ def run_extras(device, handoff_only: bool = False, attention_only: bool = False,
         ms = statistics.median(times[2:])
         out[f"handoff_{name}"] = {"us_per_seq": round(ms * 1e3 / B, 3), "ms": round(ms, 4),
                                   "GBps": round(hbytes / (ms / 1e3) / 1e9, 1), "seqs": B, "tokens": tok}
+    if cpu:  # the same runs from a host copy of the contiguous caches into a host pool
+        sk, sv = src.keys.cpu(), src.values.cpu()
+        hk = torch.empty(pool.keys.shape, dtype=pool.keys.dtype)
+        hv = torch.empty_like(hk)
+        c = cpu_copy_runs(sk, sv, hk, hv, runs, hbytes)
+        c["cpu_us_per_seq"] = round(c["cpu_ms"] * 1e3 / B, 2)
+        c["gpu_over_cpu"] = round(c["cpu_ms"] / out["handoff_vector"]["ms"], 1)
+        out["handoff_vector"].update(c)
+        del sk, sv, hk, hv
     if handoff_only:
         return out
     # decode append: 256 steps of one token per sequence, all layers, captured in one graph
@@ -1160,7 +1199,7 @@ def run_extras(device, handoff_only: bool = False, attention_only: bool = False,
         entry = {"forks": 256, "cow_blocks": copied, "cow_ms_incl_host": round(a.elapsed_time(b), 4),
                  "suffix_GBps": round(scatter_bytes(256 * 128) / (c0.elapsed_time(c) / 1e3) / 1e9, 1)}
         if copied:
-            entry.update(bench_cow_device(device, pool4, parent, forks, prefix_len, flush))
+            entry.update(bench_cow_device(device, pool4, parent, forks, prefix_len, flush, cpu=cpu))
         else:
             out["suffix_prefill_attention"] = bench_prefill_attention(device, pool4, forks, 128, flush)
             out["suffix_prefill_attention_mma_sync"] = bench_prefill_attention(device, pool4, forks, 128, flush,
