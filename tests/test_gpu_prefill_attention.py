@@ -55,11 +55,10 @@ def test_golden_prefill_attention(cuda, golden, case, kernel):
     assert _ops.read_status(cuda) == _lib.OK
 
 
-def _batch(cuda, oracle, dtype, D, Hq, Hkv, prefixes, suffixes, seed, kernel="auto"):
+def _batch(cuda, oracle, dtype, D, Hq, Hkv, prefixes, suffixes, seed, kernel="auto", bs=16):
     """Sequences with the given cached prefixes and new suffixes in one pool; the suffix
     tokens' attention from one launch against the oracle, sequence by sequence."""
     g = torch.Generator().manual_seed(seed)
-    bs = 16
     seq_lens = [p + s for p, s in zip(prefixes, suffixes)]
     NB = sum(-(-n // bs) for n in seq_lens) + 5
     L = 2
@@ -100,6 +99,14 @@ SUFFIXES = [37, 16, 45, 1, 64, 3]
 @pytest.mark.parametrize("D, Hq, Hkv", [(64, 14, 2), (128, 8, 2), (64, 8, 8), (64, 16, 2)])
 def test_batch_matches_oracle(cuda, oracle, dtype, D, Hq, Hkv, kernel):
     _batch(cuda, oracle, dtype, D, Hq, Hkv, PREFIXES, SUFFIXES, seed=D + Hq, kernel=kernel)
+
+
+@pytest.mark.parametrize("kernel", ["tcgen05", "mma_sync", "generic"])
+@pytest.mark.parametrize("bs", [8, 32, 12])
+def test_block_sizes(cuda, oracle, bs, kernel):
+    """Block sizes other than 16: powers of two take the shift, 12 the division, in every
+    kernel's block-table lookup."""
+    _batch(cuda, oracle, torch.bfloat16, 64, 14, 2, PREFIXES, SUFFIXES, seed=bs, kernel=kernel, bs=bs)
 
 
 def test_float32_takes_the_generic_kernel(cuda, oracle):
