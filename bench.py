@@ -339,6 +339,63 @@ def cpu_copy_runs(src_k, src_v, dst_k, dst_v, runs, n_bytes: int, seconds: float
             "cpu_kind": "port (C oracle copy_runs)"}
 
 
+def _host_layer(pool, layer: int):
+    """One layer of a device pool copied to the host, as [1, blocks, heads, rows, dim]."""
+    return pool.keys[layer : layer + 1].cpu(), pool.values[layer : layer + 1].cpu()
+
+
+def cpu_paged_attention(pool, tables, q_host, n_q: int, layer: int, sample: int | None = None) -> dict:
+    """Attention of sequences over their paged K/V on the host, as the reference runs its
+    paged branch one sequence at a time (augur/attention.py:72-86): read_paged_kv, the GQA
+    repeat, q k^T / sqrt(D), masked float32 softmax, P V, by the oracle's torch restatement on
+    all host threads. q_host holds n_q query tokens per sequence, sequence-major. With
+    `sample`, the first `sample` sequences are timed and the layer's time is scaled by
+    sequences."""
+    from oracle import kv_oracle
+
+    hk, hv = _host_layer(pool, layer)
+    seqs = len(tables) if sample is None else min(sample, len(tables))
+    t0 = time.perf_counter()
+    for b in range(seqs):
+        t = tables[b]
+        kk, vv = kv_oracle.read_paged_kv(hk, hv, 0, kv_oracle.RefBlockTable(t.block_ids, BS, t.seq_len))
+        q = q_host[b * n_q : (b + 1) * n_q].transpose(0, 1).unsqueeze(0)  # [1, Hq, n_q, D]
+        if n_q == 1:
+            kv_oracle.decode_attention(q, kk, vv)
+        else:
+            kv_oracle.prefill_attention(q, kk, vv)
+    el = time.perf_counter() - t0
+    per_layer = el * len(tables) / seqs
+    return {"cpu_ms_per_layer": round(per_layer * 1e3, 2), "cpu_threads": torch.get_num_threads(),
+            "cpu_sample": f"{seqs} of {len(tables)} sequences, one layer", "cpu_kind": "port (oracle, torch on host)"}
+
+
+def cpu_rope_write_layer(q_host, k_host, v_host, pos_host, slots_host, theta: float, n_layers: int = 2) -> dict:
+    """The reference's RoPE write on the host per layer: angles and cos / sin from the
+    positions, x * cos + rotate_half(x) * sin for q and k in the dtype (augur/rope.py:29-40,
+    torch on all host threads), then write_paged_kv of k and v through the slots (the C port
+    with all host threads); `n_layers` layers timed."""
+    from oracle import kv_oracle
+
+    T = k_host.shape[1]
+    hk = torch.empty(1, int(slots_host.max()) // BS + 1, H, BS, D, dtype=k_host.dtype)
+    hv = torch.empty_like(hk)
+    threads = kv_oracle.max_threads()
+    t0 = time.perf_counter()
+    for layer in range(n_layers):
+        inv = 1.0 / (theta ** (torch.arange(0, D, 2, dtype=torch.float32) / D))
+        fr = pos_host.to(torch.float32).unsqueeze(-1) * inv
+        emb = torch.cat((fr, fr), dim=-1)
+        c, s_ = emb.cos().unsqueeze(1).to(k_host.dtype), emb.sin().unsqueeze(1).to(k_host.dtype)
+        x, y = q_host[layer], k_host[layer]
+        _ = x * c + torch.cat((-x[..., D // 2 :], x[..., : D // 2]), dim=-1) * s_
+        ke = y * c + torch.cat((-y[..., D // 2 :], y[..., : D // 2]), dim=-1) * s_
+        kv_oracle.scatter_slots(ke.unsqueeze(0), v_host[layer].unsqueeze(0), slots_host, hk, hv, BS, threads=threads)
+    el = time.perf_counter() - t0
+    return {"cpu_us_per_layer": round(el / n_layers * 1e6, 1), "cpu_threads": threads,
+            "cpu_sample": f"{n_layers} of {L} layers, {T} tokens", "cpu_kind": "port (torch ops + C scatter on host)"}
+
+
 def cpu_reference_torch_loop(n_seqs: int = 8, threads: int | None = None) -> dict:
     """The reference's own CPU path for the prefill scatter, timed on this host: its
     per-token torch loop (augur/paged_kv_cache.py:188-192, restated in the oracle because
@@ -586,7 +643,7 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
     return line
 
 
-def bench_decode_attention(device, pool, tables, early_reads: bool = True) -> dict:
+def bench_decode_attention(device, pool, tables, early_reads: bool = True, cpu: bool = False) -> dict:
     """paged_decode_attention for every layer of one decode step, graph-captured, L2 cold.
 
     Algorithmic bytes: every cached K and V row of every sequence read once
@@ -638,10 +695,13 @@ def bench_decode_attention(device, pool, tables, early_reads: bool = True) -> di
            "timed": "CUDA graph of 24 per-layer launches, L2 flushed"}
     if early_reads:
         res["us_per_layer_without_early_reads"] = bench_decode_attention(device, pool, tables, False)["us_per_layer"]
+    if cpu:
+        res.update(cpu_paged_attention(pool, tables, qs[0].cpu(), 1, 0))
+        res["gpu_over_cpu"] = round(res["cpu_ms_per_layer"] * 1e3 / res["us_per_layer"], 1)
     return res
 
 
-def bench_rope(device, pool, reps: int = 7) -> dict:
+def bench_rope(device, pool, reps: int = 7, cpu: bool = False) -> dict:
     """RoPE fused with the paged write for a config-2-sized prefill (8,192 tokens, one layer per
     launch, all 24 layers), against the same math as separate torch ops plus the scatter.
 
@@ -705,10 +765,15 @@ def bench_rope(device, pool, reps: int = 7) -> dict:
     nbytes = T * 4752
     peak, _ = load_peaks()
     gbs = nbytes / (res["fused"] / 1e6) / 1e9
-    return {"us_per_layer_fused": round(res["fused"], 2),
-            "us_per_layer_torch_ops_then_scatter": round(res["torch_ops_then_scatter"], 2),
-            "tokens": T, "GBps_fused": round(gbs, 1), "frac_of_hbm_peak": round(gbs / peak, 4),
-            "timed": "CUDA graph of 24 per-layer launches; q, k, v of all layers (450 MB) exceed L2"}
+    out = {"us_per_layer_fused": round(res["fused"], 2),
+           "us_per_layer_torch_ops_then_scatter": round(res["torch_ops_then_scatter"], 2),
+           "tokens": T, "GBps_fused": round(gbs, 1), "frac_of_hbm_peak": round(gbs / peak, 4),
+           "timed": "CUDA graph of 24 per-layer launches; q, k, v of all layers (450 MB) exceed L2"}
+    if cpu:
+        c = cpu_rope_write_layer(q[:2].cpu(), k[:2].cpu(), v[:2].cpu(), pos.cpu(), slots.cpu().numpy(), theta)
+        out.update(c)
+        out["gpu_over_cpu"] = round(c["cpu_us_per_layer"] / res["fused"], 1)
+    return out
 
 
 def bench_decode_step(device, pool, tables) -> dict:
@@ -906,7 +971,8 @@ def bench_offload(device, pool, tables, n_seqs: int = 16) -> dict:
     return out
 
 
-def bench_prefill_attention(device, pool, tables, suffix: int, flush, kernel: str = "auto") -> dict:
+def bench_prefill_attention(device, pool, tables, suffix: int, flush, kernel: str = "auto",
+                            cpu: bool = False) -> dict:
     """Suffix prefill attention over shared prefixes (config 4: 256 forks of one prefix, each
     with its own suffix already written): every layer, the suffix queries of all forks attend
     to their prefix and causally to their suffix, one paged_prefill_attention launch per layer,
@@ -957,12 +1023,16 @@ def bench_prefill_attention(device, pool, tables, suffix: int, flush, kernel: st
     except Exception:
         tf_peak, tf_kind = 1590.0, "fallback"
     tflops = flops / (ms / 1e3) / 1e12
-    return {"seqs": B, "suffix_tokens": suffix, "cached_tokens_per_seq": seq[0], "us_per_layer": round(ms * 1e3, 2),
-            "kv_GBps": round(kv_bytes / (ms / 1e3) / 1e9, 1), "kv_frac_of_hbm_peak": round(kv_bytes / (ms / 1e3) / 1e9 / peak, 4),
-            "TFLOPs": round(tflops, 1), "tensor_frac": round(tflops / tf_peak, 4), "tensor_peak_source": tf_kind,
-            "kernel": ("attn_prefill_mma_kernel<bf16,64> (mma.sync)" if kernel == "mma_sync"
-                       else "attn_prefill_umma_kernel<bf16,64> (tcgen05, TMEM accumulators)"),
-            "timed": "CUDA graph of 24 per-layer launches, L2 flushed; the forks share the prefix's blocks"}
+    res = {"seqs": B, "suffix_tokens": suffix, "cached_tokens_per_seq": seq[0], "us_per_layer": round(ms * 1e3, 2),
+           "kv_GBps": round(kv_bytes / (ms / 1e3) / 1e9, 1), "kv_frac_of_hbm_peak": round(kv_bytes / (ms / 1e3) / 1e9 / peak, 4),
+           "TFLOPs": round(tflops, 1), "tensor_frac": round(tflops / tf_peak, 4), "tensor_peak_source": tf_kind,
+           "kernel": ("attn_prefill_mma_kernel<bf16,64> (mma.sync)" if kernel == "mma_sync"
+                      else "attn_prefill_umma_kernel<bf16,64> (tcgen05, TMEM accumulators)"),
+           "timed": "CUDA graph of 24 per-layer launches, L2 flushed; the forks share the prefix's blocks"}
+    if cpu:
+        res.update(cpu_paged_attention(pool, tables, q.cpu(), suffix, 0, sample=8))
+        res["gpu_over_cpu"] = round(res["cpu_ms_per_layer"] * 1e3 / res["us_per_layer"], 1)
+    return res
 
 
 def run_prefill_attention_only(device) -> dict:
@@ -1151,13 +1221,29 @@ def run_extras(device, handoff_only: bool = False, attention_only: bool = False,
                             "frac_of_hbm_peak": round(abytes * steps / (ms / 1e3) / 1e9 / peak, 4),
                             "hbm_floor_us": round(abytes / peak / 1e3, 3),
                             "timed": "one CUDA graph of 256 append launches (one launch per step, all layers)"}
+    if cpu:  # one step on the host: the C port's write_paged_kv of the 32 tokens, all layers, one thread
+        from oracle import kv_oracle
+
+        hk = torch.empty(pool.keys.shape, dtype=pool.keys.dtype)
+        hv = torch.empty_like(hk)
+        sk, sv, sl = nk[0].cpu(), nv[0].cpu(), slot_t[0].cpu().numpy()
+        kv_oracle.scatter_slots(sk, sv, sl, hk, hv, BS, threads=1)
+        n, t0 = 0, time.perf_counter()
+        while n < 200 or time.perf_counter() - t0 < 0.3:
+            kv_oracle.scatter_slots(sk, sv, sl, hk, hv, BS, threads=1)
+            n += 1
+        cpu_us = (time.perf_counter() - t0) / n * 1e6
+        out["decode_append"].update({"cpu_us_per_step": round(cpu_us, 2), "cpu_threads": 1,
+                                     "cpu_kind": "port (C oracle scatter)",
+                                     "gpu_over_cpu": round(cpu_us / out["decode_append"]["us_per_step"], 1)})
+        del hk, hv
     graph.reset()
     del src, nk, nv
 
     # ---- decode attention reading the pool in place: one decode step of the
     # 32 sequences (each n + 256 tokens long now) across all 24 layers
     if not (rope_only or offload_only):
-        out["decode_attention"] = bench_decode_attention(device, pool, tables)
+        out["decode_attention"] = bench_decode_attention(device, pool, tables, cpu=cpu)
         out["decode_attention_256_seqs"] = bench_decode_attention_large(device)
         out["decode_step"] = bench_decode_step(device, pool, tables)
     if attention_only:
@@ -1168,7 +1254,7 @@ def run_extras(device, handoff_only: bool = False, attention_only: bool = False,
         if offload_only:
             return out
     # ---- RoPE fused with the paged write, config-2-sized prefill, all layers
-    out["rope_scatter"] = bench_rope(device, pool)
+    out["rope_scatter"] = bench_rope(device, pool, cpu=cpu)
     if rope_only:
         return out
 
@@ -1201,7 +1287,7 @@ def run_extras(device, handoff_only: bool = False, attention_only: bool = False,
         if copied:
             entry.update(bench_cow_device(device, pool4, parent, forks, prefix_len, flush, cpu=cpu))
         else:
-            out["suffix_prefill_attention"] = bench_prefill_attention(device, pool4, forks, 128, flush)
+            out["suffix_prefill_attention"] = bench_prefill_attention(device, pool4, forks, 128, flush, cpu=cpu)
             out["suffix_prefill_attention_mma_sync"] = bench_prefill_attention(device, pool4, forks, 128, flush,
                                                                                kernel="mma_sync")
         out[f"prefix_fork_{prefix_len}"] = entry
