@@ -131,10 +131,12 @@ class PagedSequences:
         self.last_cow_blocks = cow_partial_blocks(self.cache, tables)  # one launch; none when nothing is shared
         return tables
 
-    def decode_step(self, seq_ids: Sequence[int]) -> DecodeStep:
+    def decode_step(self, seq_ids: Sequence[int], early_reads: bool = False) -> DecodeStep:
         """The next decode step of these sequences: shared partial last blocks are copied,
-        then each table grows by one position (see DecodeStep)."""
-        return DecodeStep(self.cache, self._prepare_append(seq_ids))
+        then each table grows by one position (see DecodeStep, and its early_reads: the
+        copy-on-write launch here is followed by the step's uploads, so it has finished
+        before the first layer's launch)."""
+        return DecodeStep(self.cache, self._prepare_append(seq_ids), early_reads=early_reads)
 
     def update_graph_step(self, step: DecodeGraphStep, seq_ids: Sequence[int]) -> None:
         """decode_step for a captured step: copy shared partial blocks, then step.update."""

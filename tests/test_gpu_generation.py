@@ -22,7 +22,6 @@ tolerance (1e-2), as the kernels sum in another order.
 
 from __future__ import annotations
 
-import numpy as np
 import pytest
 import torch
 
@@ -57,7 +56,7 @@ def _new_token(i: int, step: int) -> int:
     return 5000 + 101 * i + step
 
 
-def _device_run(cuda):
+def _device_run(cuda, early: bool):
     pool = ab.PagedKVCache(keys=poison_(torch.empty(L, NB, H, BS, D, dtype=DT, device=cuda)),
                            values=poison_(torch.empty(L, NB, H, BS, D, dtype=DT, device=cuda)),
                            block_size=BS, allocator=ab.BlockAllocator(NB))
@@ -86,7 +85,7 @@ def _device_run(cuda):
     for st in range(STEPS):
         for i, sid in enumerate(ids):
             tokens[sid].append(_new_token(i, st))
-        step = seqs.decode_step(ids)
+        step = seqs.decode_step(ids, early_reads=early)
         assert seqs.last_cow_blocks == (N_FORKS if st == 0 else 0)
         outs = []
         for layer in range(L):
@@ -105,8 +104,11 @@ def _device_run(cuda):
     return ids, prompts, prefill, decode, gathered
 
 
-def test_batched_generation_matches_the_reference_one_sequence_at_a_time(cuda, oracle):
-    ids, prompts, prefill, decode, gathered = _device_run(cuda)
+@pytest.mark.parametrize("early", [False, True])
+def test_batched_generation_matches_the_reference_one_sequence_at_a_time(cuda, oracle, early):
+    """early: every decode layer reads lengths, tables and pool rows before the launch ahead
+    of it has finished (the new tokens' rows after it)."""
+    ids, prompts, prefill, decode, gathered = _device_run(cuda, early)
     NBR = 512
     rk = poison_(torch.empty(L, NBR, H, BS, D, dtype=DT))
     rv = poison_(torch.empty(L, NBR, H, BS, D, dtype=DT))
