@@ -597,7 +597,7 @@ def run_ours(args, world: int, rank: int, local: int) -> dict | None:
     del pool
     torch.cuda.empty_cache()
     if not args.skip_scaleout:
-        # north_star's multi-GPU workloads, every rank taking part: config 5
+        # the multi-GPU workloads, every rank taking part: config 5
         # sharded over the ranks (strong scaling) and, at even N, the
         # disaggregated push; both checked against the oracle on every rank
         box = box_phase(world, rank, local)
