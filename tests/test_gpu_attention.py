@@ -263,7 +263,7 @@ def test_back_to_back_launches_share_the_workspace(cuda, oracle):
         _case(cuda, oracle, torch.float16, len(lens), 14, 2, 64, 16, lens, seed, False)
 
 
-@pytest.mark.parametrize("nseq", [5, 40, 300])
+@pytest.mark.parametrize("nseq", [5, 40, 300, 1000])
 def test_early_reads_back_to_back_layers(cuda, oracle, nseq):
     """AUGUR_KV_ATTN_EARLY_READS: each layer's launch reads lengths, tables and pool rows
     before the previous layer's launch (which shares its workspace) has finished. Six
@@ -271,10 +271,12 @@ def test_early_reads_back_to_back_layers(cuda, oracle, nseq):
     outputs of launches without early reads and the oracle's within tolerance (a small
     batch's plan may take fewer, longer chunks with early reads, so the summation order can
     differ). Five sequences leave most CTAs without an item (they exit through the
-    scheduler's counters); 300 take several items per CTA."""
+    scheduler's counters); 300 take several items per CTA; 1,000 short ones are more
+    (sequence, KV head) units than the plan's item bound, so every sequence runs unsplit."""
     L, Hq, Hkv, D, bs = 6, 14, 2, 64, 16
     rng = np.random.default_rng(nseq)
-    lens = [int(x) for x in rng.integers(1, 2500 if nseq < 100 else 900, size=nseq)]
+    hi = 2500 if nseq < 100 else (900 if nseq < 1000 else 64)
+    lens = [int(x) for x in rng.integers(1, hi, size=nseq)]
     nblk = [-(-n // bs) for n in lens]
     NB = sum(nblk) + 3
     g = torch.Generator().manual_seed(nseq)
