@@ -43,6 +43,7 @@
 #include <string.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "augur_kv.h"
 #include "common.cuh"
@@ -662,33 +663,49 @@ __global__ void __launch_bounds__(kUThreads, UCfg<D>::kMinCtas) attn_prefill_umm
     float sv[KH];
     tmem_ld32(tmem + uint32_t(s & 1) * kUKeys + my_lanes + half * KH, sv);
     float mx = kNegInf;
+    // one loop body per rounding mode, chosen once per stage (CTA-uniform), so
+    // the unrolled loop issues only the mode's own instructions
+    auto scores = [&](auto twice, auto divide, auto masked) {
 #pragma unroll
-    for (int j = 0; j < KH; j += 2) {
-      float2 r = M::round2(sv[j], sv[j + 1]);
-      float x0, x1;
-      if (round_twice) {
-        if (!a.scale_exact) {
-          r.x /= a.sqrt_d;
-          r.y /= a.sqrt_d;
+      for (int j = 0; j < KH; j += 2) {
+        float2 r = M::round2(sv[j], sv[j + 1]);
+        float x0, x1;
+        if constexpr (decltype(twice)::value) {
+          if constexpr (decltype(divide)::value) {
+            r.x /= a.sqrt_d;
+            r.y /= a.sqrt_d;
+          } else {
+            r.x *= scale1;
+            r.y *= scale1;
+          }
+          r = M::round2(r.x, r.y);
+          x0 = r.x * kLog2e;
+          x1 = r.y * kLog2e;
         } else {
-          r.x *= scale1;
-          r.y *= scale1;
+          x0 = r.x * scale1;
+          x1 = r.y * scale1;
         }
-        r = M::round2(r.x, r.y);
-        x0 = r.x * kLog2e;
-        x1 = r.y * kLog2e;
-      } else {
-        x0 = r.x * scale1;
-        x1 = r.y * scale1;
+        if constexpr (decltype(masked)::value) {
+          const int key = s * kUKeys + half * KH + j;
+          x0 = key > qp ? kNegInf : x0;
+          x1 = key + 1 > qp ? kNegInf : x1;
+        }
+        sv[j] = x0;
+        sv[j + 1] = x1;
+        mx = fmaxf(mx, fmaxf(x0, x1));
       }
-      if (need_mask) {
-        const int key = s * kUKeys + half * KH + j;
-        x0 = key > qp ? kNegInf : x0;
-        x1 = key + 1 > qp ? kNegInf : x1;
-      }
-      sv[j] = x0;
-      sv[j + 1] = x1;
-      mx = fmaxf(mx, fmaxf(x0, x1));
+    };
+    using yes = std::true_type;
+    using no = std::false_type;
+    if (!round_twice) {
+      if (need_mask) scores(no{}, no{}, yes{});
+      else scores(no{}, no{}, no{});
+    } else if (a.scale_exact) {
+      if (need_mask) scores(yes{}, no{}, yes{});
+      else scores(yes{}, no{}, no{});
+    } else {
+      if (need_mask) scores(yes{}, yes{}, yes{});
+      else scores(yes{}, yes{}, no{});
     }
     // the row's maximum over both halves (red_m is rewritten only after the
     // next stage's first barrier, when both halves have read it)
