@@ -55,6 +55,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "augur_kv.h"
 #include "common.cuh"
@@ -781,35 +782,41 @@ __global__ void __launch_bounds__(SplitCfg<D, NS>::kThreads, (D == 64 && NT == 1
     // round as the reference's dtype matmul and scalar division do, move to
     // base 2, mask the tail of the last stage (rows are tokens)
     const bool full = s0 + kStageTok <= tok1;
+    // one loop body per rounding mode, chosen once per stage (warp-uniform)
+    auto scores = [&](auto twice, auto divide) {
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt) {
+      for (int mt = 0; mt < 2; ++mt) {
 #pragma unroll
-      for (int hp = 0; hp < 2; ++hp) {
-        const bool dead = !full && s0 + mt * 16 + hp * 8 + g >= tok1;
+        for (int hp = 0; hp < 2; ++hp) {
+          const bool dead = !full && s0 + mt * 16 + hp * 8 + g >= tok1;
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          float2 r = round2<T>(s[mt][nt][2 * hp], s[mt][nt][2 * hp + 1]);
-          float x0, x1;
-          if (round_twice) {
-            if (!a.scale_exact) {
-              r.x /= a.sqrt_d;
-              r.y /= a.sqrt_d;
+          for (int nt = 0; nt < NT; ++nt) {
+            float2 r = round2<T>(s[mt][nt][2 * hp], s[mt][nt][2 * hp + 1]);
+            float x0, x1;
+            if constexpr (decltype(twice)::value) {
+              if constexpr (decltype(divide)::value) {
+                r.x /= a.sqrt_d;
+                r.y /= a.sqrt_d;
+              } else {
+                r.x *= scale1;
+                r.y *= scale1;
+              }
+              r = round2<T>(r.x, r.y);
+              x0 = r.x * kLog2e;
+              x1 = r.y * kLog2e;
             } else {
-              r.x *= scale1;
-              r.y *= scale1;
+              x0 = r.x * scale1;
+              x1 = r.y * scale1;
             }
-            r = round2<T>(r.x, r.y);
-            x0 = r.x * kLog2e;
-            x1 = r.y * kLog2e;
-          } else {
-            x0 = r.x * scale1;
-            x1 = r.y * scale1;
+            s[mt][nt][2 * hp] = dead ? kNegInf : x0;
+            s[mt][nt][2 * hp + 1] = dead ? kNegInf : x1;
           }
-          s[mt][nt][2 * hp] = dead ? kNegInf : x0;
-          s[mt][nt][2 * hp + 1] = dead ? kNegInf : x1;
         }
       }
-    }
+    };
+    if (!round_twice) scores(std::false_type{}, std::false_type{});
+    else if (a.scale_exact) scores(std::true_type{}, std::false_type{});
+    else scores(std::true_type{}, std::true_type{});
     // column (head) maxima over the stage's 32 tokens: this lane's 4, then the 8 g-lanes
     float mnew[NT][2];
 #pragma unroll

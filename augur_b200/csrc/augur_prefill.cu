@@ -296,37 +296,52 @@ __global__ void __launch_bounds__(kMaxGroups * 32, D == 64 ? AUGUR_KV_PREFILL_MI
     // mask only where the stage's last key is past the tile's first query
     const bool need_mask = (s + 1) * kKT - 1 > past + i0;
     float rmax[2] = {kNegInf, kNegInf};
+    // one loop body per rounding mode and mask case, chosen once per stage
+    auto scores = [&](auto twice, auto divide, auto masked) {
 #pragma unroll
-    for (int j = 0; j < NJ; ++j) {
+      for (int j = 0; j < NJ; ++j) {
 #pragma unroll
-      for (int hp = 0; hp < 2; ++hp) {
-        float2 r = M::round2(sc[j][2 * hp], sc[j][2 * hp + 1]);
-        float x0, x1;
-        if (round_twice) {
-          if (!a.scale_exact) {
-            r.x /= a.sqrt_d;
-            r.y /= a.sqrt_d;
+        for (int hp = 0; hp < 2; ++hp) {
+          float2 r = M::round2(sc[j][2 * hp], sc[j][2 * hp + 1]);
+          float x0, x1;
+          if constexpr (decltype(twice)::value) {
+            if constexpr (decltype(divide)::value) {
+              r.x /= a.sqrt_d;
+              r.y /= a.sqrt_d;
+            } else {
+              r.x *= scale1;
+              r.y *= scale1;
+            }
+            r = M::round2(r.x, r.y);
+            x0 = r.x * kLog2e;
+            x1 = r.y * kLog2e;
           } else {
-            r.x *= scale1;
-            r.y *= scale1;
+            x0 = r.x * scale1;
+            x1 = r.y * scale1;
           }
-          r = M::round2(r.x, r.y);
-          x0 = r.x * kLog2e;
-          x1 = r.y * kLog2e;
-        } else {
-          x0 = r.x * scale1;
-          x1 = r.y * scale1;
+          if constexpr (decltype(masked)::value) {
+            const int key = s * kKT + j * 8 + 2 * t;
+            const int qp = hp ? qp1 : qp0;
+            x0 = key > qp ? kNegInf : x0;
+            x1 = key + 1 > qp ? kNegInf : x1;
+          }
+          sc[j][2 * hp] = x0;
+          sc[j][2 * hp + 1] = x1;
+          rmax[hp] = fmaxf(rmax[hp], fmaxf(x0, x1));
         }
-        if (need_mask) {
-          const int key = s * kKT + j * 8 + 2 * t;
-          const int qp = hp ? qp1 : qp0;
-          x0 = key > qp ? kNegInf : x0;
-          x1 = key + 1 > qp ? kNegInf : x1;
-        }
-        sc[j][2 * hp] = x0;
-        sc[j][2 * hp + 1] = x1;
-        rmax[hp] = fmaxf(rmax[hp], fmaxf(x0, x1));
       }
+    };
+    using yes = std::true_type;
+    using no = std::false_type;
+    if (!round_twice) {
+      if (need_mask) scores(no{}, no{}, yes{});
+      else scores(no{}, no{}, no{});
+    } else if (a.scale_exact) {
+      if (need_mask) scores(yes{}, no{}, yes{});
+      else scores(yes{}, no{}, no{});
+    } else {
+      if (need_mask) scores(yes{}, yes{}, yes{});
+      else scores(yes{}, yes{}, no{});
     }
     float alpha[2];
 #pragma unroll
