@@ -178,6 +178,7 @@ class DecodeGraphStep:
             self._q_rot = torch.empty(batch, n_q_heads, D, dtype=dt, device=dev)
             self._status = _ops.status_word(dev)
         self._copied: torch.cuda.Event | None = None
+        self._rows: list[list[int] | None] = [None] * batch  # block ids each staging row holds
         a = self._args = _lib.DecodeArgs()
         kc = cache.keys
         a.k_pool, a.v_pool = kc.data_ptr(), cache.values.data_ptr()
@@ -219,10 +220,16 @@ class DecodeGraphStep:
         h32 = self._h32.numpy()
         lens, blocks = h32[: self.batch], h32[self.batch :].reshape(self.batch, self.max_blocks)
         lens[:n], lens[n:] = [t.seq_len for t in tables], 0
-        blocks.fill(-1)
-        for b, t in enumerate(tables):
-            ids = t.block_ids[: self.max_blocks]  # positions below capacity live in these
-            blocks[b, : len(ids)] = ids
+        # the staging buffer keeps the rows it was given: a row is rewritten only
+        # when its table's block ids differ from what it holds (a block appended,
+        # a copied last block, another sequence in the row), which spares the
+        # conversion of every id on every step
+        for b in range(self.batch):
+            ids = tables[b].block_ids[: self.max_blocks] if b < n else []  # positions below capacity
+            if self._rows[b] != ids:
+                blocks[b].fill(-1)
+                blocks[b, : len(ids)] = ids
+                self._rows[b] = ids
         dev = self.cache.keys.device
         with _ops._DeviceGuard(dev):
             self._d64.copy_(self._h64, non_blocking=True)
