@@ -158,6 +158,67 @@ def test_graph_step_replays_match_eager_steps(cuda, early):
     assert _ops.read_status(cuda) == _lib.OK
 
 
+def test_graph_step_rows_follow_reordered_batches(cuda):
+    """DecodeGraphStep keeps each staging row of the block tables until that row's block ids
+    change. The same captured step, replayed after the batch's sequences change rows from
+    step to step, matches eager steps in the same order: the same pool bits, outputs within
+    the bf16 tolerance."""
+    from augur_b200.decode import DecodeGraphStep
+
+    L, H, Hq, D, bs, NB = 2, 2, 14, 64, 16, 96
+    prior = [3, 15, 16, 40, 300]
+    orders = [[0, 1, 2, 3, 4], [4, 0, 1, 2, 3], [2, 4, 0, 3, 1], [2, 4, 0, 3, 1], [1, 0, 4, 2, 3]]
+    g = torch.Generator().manual_seed(57)
+
+    def fresh():
+        pool = ab.PagedKVCache(keys=poison_(torch.empty(L, NB, H, bs, D, dtype=torch.bfloat16, device=cuda)),
+                               values=poison_(torch.empty(L, NB, H, bs, D, dtype=torch.bfloat16, device=cuda)),
+                               block_size=bs, allocator=ab.BlockAllocator(NB))
+        return pool, [ab.SequenceBlockTable.empty(bs) for _ in prior]
+
+    (pool_e, tabs_e), (pool_g, tabs_g) = fresh(), fresh()
+    T = sum(prior)
+    pk = torch.randn(L, T, H, D, generator=g).to(torch.bfloat16).to(cuda)
+    pv = torch.randn(L, T, H, D, generator=g).to(torch.bfloat16).to(cuda)
+    for pool, tabs in ((pool_e, tabs_e), (pool_g, tabs_g)):
+        sm = batched.prefill_slot_mapping(tabs, prior, pool.allocator)
+        flat = np.concatenate([sm[b, :n] for b, n in enumerate(prior)])
+        batched.write_paged_kv_batch(pool, pk, pv, torch.from_numpy(flat).to(cuda))
+    B = len(prior)
+    q_in = torch.zeros(L, B, Hq, 1, D, dtype=torch.bfloat16, device=cuda)
+    k_in = torch.zeros(L, B, H, 1, D, dtype=torch.bfloat16, device=cuda)
+    v_in = torch.zeros(L, B, H, 1, D, dtype=torch.bfloat16, device=cuda)
+    gs = DecodeGraphStep(pool_g, B, 24, Hq, THETA)
+    graph = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream(cuda)
+    cs.wait_stream(torch.cuda.current_stream(cuda))
+    outs_g = None
+    for s, order in enumerate(orders):
+        q = torch.randn(L, B, Hq, 1, D, generator=g).to(torch.bfloat16).to(cuda)
+        k = torch.randn(L, B, H, 1, D, generator=g).to(torch.bfloat16).to(cuda)
+        v = torch.randn(L, B, H, 1, D, generator=g).to(torch.bfloat16).to(cuda)
+        step = DecodeStep(pool_e, [tabs_e[i] for i in order])
+        outs_e = [paged_decode_layer(step, pool_e, layer, q[layer], k[layer], v[layer], THETA) for layer in range(L)]
+        with torch.cuda.stream(cs):
+            q_in.copy_(q)
+            k_in.copy_(k)
+            v_in.copy_(v)
+            gs.update([tabs_g[i] for i in order])
+            if s == 0:
+                with torch.cuda.graph(graph, stream=cs):
+                    outs_g = [gs.layer(layer, q_in[layer], k_in[layer], v_in[layer]) for layer in range(L)]
+            graph.replay()
+        torch.cuda.synchronize(cuda)
+        for layer in range(L):
+            torch.testing.assert_close(outs_g[layer].float(), outs_e[layer].float(), rtol=1e-2, atol=1e-2,
+                                       msg=lambda m, s=s, layer=layer: f"step {s} layer {layer}: {m}")
+    graph.reset()
+    assert [t.block_ids for t in tabs_g] == [t.block_ids for t in tabs_e]
+    assert_bits_equal(pool_g.keys, pool_e.keys.cpu(), "pool keys")
+    assert_bits_equal(pool_g.values, pool_e.values.cpu(), "pool values")
+    assert _ops.read_status(cuda) == _lib.OK
+
+
 def test_graph_step_rejects_what_it_cannot_describe(cuda):
     from augur_b200.decode import DecodeGraphStep
 
