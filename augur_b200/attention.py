@@ -14,6 +14,7 @@ order.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 from collections.abc import Sequence
 
@@ -70,27 +71,64 @@ def _workspace(lib, device: torch.device, st: torch.cuda.Stream, sizes: tuple) -
 class DecodeTables:
     """Device copy of a batch's block tables and lengths, reusable across layers.
 
-    blocks: int32 [batch, max_blocks] (unused entries -1), lens: int32 [batch].
+    blocks: int32 [batch, max_blocks] (unused entries -1), lens: int32 [batch]: views of
+    one device buffer filled by one copy (rows, then lengths).
     """
 
     def __init__(self, tables: Sequence[SequenceBlockTable], device: torch.device,
-                 seq_lens: Sequence[int] | None = None) -> None:
+                 seq_lens: Sequence[int] | None = None, stream: torch.cuda.Stream | None = None) -> None:
+        """stream: the stream the copy is ordered on (the current one by default); launches
+        on another stream must wait for it."""
         lens = [t.seq_len for t in tables] if seq_lens is None else [int(n) for n in seq_lens]
         if len(lens) != len(tables):
             raise ValueError("seq_lens and tables must have the same length")
-        width = max([len(t.block_ids) for t in tables] + [1])
-        host = np.full((len(tables), width), -1, dtype=np.int32)
-        for b, t in enumerate(tables):
-            if lens[b] < 0 or -(-lens[b] // t.block_size) > len(t.block_ids):
-                raise ValueError("position exceeds block table capacity")
-            host[b, : len(t.block_ids)] = t.block_ids
+        host, width = _table_rows(tables, lens, 0)
+        self._set(upload_int32(host, device, stream), 0, tables, lens, width)
+
+    def _set(self, dev: Tensor, offset: int, tables: Sequence[SequenceBlockTable], lens: list[int],
+             width: int) -> None:
+        """Views of dev laid out as _table_rows packs them from int32 element `offset` on."""
+        B = len(tables)
+        self.blocks = dev[offset: offset + B * width].view(B, width)
+        self.lens = dev[offset + B * width: offset + B * width + B]
         self.block_size = tables[0].block_size if tables else 1
-        if any(t.block_size != self.block_size for t in tables):
-            raise ValueError("all block tables must share one block_size")
-        self.blocks = torch.from_numpy(host).to(device)
-        self.lens = torch.tensor(lens, dtype=torch.int32).to(device)
         self.max_seq_len = max(lens, default=0)
-        self.batch = len(tables)
+        self.batch = B
+
+
+def _table_rows(tables: Sequence[SequenceBlockTable], lens: list[int], offset: int) -> tuple[np.ndarray, int]:
+    """An int32 host array of `offset` leading elements (left for the caller), then the block
+    ids ``[batch, width]`` row by row (unused entries -1), then the lengths; and width.
+    Checks that each length fits its table and that the tables share one block_size."""
+    B = len(tables)
+    width = max([len(t.block_ids) for t in tables] + [1])
+    host = np.empty(offset + B * width + B, dtype=np.int32)
+    rows = host[offset: offset + B * width].reshape(B, width)
+    rows.fill(-1)
+    for b, t in enumerate(tables):
+        if lens[b] < 0 or -(-lens[b] // t.block_size) > len(t.block_ids):
+            raise ValueError("position exceeds block table capacity")
+        rows[b, : len(t.block_ids)] = t.block_ids
+    host[offset + B * width:] = lens
+    if any(t.block_size != tables[0].block_size for t in tables):
+        raise ValueError("all block tables must share one block_size")
+    return host, width
+
+
+def upload_int32(host: np.ndarray, device: torch.device, stream: torch.cuda.Stream | None = None) -> Tensor:
+    """A 1-D int32 host array on device in one copy. To a GPU it goes through pinned memory
+    as a copy ordered on `stream` (the current stream when None) that the host does not wait
+    for: kernels on that stream see it, another stream must wait on that one first. The
+    staging block is not reused before the copy has run (torch's pinned allocator records
+    the copy)."""
+    t = torch.from_numpy(host)
+    if torch.device(device).type != "cuda" or t.numel() == 0:
+        return t.to(device)
+    with torch.cuda.stream(stream) if stream is not None else contextlib.nullcontext():
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("host data cannot be uploaded inside a CUDA graph capture: "
+                               "build the device tables before capturing")
+        return t.pin_memory().to(device, non_blocking=True)
 
 
 def paged_decode_attention(
@@ -135,7 +173,7 @@ def paged_decode_attention(
         raise ValueError("query and cache dtypes differ")
     if q3.stride(-1) != 1:
         q3 = q3.contiguous()
-    dt = tables if isinstance(tables, DecodeTables) else DecodeTables(tables, cache.keys.device)
+    dt = tables if isinstance(tables, DecodeTables) else DecodeTables(tables, cache.keys.device, stream=stream)
     if dt.batch != B:
         raise ValueError("one block table per sequence is required")
     if dt.block_size != bs:
@@ -179,7 +217,9 @@ class PrefillQueries:
     CUDA graph, where no host data may be uploaded): starts int32 [batch + 1], sequence b's
     query tokens being rows [starts[b], starts[b + 1]) of q."""
 
-    def __init__(self, q_lens: Sequence[int], device: torch.device) -> None:
+    def __init__(self, q_lens: Sequence[int], device: torch.device,
+                 stream: torch.cuda.Stream | None = None) -> None:
+        """stream: the stream the copy is ordered on (the current one by default)."""
         lens = np.asarray(q_lens, dtype=np.int64)
         if lens.size and lens.min() < 0:
             raise ValueError("q_lens must be non-negative")
@@ -188,7 +228,7 @@ class PrefillQueries:
         self.lens = lens
         self.total = int(starts[-1])
         self.max_len = int(lens.max(initial=0))
-        self.starts = torch.from_numpy(starts).to(device)
+        self.starts = upload_int32(starts, device, stream)
 
 
 def paged_prefill_attention(
@@ -233,11 +273,11 @@ def paged_prefill_attention(
         raise ValueError("query shape does not match the cache (head_dim, or heads not a multiple of KV heads)")
     if q.dtype != cache.keys.dtype:
         raise ValueError("query and cache dtypes differ")
-    pq = q_lens if isinstance(q_lens, PrefillQueries) else PrefillQueries(q_lens, cache.keys.device)
+    pq = q_lens if isinstance(q_lens, PrefillQueries) else PrefillQueries(q_lens, cache.keys.device, stream=stream)
     lens = pq.lens
     if pq.total != T:
         raise ValueError("q_lens must add up to the number of query tokens")
-    dt = tables if isinstance(tables, DecodeTables) else DecodeTables(tables, cache.keys.device)
+    dt = tables if isinstance(tables, DecodeTables) else DecodeTables(tables, cache.keys.device, stream=stream)
     if dt.batch != lens.size:
         raise ValueError("one block table per sequence is required")
     if dt.block_size != bs:

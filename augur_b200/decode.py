@@ -30,7 +30,7 @@ import torch
 from torch import Tensor
 
 from . import _lib, _ops
-from .attention import DecodeTables, _workspace, paged_decode_attention, workspace_bytes
+from .attention import DecodeTables, _table_rows, _workspace, paged_decode_attention, upload_int32, workspace_bytes
 from .batched import decode_slot_mapping
 from .paged_kv_cache import PagedKVCache, SequenceBlockTable
 from .rope import rope_tables, write_paged_kv_batch_rope
@@ -49,13 +49,27 @@ class DecodeStep:
         of the pool issued just before the first layer does."""
         device = cache.keys.device
         self.flags = _lib.ATTN_AUTO | (_lib.ATTN_EARLY_READS if early_reads else 0)
-        positions = np.asarray([t.seq_len for t in tables], dtype=np.int64)
+        positions = [t.seq_len for t in tables]
         slots = decode_slot_mapping(tables, cache.allocator)  # seq_len += 1 for every table
-        self.batch = len(tables)
-        self.positions = torch.from_numpy(positions).to(device)
-        self.slots = torch.from_numpy(slots).to(device)
-        self.max_position = int(positions.max(initial=0))
-        self.tables = DecodeTables(tables, device)
+        B = self.batch = len(tables)
+        self.max_position = max(positions, default=0)
+        # one copy for the step: positions and slots (int64, as pairs of int32), then the
+        # block tables and lengths as DecodeTables lays them out
+        lens = [t.seq_len for t in tables]
+        host, width = _table_rows(tables, lens, 4 * B)
+        head = host[: 4 * B].view(np.int64)
+        head[:B] = positions
+        head[B:] = slots
+        dev = upload_int32(host, device)
+        pairs = dev[: 4 * B].view(torch.int64) if B else torch.empty(0, dtype=torch.int64, device=device)
+        self.positions, self.slots = pairs[:B], pairs[B:]
+        self.tables = DecodeTables.__new__(DecodeTables)
+        self.tables._set(dev, 4 * B, tables, lens, width)
+        # the copy is ordered on the current stream; a layer launched on another waits for it
+        self.uploaded: torch.cuda.Event | None = None
+        if device.type == "cuda":
+            self.uploaded = torch.cuda.Event()
+            self.uploaded.record(torch.cuda.current_stream(device))
         self._fast: tuple | None = None  # launch arguments shared by the layers, built on first use
 
     def _prepare(self, cache: PagedKVCache, q: Tensor, key: Tensor, value: Tensor,
@@ -79,6 +93,8 @@ class DecodeStep:
         lib = _lib.load()
         cos, sin = rope_tables(D, rope_theta, dt, self.max_position + 1, dev)
         st = torch.cuda.current_stream(dev)
+        if self.uploaded is not None:
+            st.wait_event(self.uploaded)  # every prepared launch is on st
         dcode = _ops.dtype_code(q)
         cnt, scr = _workspace(lib, dev, st, (B, Hq, Hkv, D, self.tables.max_seq_len, dcode, _lib.ATTN_AUTO))
         q_rot = torch.empty(B, Hq, D, dtype=dt, device=dev)  # reused by every layer, stream-ordered
@@ -102,7 +118,8 @@ class DecodeStep:
         a.status = status.data_ptr()
         sig = _signature(q, key, value)
         # the tensors the argument block points into stay referenced with it
-        return (lib, st, ctypes.addressof(a), sig, a, cache, cos, sin, q_rot, cnt, scr, status, rope_theta)
+        return (lib, st.cuda_stream, ctypes.addressof(a), sig, a, cache, cos, sin, q_rot, cnt, scr, status,
+                rope_theta)
 
     def layer(self, cache: PagedKVCache, layer_idx: int, q: Tensor, key: Tensor, value: Tensor,
               rope_theta: float) -> Tensor | None:
@@ -117,13 +134,15 @@ class DecodeStep:
                 return None
         if _signature(q, key, value) != f[3]:
             return None
-        lib, st = f[0], f[1]
+        lib, stream = f[0], f[1]
         dev = cache.keys.device
-        if not 0 <= layer_idx < f[4].n_layers or _current_raw_stream(dev) != st.cuda_stream:
+        if not 0 <= layer_idx < f[4].n_layers or _current_raw_stream(dev) != stream:
             return None
-        out = torch.empty(q.shape, dtype=q.dtype, device=dev)
+        # q's shape, dtype and device (the signature holds them to the prepared ones), contiguous;
+        # empty_like skips torch.empty's device-argument parsing, a few us of every layer's host time
+        out = torch.empty_like(q, memory_format=torch.contiguous_format)
         code = lib.augur_kv_decode_layer(f[2], layer_idx, q.data_ptr(), key.data_ptr(), value.data_ptr(),
-                                         out.data_ptr(), st.cuda_stream)
+                                         out.data_ptr(), stream)
         _lib.check(code, "augur_kv_decode_layer")
         _ops.launch_count += f[4].launches
         return out
@@ -258,13 +277,20 @@ class DecodeGraphStep:
         return out
 
 
+# torch.cuda.current_device() without its lazy-init check: the step that asks has
+# already launched on the device
+_cuda_device = getattr(torch._C, "_cuda_getDevice", None) or torch.cuda.current_device
+_cuda_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _current_raw_stream(dev: torch.device) -> int:
     """Handle of the current stream on dev (0 when dev is not the current device, which sends
     the caller to the general path)."""
-    if dev.index != torch.cuda.current_device():
+    if dev.index != _cuda_device():
         return 0
-    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
-    return raw(dev.index) if raw is not None else torch.cuda.current_stream(dev).cuda_stream
+    if _cuda_raw_stream is not None:
+        return _cuda_raw_stream(dev.index)
+    return torch.cuda.current_stream(dev).cuda_stream
 
 
 def paged_decode_layer(
@@ -289,6 +315,8 @@ def paged_decode_layer(
         out = step.layer(cache, layer_idx, q, key, value, rope_theta)
         if out is not None:
             return out
+    if step.uploaded is not None:  # the step's slots, positions and tables, on whichever stream
+        (stream if stream is not None else torch.cuda.current_stream(cache.keys.device)).wait_event(step.uploaded)
     B = step.batch
     for name, t in (("q", q), ("key", key), ("value", value)):
         if t.dim() != 4 or t.shape[0] != B or t.shape[2] != 1:

@@ -323,6 +323,35 @@ def test_paged_decode_attention_refuses_cpu_and_bad_shapes():
         DecodeTables([ab.SequenceBlockTable(block_ids=[0], block_size=16, seq_len=17)], torch.device("cpu"))
 
 
+def test_decode_step_packs_its_arrays_into_one_buffer():
+    """A decode step's positions, slots, block tables and lengths are views of one buffer,
+    filled by one copy, with the values the per-array builders give."""
+    from augur_b200.attention import DecodeTables
+    from augur_b200.decode import DecodeStep
+
+    cpu = ab.new_paged_kv_cache(ab.QwenConfig(), num_blocks=8, block_size=4, device=torch.device("cpu"),
+                                dtype=torch.bfloat16)
+    tables = [ab.SequenceBlockTable(block_ids=[], block_size=4, seq_len=0) for _ in range(3)]
+    for t, n in zip(tables, (4, 6, 1)):  # the first grows a block at the step, the others do not
+        t.ensure_position(n - 1, cpu.allocator)
+        t.seq_len = n
+    twins = [ab.SequenceBlockTable(block_ids=list(t.block_ids), block_size=4, seq_len=t.seq_len) for t in tables]
+    step = DecodeStep(cpu, tables)
+    assert step.positions.tolist() == [4, 6, 1] and step.max_position == 6 and step.batch == 3
+    assert step.slots.tolist() == [t.block_ids[p // 4] * 4 + p % 4 for t, p in zip(tables, (4, 6, 1))]
+    assert step.slots.dtype == step.positions.dtype == torch.int64
+    for t in twins:
+        t.seq_len += 1
+        t.block_ids = next(u for u in tables if u.block_ids[: len(t.block_ids)] == t.block_ids).block_ids
+    ref = DecodeTables(twins, torch.device("cpu"))
+    assert torch.equal(step.tables.blocks, ref.blocks) and torch.equal(step.tables.lens, ref.lens)
+    assert step.tables.lens.tolist() == [5, 7, 2] and step.tables.max_seq_len == 7
+    base = step.positions.untyped_storage().data_ptr()
+    assert step.tables.blocks.untyped_storage().data_ptr() == base == step.tables.lens.untyped_storage().data_ptr()
+    empty = DecodeStep(cpu, [])
+    assert empty.batch == 0 and empty.positions.numel() == 0 and empty.tables.blocks.shape == (0, 1)
+
+
 def test_rope_tables_follow_the_reference_formula(oracle):
     """The product's cos/sin tables equal the oracle's (pinned to augur/rope.py) bit for bit."""
     from augur_b200.rope import rope_tables
