@@ -350,6 +350,12 @@ def test_decode_step_packs_its_arrays_into_one_buffer():
     assert step.tables.blocks.untyped_storage().data_ptr() == base == step.tables.lens.untyped_storage().data_ptr()
     empty = DecodeStep(cpu, [])
     assert empty.batch == 0 and empty.positions.numel() == 0 and empty.tables.blocks.shape == (0, 1)
+    # a table's ids are converted again whenever its list changes, in place too (copy-on-write)
+    tables[1].block_ids[0] = 7
+    assert DecodeTables(tables, torch.device("cpu")).blocks[1, 0] == 7
+    tables[1].block_ids = [5, 6]
+    assert DecodeTables(tables, torch.device("cpu")).blocks[1].tolist()[:3] == [5, 6, -1]
+    assert tables[1] == ab.SequenceBlockTable(block_ids=[5, 6], block_size=4, seq_len=7)
 
 
 def test_rope_tables_follow_the_reference_formula(oracle):
