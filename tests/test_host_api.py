@@ -354,7 +354,7 @@ def test_decode_step_packs_its_arrays_into_one_buffer():
     tables[1].block_ids[0] = 7
     assert DecodeTables(tables, torch.device("cpu")).blocks[1, 0] == 7
     tables[1].block_ids = [5, 6]
-    assert DecodeTables(tables, torch.device("cpu")).blocks[1].tolist()[:3] == [5, 6, -1]
+    assert DecodeTables(tables, torch.device("cpu")).blocks[1].tolist()[:2] == [5, 6]
     assert tables[1] == ab.SequenceBlockTable(block_ids=[5, 6], block_size=4, seq_len=7)
 
 
