@@ -22,11 +22,13 @@ pytestmark = pytest.mark.gpu
 THETA = 1000000.0
 
 
-@pytest.mark.parametrize("path", ["prepared", "general", "mixed"])
+@pytest.mark.parametrize("path", ["prepared", "general", "mixed", "side"])
 def test_decode_layers_match_the_reference_branch(cuda, oracle, path):
     """path: the step's prepared launches, the general wrappers (an explicit stream), or
     both in one step (a later layer's q is a strided view, which the prepared arguments
-    do not describe, so that layer takes the general path)."""
+    do not describe, so that layer takes the general path); side: the prepared launches
+    with another stream current than the one the step uploaded its arrays on (they wait
+    for the upload, and through it for the prompt writes before it)."""
     L, H, Hq, D, bs, NB = 2, 2, 14, 64, 16, 64
     prior = [0, 1, 15, 16, 300]
     g = torch.Generator().manual_seed(12)
@@ -61,7 +63,13 @@ def test_decode_layers_match_the_reference_branch(cuda, oracle, path):
             wide[:, :, :1] = qd
             qd = wide[:, :, :1]
             assert qd.stride() != q.stride()
-        out = paged_decode_layer(step, pool, layer, qd, k.to(cuda), v.to(cuda), THETA, stream=stream)
+        if path == "side":
+            side = torch.cuda.Stream(cuda)
+            with torch.cuda.stream(side):
+                out = paged_decode_layer(step, pool, layer, qd, k.to(cuda), v.to(cuda), THETA)
+            torch.cuda.current_stream(cuda).wait_stream(side)
+        else:
+            out = paged_decode_layer(step, pool, layer, qd, k.to(cuda), v.to(cuda), THETA, stream=stream)
         assert out.shape == (len(prior), Hq, 1, D)
         for b, n in enumerate(prior):
             pos = torch.tensor([[n]])
